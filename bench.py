@@ -1,0 +1,371 @@
+#!/usr/bin/env python
+"""MLA decode benchmark on B200 (one JSON line on rank 0).
+
+Workload: DeepSeek-V3-shaped dense paged MLA decode --
+64 sequences per GPU, seq_q 1, 128 query heads, one 576-dim latent head
+(values = first 512 dims), page 64, bf16 N(0,1), context lengths
+U[1024, 8192], block table a random permutation of a pooled page cache,
+softmax scale 576^-0.5.  A step is one decode of the batch (decode kernel +
+split combine; the tile metadata is computed once per batch, as it is shared
+by every layer of a model step).  With --gpus N (torchrun) the global batch
+of 64*N sequences is sharded by sequence across the ranks (greedy by KV bytes,
+no collective on the data path): weak scaling.
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+numpy restatement of flag_attn.testing in oracle/) on the host cores instead.
+"""
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B_PER_GPU, S_Q, H_Q, D_QK, D_V, PAGE = 64, 1, 128, 576, 512, 64
+CTX_LO, CTX_HI = 1024, 8192
+SEED = 2026
+WORKLOAD = "dense_paged_mla_decode_b64_h128_ctx1k-8k_bf16"
+METRIC = "mla_decode_tokens_per_s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--cpu-seconds", type=float, default=10.0,
+                   help="budget of the cpu_baseline sample")
+    return p.parse_args()
+
+
+def global_lens(world):
+    rs = np.random.RandomState(SEED)
+    return rs.randint(CTX_LO, CTX_HI + 1, size=B_PER_GPU * world).astype(np.int32)
+
+
+def algorithmic_bytes(lens):
+    n = len(lens)
+    return int(np.sum(lens.astype(np.int64)) * D_QK * 2 + n * S_Q * H_Q * (D_QK * 2 + D_V * 2 + 4))
+
+
+def algorithmic_flops(lens):
+    return int(np.sum(lens.astype(np.int64)) * 2 * S_Q * H_Q * (D_QK + D_V))
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:  # noqa: BLE001
+        return 6650.0, 1590.0, "fallback"
+
+
+def profiled_traffic():
+    """dram read+write bytes per decode launch from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "mla_decode_config2.md")
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(path).read())
+        return int(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id):
+        self.proc = None
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", bus_id], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.tmp.flush()
+        rows = [r.split(",") for r in open(self.tmp.name).read().strip().splitlines() if r]
+        os.unlink(self.tmp.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            if len(r) >= 9:
+                for name, val in zip(names, r[5:9]):
+                    if val.strip() == "Active":
+                        reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import flagattention_b200 as fa
+    from flagattention_b200 import _torch as fat
+    from flagattention_b200.mla import MlaCall
+    from flagattention_b200.shard import partition_sequences
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    lens_all = global_lens(world)
+    mine = partition_sequences(lens_all, world)[rank]
+    lens = lens_all[mine]
+    B = len(lens)
+    g = torch.Generator(device=dev).manual_seed(SEED + 17 * rank)
+    npages = int(np.sum((lens + PAGE - 1) // PAGE))
+    kcache = torch.randn((npages, PAGE, 1, D_QK), generator=g, device=dev, dtype=torch.bfloat16)
+    q = torch.randn((B, S_Q, H_Q, D_QK), generator=g, device=dev, dtype=torch.bfloat16)
+    perm = torch.randperm(npages, generator=g, device=dev).to(torch.int32)
+    width = int(((lens.max() + PAGE - 1) // PAGE))
+    bt = torch.zeros((B, width), dtype=torch.int32, device=dev)
+    off = 0
+    for i, n in enumerate(lens):
+        k = int((n + PAGE - 1) // PAGE)
+        bt[i, :k] = perm[off:off + k]
+        off += k
+    seq = torch.from_numpy(lens).to(dev)
+    meta, splits = fa.get_mla_metadata(seq, S_Q * H_Q, 1)
+    out = torch.empty((B, S_Q, H_Q, D_V), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((B, H_Q, S_Q), dtype=torch.float32, device=dev)
+    call = MlaCall(q, kcache, kcache.stride(0), kcache.stride(1), npages, PAGE, bt, seq, 0, meta,
+                   splits, out, lse, D_QK ** -0.5)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)   # > 126 MB L2
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev):
+        flush.fill_(1)
+        ev[0].record(stream)
+        call.partial()
+        ev[1].record(stream)
+        call.combine()
+        ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        step([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+    torch.cuda.synchronize()
+    assert fat.read_status(dev) == 0, "device wait timeout during warm-up"
+
+    props = torch.cuda.get_device_properties(dev)
+    bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+    sampler = ClockSampler(bus) if rank == 0 else None
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        step(evs[i])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    dec = [e[0].elapsed_time(e[1]) for e in evs]
+    comb = [e[1].elapsed_time(e[2]) for e in evs]
+    step_ms = sum(dec) / len(dec) + sum(comb) / len(comb)
+    dec_ms = sum(dec) / len(dec)
+    assert fat.read_status(dev) == 0, "device wait timeout in the timed region"
+
+    # end-to-end through the public API with host buffers
+    q_h = q.cpu().pin_memory()
+    seq_h = seq.cpu().pin_memory()
+    bt_h = bt.cpu().pin_memory()
+    q_d, seq_d, bt_d = torch.empty_like(q), torch.empty_like(seq), torch.empty_like(bt)
+    out_h = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    lse_h = torch.empty(lse.shape, dtype=lse.dtype, pin_memory=True)
+
+    def e2e_step(ev):
+        flush.fill_(1)
+        ev[0].record(stream)
+        q_d.copy_(q_h, non_blocking=True)
+        seq_d.copy_(seq_h, non_blocking=True)
+        bt_d.copy_(bt_h, non_blocking=True)
+        m, s = fa.get_mla_metadata(seq_d, S_Q * H_Q, 1)
+        o, l = fa.flash_mla_with_kvcache(q_d, kcache, bt_d, seq_d, D_V, m, s)
+        out_h.copy_(o, non_blocking=True)
+        lse_h.copy_(l, non_blocking=True)
+        ev[1].record(stream)
+
+    for _ in range(args.warmup):
+        e2e_step([torch.cuda.Event(enable_timing=True) for _ in range(2)])
+    e2e_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        e2e_step(e2e_evs[i])
+    torch.cuda.synchronize()
+    e2e_ms = sum(e[0].elapsed_time(e[1]) for e in e2e_evs) / args.steps
+    h2d = q.numel() * 2 + seq.numel() * 4 + bt.numel() * 4
+    d2h = out.numel() * 2 + lse.numel() * 4
+
+    t = torch.tensor([step_ms, dec_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, dec_ms, e2e_ms = t.tolist()
+    tokens = len(lens_all) * S_Q
+    bytes_local = algorithmic_bytes(lens)
+    flops_local = algorithmic_flops(lens)
+    if rank == 0:
+        peak_gbs, peak_tf, peak_kind = measured_peaks()
+        achieved = bytes_local / (dec_ms * 1e-3) / 1e9
+        traffic = profiled_traffic()
+        rec = {
+            "metric": METRIC, "value": tokens / (step_ms * 1e-3), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": B_PER_GPU,
+                       "global_batch": len(lens_all), "seq_q": S_Q, "heads_q": H_Q,
+                       "d_qk": D_QK, "d_v": D_V, "page_size": PAGE,
+                       "ctx": [CTX_LO, CTX_HI], "parallelism": f"seq-shard{world}",
+                       "l2": "flushed before every step (256 MB write, outside the events)",
+                       "metadata": "computed once per batch (outside the step)"},
+            "hbm_gbs_step": bytes_local / (step_ms * 1e-3) / 1e9,
+            "hbm_frac_step": bytes_local / (step_ms * 1e-3) / 1e9 / peak_gbs,
+            "tensor_tflops_decode": flops_local / (dec_ms * 1e-3) / 1e12,
+            "ms_decode_kernel": dec_ms, "ms_combine_kernel": step_ms - dec_ms,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs,
+                         "unit": "GB/s", "frac": achieved / peak_gbs,
+                         "traffic": traffic, "peak_source": peak_kind,
+                         "kernel": "mla_decode_tc_kernel<bf16,64,dense>",
+                         "algorithmic_bytes_per_launch": bytes_local},
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tok/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms,
+                    "path": "get_mla_metadata + flash_mla_with_kvcache, pinned host buffers"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks,
+        }
+        if world == 1:
+            rec["cpu_baseline"] = cpu_baseline(q, kcache, bt, lens, args.cpu_seconds)
+        print(json.dumps(rec), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------ CPU timing
+def _host_sequence(q, kcache, bt, lens, i):
+    """Sequence i as float32 numpy (its pages gathered, block table remapped)."""
+    import torch
+    n = int(lens[i])
+    k = (n + PAGE - 1) // PAGE
+    pages = bt[i, :k].long()
+    kc = kcache[pages].float().cpu().numpy()
+    return q[i:i + 1].float().cpu().numpy(), kc, np.arange(k, dtype=np.int32)[None], lens[i:i + 1]
+
+
+def time_oracle(samples, budget_s):
+    """Run the oracle over the samples round-robin for ~budget_s; tok/s."""
+    import oracle
+    done, t0 = 0, time.perf_counter()
+    while True:
+        qs, kc, bt, ln = samples[done % len(samples)]
+        oracle.mla_decode_dense(qs, kc, bt, ln, D_V, D_QK ** -0.5)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s and done >= 2:
+            return done * S_Q / el, done, el
+
+
+def _threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+        return int(n)
+    except Exception:  # noqa: BLE001
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(q, kcache, bt, lens, budget):
+    samples = [_host_sequence(q, kcache, bt, lens, i) for i in range(min(8, len(lens)))]
+    tps, done, el = time_oracle(samples, budget)
+    return {"value": tps, "unit": "tok/s", "cores": _threads(), "kind": "port",
+            "sample": f"{done} sequence decodes of the config-2 workload (first 8 sequences, "
+                      f"ctx {int(lens[:8].min())}-{int(lens[:8].max())}, 128 heads) through the "
+                      f"numpy oracle in {el:.1f}s, float32, all BLAS threads"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    lens = global_lens(1)
+    rs = np.random.RandomState(SEED)
+    n_seq = 8
+    samples = []
+    for i in range(n_seq):
+        n = int(lens[i])
+        k = (n + PAGE - 1) // PAGE
+        kc = rs.standard_normal((k, PAGE, 1, D_QK)).astype(np.float32)
+        qs = rs.standard_normal((1, S_Q, H_Q, D_QK)).astype(np.float32)
+        samples.append((qs, kc, np.arange(k, dtype=np.int32)[None], lens[i:i + 1]))
+    per_step = max(0.5, min(2.0, 150.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        time_oracle(samples, per_step)
+    vals = []
+    t0 = time.perf_counter()
+    total_done = 0
+    for _ in range(args.steps):
+        v, d, _ = time_oracle(samples, per_step)
+        vals.append(v)
+        total_done += d
+    el = time.perf_counter() - t0
+    value = total_done * S_Q / el
+    cores = _threads()
+    rec = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic (seeded N(0,1))", "impl": "reference",
+           "config": {"workload": WORKLOAD, "batch_per_gpu": B_PER_GPU, "seq_q": S_Q,
+                      "heads_q": H_Q, "d_qk": D_QK, "d_v": D_V, "page_size": PAGE,
+                      "ctx": [CTX_LO, CTX_HI], "parallelism": "host cpu"},
+           "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                            "sample": f"each step decodes config-2 sequences (the first {n_seq},"
+                                      f" round-robin) for ~{per_step:.1f}s through the numpy "
+                                      "restatement of flag_attn.testing"},
+           "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(rec), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,380 @@
+// capi.cu -- the extern "C" boundary declared in include/flagattn_b200.h.
+//
+// Host-side argument validation (mirroring the reference's asserts, e.g.
+// paged.py:45-46,124 and split_kv.py:281-289, as negative status codes),
+// the reference's split heuristics, TMA tensor-map encoding and the launches.
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "flagattn_b200.h"
+
+namespace fa {
+void launch_mla_metadata(const int32_t *, int, int, int, int32_t *, int32_t *, cudaStream_t);
+void launch_lse_combine(const float *, const float *, int, int64_t, int, int, int, void *, int,
+                        int64_t, int64_t, int64_t, float *, cudaStream_t);
+void launch_mla_combine(const float *, const float *, const int32_t *, int, int, int, int, void *,
+                        int, int64_t, int64_t, int64_t, float *, cudaStream_t);
+cudaError_t launch_generic_decode(const fa_decode_args *, cudaStream_t);
+size_t generic_smem_bytes(int, int);
+cudaError_t launch_mla_tc(const CUtensorMap &, const CUtensorMap &, const fa_mla_args *, int, int,
+                          int64_t, cudaStream_t);
+}  // namespace fa
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int status, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int status, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  return fail(FA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+int next_pow2(int x) {
+  int p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 3-D bf16/f16 map {d, rows, groups} with a {64, box_rows, 1} box, 128-byte
+// swizzle (the UMMA K-major / MN-major SW128 canonical layout).
+int encode_map(CUtensorMap *map, const void *base, int dtype, uint64_t d, uint64_t rows,
+               uint64_t groups, uint64_t row_stride_elems, uint64_t group_stride_elems,
+               uint32_t box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {d, rows, groups};
+  cuuint64_t strides[2] = {row_stride_elems * 2, group_stride_elems * 2};
+  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(map, dtype == FA_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   3, const_cast<void *>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FA_ERR_INVALID_ARGUMENT,
+                "tensor map rejected (code %d): dims {%llu,%llu,%llu} strides {%llu,%llu} B",
+                static_cast<int>(r), (unsigned long long)d, (unsigned long long)rows,
+                (unsigned long long)groups, (unsigned long long)strides[0],
+                (unsigned long long)strides[1]);
+  return FA_OK;
+}
+
+int mla_block_n() {
+  static int bn = [] {
+    const char *e = getenv("FA_MLA_BLOCK_N");
+    return (e && atoi(e) == 32) ? 32 : 64;
+  }();
+  return bn;
+}
+
+int validate_decode(const fa_decode_args *a) {
+  if (!a) return fail(FA_ERR_INVALID_ARGUMENT, "null args");
+  if (!a->q || !a->k || !a->v || !a->o) return fail(FA_ERR_INVALID_ARGUMENT, "null tensor");
+  if (a->batch < 0 || a->num_q_heads <= 0 || a->num_kv_heads <= 0 || a->m_q <= 0)
+    return fail(FA_ERR_INVALID_ARGUMENT, "bad batch/heads/m_q");
+  if (a->num_q_heads % a->num_kv_heads != 0)
+    return fail(FA_ERR_INVALID_ARGUMENT, "number of heads in q must be a multiple of that in k & v");
+  if (a->d_qk <= 0 || a->d_qk > 576 || a->d_v <= 0 || a->d_v > 512 || a->d_v > a->d_qk)
+    return fail(FA_ERR_UNSUPPORTED, "head size d_qk=%d d_v=%d outside [1,576]/[1,512]", a->d_qk,
+                a->d_v);
+  if (a->d_v % 4 != 0) return fail(FA_ERR_UNSUPPORTED, "d_v must be a multiple of 4");
+  if (a->dtype != FA_DTYPE_BF16 && a->dtype != FA_DTYPE_F16 && a->dtype != FA_DTYPE_F32)
+    return fail(FA_ERR_INVALID_ARGUMENT, "dtype %d", a->dtype);
+  if (a->block_table) {
+    if (a->page_size <= 0) return fail(FA_ERR_INVALID_ARGUMENT, "page_size %d", a->page_size);
+    if (!a->seq_lens) return fail(FA_ERR_INVALID_ARGUMENT, "paged mode needs seq_lens");
+  } else if (!a->seq_lens && a->n_ctx < 0) {
+    return fail(FA_ERR_INVALID_ARGUMENT, "n_ctx %d", a->n_ctx);
+  }
+  if (a->num_splits < 1) return fail(FA_ERR_INVALID_ARGUMENT, "num_splits %d", a->num_splits);
+  if (a->num_splits > 1 && (!a->part_o || !a->part_lse || !aligned16(a->part_o)))
+    return fail(FA_ERR_INVALID_ARGUMENT, "num_splits > 1 needs 16-byte aligned f32 workspace");
+  if (a->num_splits > 1 && a->partition_size <= 0)
+    return fail(FA_ERR_INVALID_ARGUMENT, "num_splits > 1 needs partition_size > 0");
+  if (fa::generic_smem_bytes(a->d_qk, a->d_v) > 227 * 1024)
+    return fail(FA_ERR_UNSUPPORTED, "head size too large for the generic kernel");
+  return FA_OK;
+}
+
+int run_decode(const fa_decode_args *a, void *stream) {
+  int st = validate_decode(a);
+  if (st != FA_OK) return st;
+  if (a->batch == 0) return FA_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = fa::launch_generic_decode(a, s);
+  if (e != cudaSuccess) return cuda_fail(e, "generic decode launch");
+  if (a->num_splits > 1) {
+    const int64_t rows = static_cast<int64_t>(a->batch) * a->num_q_heads * a->m_q;
+    fa::launch_lse_combine(a->part_o, a->part_lse, a->num_splits, rows, a->num_q_heads, a->m_q,
+                           a->d_v, a->o, a->dtype, a->o_stride_b, a->o_stride_h, a->o_stride_m,
+                           a->lse, s);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "combine launch");
+  }
+  return FA_OK;
+}
+
+int mla_m_blocks(int s_q, int h_q, bool sparse) {
+  return sparse ? s_q : static_cast<int>(cdiv64(static_cast<int64_t>(s_q) * h_q, 128));
+}
+
+int validate_mla(const fa_mla_args *a) {
+  if (!a) return fail(FA_ERR_INVALID_ARGUMENT, "null args");
+  const bool sparse = a->indices != nullptr;
+  if (!a->q || !a->kcache || !a->out || !a->lse || !a->tile_meta || !a->num_splits)
+    return fail(FA_ERR_INVALID_ARGUMENT, "null tensor");
+  if (a->d_qk != 576 || a->d_v != 512)
+    return fail(FA_ERR_UNSUPPORTED, "MLA path needs d_qk=576, d_v=512 (got %d/%d)", a->d_qk,
+                a->d_v);
+  if (a->dtype != FA_DTYPE_BF16 && a->dtype != FA_DTYPE_F16)
+    return fail(FA_ERR_UNSUPPORTED, "MLA path computes in bf16 or f16");
+  if (a->out_dtype != a->dtype && a->out_dtype != FA_DTYPE_F32)
+    return fail(FA_ERR_INVALID_ARGUMENT, "out_dtype must equal dtype or be f32");
+  if (a->batch < 0 || a->s_q <= 0 || a->h_q <= 0) return fail(FA_ERR_INVALID_ARGUMENT, "shape");
+  if (sparse && a->h_q > 128) return fail(FA_ERR_UNSUPPORTED, "sparse path needs h_q <= 128");
+  if (sparse && (a->topk <= 0 || a->causal))
+    return fail(FA_ERR_INVALID_ARGUMENT, "sparse needs topk > 0 and causal == 0");
+  if (a->num_sm_parts <= 0) return fail(FA_ERR_INVALID_ARGUMENT, "num_sm_parts");
+  if (!aligned16(a->q) || !aligned16(a->kcache) || !aligned16(a->out))
+    return fail(FA_ERR_INVALID_ARGUMENT, "q / kcache / out must be 16-byte aligned");
+  if (a->q_stride_h % 8 || a->q_stride_b % 8 || a->q_stride_s % 8 || a->kv_stride_tok % 8 ||
+      a->kv_stride_page % 8 || a->o_stride_b % 8 || a->o_stride_s % 8 || a->o_stride_h % 8)
+    return fail(FA_ERR_INVALID_ARGUMENT, "strides must be multiples of 8 elements (16 bytes)");
+  if (!sparse && a->s_q > 1 && a->q_stride_s != static_cast<int64_t>(a->h_q) * a->q_stride_h)
+    return fail(FA_ERR_UNSUPPORTED, "q rows (s_q, h_q) must be contiguous: q_stride_s == h_q*q_stride_h");
+  if (a->page_size <= 0 || a->page_size % 64 != 0)
+    return fail(FA_ERR_UNSUPPORTED, "page_size must be a multiple of 64 (got %d)", a->page_size);
+  if (!sparse && a->block_table == nullptr && !a->seq_lens && a->n_ctx < 0)
+    return fail(FA_ERR_INVALID_ARGUMENT, "n_ctx");
+  if (!sparse && a->block_table != nullptr && !a->seq_lens)
+    return fail(FA_ERR_INVALID_ARGUMENT, "paged dense decode needs seq_lens");
+  if (!a->part_o || !a->part_lse || !aligned16(a->part_o))
+    return fail(FA_ERR_INVALID_ARGUMENT, "workspace must be given and 16-byte aligned");
+  return FA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_version(void) { return (0 << 16) | (1 << 8) | 0; }
+
+const char *fa_status_string(int status) {
+  switch (status) {
+    case FA_OK: return "ok";
+    case FA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case FA_ERR_UNSUPPORTED: return "unsupported";
+    case FA_ERR_CUDA: return "cuda error";
+    case FA_ERR_NO_DEVICE: return "no device";
+    default: return "unknown status";
+  }
+}
+
+const char *fa_last_error(void) { return g_last_error; }
+
+int fa_device_sm_count(int device, int *sm_count) {
+  if (!sm_count) return fail(FA_ERR_INVALID_ARGUMENT, "null out");
+  cudaError_t e = cudaDeviceGetAttribute(sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return fail(FA_ERR_NO_DEVICE, "%s", cudaGetErrorString(e));
+  return FA_OK;
+}
+
+int fa_paged_num_splits(int num_seqs, int num_kv_heads, int max_context_len, int kv_block_size,
+                        int num_sms, int requested_splits, int *num_splits, int *partition_size) {
+  if (!num_splits || !partition_size) return fail(FA_ERR_INVALID_ARGUMENT, "null out");
+  int ns = requested_splits, ps = 0;
+  if (ns == 0) {
+    if (static_cast<int64_t>(num_seqs) * num_kv_heads > 2LL * num_sms) {
+      ns = 1;
+      if (max_context_len >= 4096) {
+        ps = kv_block_size > 256 ? kv_block_size : 256;
+        ns = static_cast<int>(cdiv64(max_context_len, ps));
+      }
+    } else {
+      ps = kv_block_size > 256 ? kv_block_size : 256;
+      ns = static_cast<int>(cdiv64(max_context_len, ps));
+      if (max_context_len <= 1024 || kv_block_size >= 256) ns = 1;
+    }
+  } else if (ns > 1) {
+    ps = next_pow2(static_cast<int>(cdiv64(max_context_len, ns)));
+  }
+  if (ns < 1) ns = 1;
+  if (ns == 1) ps = 0;
+  *num_splits = ns;
+  *partition_size = ps;
+  return FA_OK;
+}
+
+int fa_split_kv_num_splits(int batch, int heads, int m, int n, int block_m, int block_n,
+                           int num_sms, int max_splits, int *num_splits) {
+  if (!num_splits || block_m <= 0 || block_n <= 0 || num_sms <= 0)
+    return fail(FA_ERR_INVALID_ARGUMENT, "bad heuristic arguments");
+  const int64_t nb = static_cast<int64_t>(batch) * heads * cdiv64(m, block_m);
+  *num_splits = 1;
+  if (static_cast<double>(nb) >= 0.8 * num_sms) return FA_OK;
+  const int64_t n_blocks = cdiv64(n, block_n);
+  int64_t lim = num_sms;
+  if (n_blocks < lim) lim = n_blocks;
+  if (max_splits < lim) lim = max_splits;
+  double best = 0.0;
+  double eff[1024];
+  bool avail[1024];
+  if (lim > 1023) lim = 1023;
+  for (int64_t s = 1; s <= lim; ++s) {
+    const int64_t per = cdiv64(n_blocks, s);
+    avail[s] = (s == 1) || (per * s - n_blocks < per);
+    if (avail[s]) {
+      const double waves = static_cast<double>(nb * s) / static_cast<double>(num_sms);
+      eff[s] = waves / std::ceil(waves);
+      if (eff[s] > best) best = eff[s];
+    }
+  }
+  for (int64_t s = 1; s <= lim; ++s) {
+    if (avail[s] && eff[s] >= 0.85 * best) {
+      *num_splits = static_cast<int>(s);
+      return FA_OK;
+    }
+  }
+  return FA_OK;
+}
+
+int fa_decode_workspace_size(const fa_decode_args *a, size_t *part_o_bytes,
+                             size_t *part_lse_bytes) {
+  if (!a || !part_o_bytes || !part_lse_bytes) return fail(FA_ERR_INVALID_ARGUMENT, "null");
+  const size_t rows = static_cast<size_t>(a->batch) * a->num_q_heads * a->m_q;
+  const size_t s = a->num_splits > 1 ? static_cast<size_t>(a->num_splits) : 0;
+  *part_o_bytes = s * rows * a->d_v * sizeof(float);
+  *part_lse_bytes = s * rows * sizeof(float);
+  return FA_OK;
+}
+
+int fa_paged_attention(const fa_decode_args *a, void *stream) {
+  if (a && !a->block_table) return fail(FA_ERR_INVALID_ARGUMENT, "paged attention needs a block table");
+  return run_decode(a, stream);
+}
+
+int fa_split_kv_attention(const fa_decode_args *a, void *stream) {
+  if (a && a->block_table) return fail(FA_ERR_INVALID_ARGUMENT, "split-KV attention takes contiguous keys");
+  return run_decode(a, stream);
+}
+
+int fa_lse_combine(const float *part_o, const float *part_lse, int num_parts, int64_t rows,
+                   int d_v, void *o, int dtype, float *lse, void *stream) {
+  if (!part_o || !part_lse || !o || num_parts < 1 || rows < 0 || d_v <= 0 || d_v % 4)
+    return fail(FA_ERR_INVALID_ARGUMENT, "bad combine arguments");
+  if (!aligned16(part_o)) return fail(FA_ERR_INVALID_ARGUMENT, "part_o must be 16-byte aligned");
+  fa::launch_lse_combine(part_o, part_lse, num_parts, rows, 1, 1, d_v, o, dtype, d_v, 0, 0, lse,
+                         static_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? FA_OK : cuda_fail(e, "combine launch");
+}
+
+int fa_mla_num_sm_parts(int device, int s_q, int h_q, int sparse, int *num_sm_parts) {
+  if (!num_sm_parts || s_q <= 0 || h_q <= 0) return fail(FA_ERR_INVALID_ARGUMENT, "bad arguments");
+  int sms = 0;
+  int st = fa_device_sm_count(device, &sms);
+  if (st != FA_OK) return st;
+  const int mb = mla_m_blocks(s_q, h_q, sparse != 0);
+  int parts = sms / 2 / mb;
+  *num_sm_parts = parts > 0 ? parts : 1;
+  return FA_OK;
+}
+
+int fa_mla_workspace_size(int batch, int s_q, int h_q, int d_v, int num_sm_parts,
+                          size_t *part_o_bytes, size_t *part_lse_bytes) {
+  if (!part_o_bytes || !part_lse_bytes || batch < 0 || num_sm_parts < 1)
+    return fail(FA_ERR_INVALID_ARGUMENT, "bad arguments");
+  const size_t slots = static_cast<size_t>(batch) + num_sm_parts;
+  const size_t rows = static_cast<size_t>(s_q) * h_q;
+  *part_o_bytes = slots * rows * d_v * sizeof(float);
+  *part_lse_bytes = slots * rows * sizeof(float);
+  return FA_OK;
+}
+
+int fa_mla_get_metadata(const int32_t *seq_lens, int batch, int topk, int num_sm_parts,
+                        int32_t *tile_meta, int32_t *num_splits, void *stream) {
+  if (batch < 0 || num_sm_parts < 1 || !tile_meta || !num_splits || (topk <= 0 && !seq_lens && batch))
+    return fail(FA_ERR_INVALID_ARGUMENT, "bad metadata arguments");
+  fa::launch_mla_metadata(seq_lens, batch, topk, num_sm_parts, tile_meta, num_splits,
+                          static_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? FA_OK : cuda_fail(e, "metadata launch");
+}
+
+int fa_mla_combine(const fa_mla_args *a, void *stream) {
+  int st = validate_mla(a);
+  if (st != FA_OK) return st;
+  if (a->batch == 0) return FA_OK;
+  fa::launch_mla_combine(a->part_o, a->part_lse, a->num_splits, a->batch, a->s_q, a->h_q, a->d_v,
+                         a->out, a->out_dtype, a->o_stride_b, a->o_stride_s, a->o_stride_h, a->lse,
+                         static_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? FA_OK : cuda_fail(e, "MLA combine launch");
+}
+
+int fa_mla_decode_partial(const fa_mla_args *a, void *stream) {
+  int st = validate_mla(a);
+  if (st != FA_OK) return st;
+  if (a->batch == 0) return FA_OK;
+  const bool sparse = a->indices != nullptr;
+  const int bn = mla_block_n();
+  const int m_blocks = mla_m_blocks(a->s_q, a->h_q, sparse);
+  CUtensorMap qm, km;
+  st = encode_map(&qm, a->q, a->dtype, 576, static_cast<uint64_t>(a->s_q) * a->h_q, a->batch,
+                  a->q_stride_h, a->q_stride_b, 128);
+  if (st != FA_OK) return st;
+  const bool paged = a->block_table != nullptr;
+  if (sparse || paged)
+    st = encode_map(&km, a->kcache, a->dtype, 576, a->page_size, a->num_pages, a->kv_stride_tok,
+                    a->kv_stride_page, bn);
+  else
+    st = encode_map(&km, a->kcache, a->dtype, 576, a->n_ctx > 0 ? a->n_ctx : 1, a->batch,
+                    a->kv_stride_tok, a->kv_stride_page, bn);
+  if (st != FA_OK) return st;
+  const int64_t total_rows = static_cast<int64_t>(a->num_pages) * a->page_size;
+  cudaError_t e = fa::launch_mla_tc(qm, km, a, bn, m_blocks, total_rows,
+                                    static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FA_OK : cuda_fail(e, "MLA decode launch");
+}
+
+int fa_mla_decode(const fa_mla_args *a, void *stream) {
+  int st = fa_mla_decode_partial(a, stream);
+  if (st != FA_OK || a->batch == 0) return st;
+  return fa_mla_combine(a, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,108 @@
+"""Reference-compatible ``paged_attention`` (FlagAttention ``paged.py:20-177``).
+
+Same signature, argument meaning and result as ``flag_attn.paged_attention``:
+query [num_seqs, num_q_heads, head_size], caches [num_blocks, num_kv_heads,
+block_size, head_size] with identical strides, int32 context_lens and
+block_tables, returns ``out`` shaped like the query (with the value width).
+
+Two paths, chosen by shape:
+
+* the MLA latent shape (one kv head, 576-dim keys, values = the first 512
+  dims of the same cache rows, block size a multiple of 64, bf16/f16) runs on
+  the tcgen05 tensor-core kernel with the balanced tile scheduler;
+* every other shape (the reference's own test grid: head sizes 16..512,
+  grouped heads, f16/bf16/f32) runs the generic kernel with the reference's
+  split rule (``paged.py:54-67``, bit-exact through ``fa_paged_num_splits``).
+"""
+
+import ctypes
+
+import torch
+
+from flagattention_b200 import _lib
+from flagattention_b200._torch import dtype_code, ptr, require_cuda, sm_count, stream_of
+
+
+def paged_num_splits(num_seqs, num_kv_heads, max_context_len, kv_block_size, num_sms,
+                     num_splits=0):
+    """(num_splits, partition_size) per the reference rule (paged.py:54-67)."""
+    ns, ps = ctypes.c_int32(0), ctypes.c_int32(0)
+    _lib.check(_lib.lib().fa_paged_num_splits(num_seqs, num_kv_heads, max_context_len,
+                                              kv_block_size, num_sms, num_splits,
+                                              ctypes.byref(ns), ctypes.byref(ps)),
+               "fa_paged_num_splits")
+    return ns.value, ps.value
+
+
+def _is_mla(query, key_cache, value_cache):
+    return (key_cache.shape[1] == 1 and key_cache.shape[3] == 576 and value_cache.shape[3] == 512
+            and value_cache.data_ptr() == key_cache.data_ptr()
+            and value_cache.stride() == key_cache.stride()
+            and key_cache.shape[2] % 64 == 0 and query.dtype in (torch.bfloat16, torch.float16))
+
+
+def _mla_paged(query, key_cache, context_lens, block_tables, attn_scale):
+    from flagattention_b200.mla import get_mla_metadata, mla_decode
+    S, H, _ = query.shape
+    meta, splits = get_mla_metadata(context_lens, H, 1)
+    q = query.unsqueeze(1)                                # [S, 1, H, 576]
+    out = torch.empty((S, H, 512), dtype=query.dtype, device=query.device)
+    lse = torch.empty((S, H, 1), dtype=torch.float32, device=query.device)
+    mla_decode(q, key_cache, key_cache.stride(0), key_cache.stride(2), key_cache.shape[0],
+               key_cache.shape[2], block_tables, context_lens, 0, meta, splits,
+               out.unsqueeze(1), lse, attn_scale)
+    return out
+
+
+def paged_attention(query, key_cache, value_cache, context_lens, block_tables, attn_scale,
+                    max_context_len, num_splits=0):
+    """Drop-in for ``flag_attn.paged_attention`` (paged.py:20)."""
+    require_cuda(query, key_cache, value_cache, context_lens, block_tables)
+    num_seqs, num_q_heads, head_size = query.shape
+    num_kv_heads, block_size = key_cache.shape[1], key_cache.shape[2]
+    if key_cache.shape[3] != head_size:
+        raise _lib.InvalidArgument("query and key_cache head sizes differ")
+    if value_cache.shape[:3] != key_cache.shape[:3] or value_cache.stride() != key_cache.stride():
+        raise _lib.InvalidArgument("value_cache must have the same shape/strides as key_cache")
+    if num_q_heads % num_kv_heads != 0:
+        raise _lib.InvalidArgument("num_q_heads must be a multiple of num_kv_heads")
+    if context_lens.dtype != torch.int32 or block_tables.dtype != torch.int32:
+        raise _lib.InvalidArgument("context_lens and block_tables must be int32")
+    if _is_mla(query, key_cache, value_cache):
+        return _mla_paged(query, key_cache, context_lens, block_tables, attn_scale)
+    if query.stride(-1) != 1 or key_cache.stride(-1) != 1:
+        raise _lib.InvalidArgument("last dims must be contiguous")
+    d_v = value_cache.shape[3]
+    ns, ps = paged_num_splits(num_seqs, num_kv_heads, int(max_context_len), block_size,
+                              sm_count(query.device), int(num_splits))
+    if ns > 1 and not (ps >= block_size and ps % block_size == 0):
+        # the reference asserts this (paged.py:124)
+        raise _lib.InvalidArgument(f"partition_size={ps}, kv_block_size={block_size}")
+    out = torch.empty((num_seqs, num_q_heads, d_v), dtype=query.dtype, device=query.device)
+    a = _lib.DecodeArgs()
+    a.q = query.data_ptr()
+    a.q_stride_b, a.q_stride_h, a.q_stride_m = query.stride(0), query.stride(1), 0
+    a.k, a.v = key_cache.data_ptr(), value_cache.data_ptr()
+    a.k_stride_seq, a.k_stride_head, a.k_stride_tok = (key_cache.stride(0), key_cache.stride(1),
+                                                       key_cache.stride(2))
+    a.block_table = block_tables.data_ptr()
+    a.bt_stride = block_tables.stride(0)
+    a.page_size = block_size
+    a.seq_lens = context_lens.data_ptr()
+    a.batch, a.num_q_heads, a.num_kv_heads, a.m_q = num_seqs, num_q_heads, num_kv_heads, 1
+    a.d_qk, a.d_v = head_size, d_v
+    a.causal = 0
+    a.dtype = dtype_code(query)
+    a.scale = float(attn_scale)
+    a.num_splits, a.partition_size = ns, ps
+    a.o = out.data_ptr()
+    a.o_stride_b, a.o_stride_h, a.o_stride_m = out.stride(0), out.stride(1), 0
+    part = None
+    if ns > 1:
+        rows = num_seqs * num_q_heads
+        part = torch.empty(ns * rows * (d_v + 1), dtype=torch.float32, device=query.device)
+        a.part_o = part.data_ptr()
+        a.part_lse = part.data_ptr() + ns * rows * d_v * 4
+    _lib.check(_lib.lib().fa_paged_attention(ctypes.byref(a), stream_of(query)),
+               "fa_paged_attention")
+    return out
