@@ -90,6 +90,7 @@ SIGNATURES = [
     ("fa_mla_decode", _i32, [ctypes.POINTER(MlaArgs), _vp]),
     ("fa_mla_decode_partial", _i32, [ctypes.POINTER(MlaArgs), _vp]),
     ("fa_mla_combine", _i32, [ctypes.POINTER(MlaArgs), _vp]),
+    ("fa_mla_decode_static_workspace", _i32, [ctypes.POINTER(MlaArgs), _vp]),
 ]
 
 _lib = None

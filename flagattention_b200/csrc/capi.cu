@@ -189,6 +189,11 @@ int validate_mla(const fa_mla_args *a) {
 
 }  // namespace
 
+namespace fa {
+// Record a message for fa_last_error() from another translation unit.
+int record_error(int status, const char *msg) { return fail(status, "%s", msg); }
+}  // namespace fa
+
 extern "C" {
 
 int fa_version(void) { return (0 << 16) | (1 << 8) | 0; }

@@ -194,6 +194,20 @@ int fa_mla_decode_partial(const fa_mla_args *args, void *stream);
 /* Combine only (the decode kernel's split partials -> out / lse). */
 int fa_mla_combine(const fa_mla_args *args, void *stream);
 
+/* No counterpart in the reference.  fa_mla_decode for callers that cannot
+ * allocate device memory: serving engines that reserve nearly all of it for
+ * their KV-cache pool up front, and plugin / FFI hosts that pass device
+ * pointers but no allocator.  args->part_o / part_lse are ignored; the split
+ * scratch comes from an array of FA_MLA_STATIC_WORKSPACE_BYTES that the
+ * library defines in device memory (held by every GPU that loads it, until
+ * exit).  Calls needing more ((batch + num_sm_parts) * s_q * h_q * (d_v + 1)
+ * * 4 bytes, rounded) return FA_ERR_INVALID_ARGUMENT with the sizes in
+ * fa_last_error().  All calls on a device share the array: calls that
+ * overlap on the GPU race.  The first call on a device resolves the array's
+ * address; make it before capturing work into a stream. */
+#define FA_MLA_STATIC_WORKSPACE_BYTES (48u << 20)
+int fa_mla_decode_static_workspace(const fa_mla_args *args, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
