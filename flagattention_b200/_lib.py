@@ -8,7 +8,9 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libflagattn_b200.so")
+# FA_LIB_PATH selects another build of the same library (e.g. a debug build
+# with kernel tracing); by default the in-tree build is loaded.
+LIB_PATH = os.environ.get("FA_LIB_PATH") or os.path.join(_HERE, "libflagattn_b200.so")
 
 FA_OK = 0
 FA_ERR_INVALID_ARGUMENT = -1

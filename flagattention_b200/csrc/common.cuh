@@ -21,11 +21,15 @@ enum DeviceStatus : int {
   kDevTimeoutSoftmax = 3,
   kDevTimeoutExchange = 4,
   kDevTimeoutDrain = 5,
+  kDevBadSmemAlign = 6,
 };
 
-// Every wait on an mbarrier gives up after this long (globaltimer ns), sets
+// Every wait on an mbarrier gives up after this many SM clock cycles (about
+// 2 s at the B200's 1.9 GHz boost clock, longer when clocks are lower), sets
 // the CTA's abort flag and the device status word, and the kernel unwinds.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// The SM-local cycle counter is read instead of %globaltimer because it costs
+// a few cycles where the global timer costs hundreds, on every slow wait.
+constexpr long long kWaitLimitCycles = 4000000000ll;
 
 template <typename T> struct Elem;
 template <> struct Elem<__nv_bfloat16> {
@@ -104,19 +108,35 @@ __device__ __forceinline__ bool mbar_test_cluster(uint32_t bar, uint32_t parity)
   return ok != 0;
 }
 
+// Non-blocking probe of a phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_probe(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity.  Returns false (and raises the
-// CTA abort flag / device status) once kWaitLimitNs has passed, or as soon as
+// CTA abort flag / device status) once kWaitLimitCycles have passed, or as soon as
 // another role of the CTA has aborted.
 template <bool kClusterScope = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
                                           int *status, int code) {
-  if (kClusterScope ? mbar_test_cluster(bar, parity) : mbar_test(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t it = 1;; ++it) {
+  long long t0 = 0;
+  for (uint32_t it = 0;; ++it) {
     if (kClusterScope ? mbar_test_cluster(bar, parity) : mbar_test(bar, parity)) return true;
     if ((it & 63u) == 0) {
+      if (it == 0) {
+        t0 = clock64();
+        continue;
+      }
       if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (clock64() - t0 > kWaitLimitCycles) {
         *abort_flag = 1;
         if (status) atomicExch(status, code);
         return false;
@@ -251,6 +271,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() {

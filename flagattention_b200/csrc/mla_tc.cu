@@ -105,6 +105,46 @@ __device__ __forceinline__ Piece get_piece(const MlaParams &p, const int32_t *me
   return pc;
 }
 
+// Walks the tiles of a part's pieces in order, skipping empty pieces.
+// g counts tiles across pieces; qi counts the non-empty pieces started.
+struct TileCursor {
+  int piece, tok, tok0, tok_end, qi;
+  uint32_t g;
+  bool valid;
+
+  __device__ __forceinline__ void seek(const MlaParams &p, const int32_t *meta, int n_pieces,
+                                       bool sparse) {
+    while (piece < n_pieces) {
+      const Piece pc = get_piece(p, meta, piece, sparse);
+      if (pc.tok_end > pc.tok0) {
+        tok0 = tok = pc.tok0;
+        tok_end = pc.tok_end;
+        valid = true;
+        return;
+      }
+      ++piece;
+    }
+    valid = false;
+  }
+  __device__ __forceinline__ void start(const MlaParams &p, const int32_t *meta, int n_pieces,
+                                        bool sparse) {
+    piece = 0;
+    qi = 0;
+    g = 0;
+    seek(p, meta, n_pieces, sparse);
+  }
+  __device__ __forceinline__ void advance(const MlaParams &p, const int32_t *meta, int n_pieces,
+                                          bool sparse, int bn) {
+    tok += bn;
+    ++g;
+    if (tok >= tok_end) {
+      ++piece;
+      ++qi;
+      seek(p, meta, n_pieces, sparse);
+    }
+  }
+};
+
 template <typename T, int BN, bool kSparse>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     mla_decode_tc_kernel(const __grid_constant__ CUtensorMap q_map,
@@ -222,68 +262,81 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
+    // Two cursors walk the part's tiles: QK(g) may run ahead of PV; whichever
+    // is ready is issued (PV first: it frees a KV stage for the producer).
     if (lane == 0) {
       const uint32_t idesc_qk = umma_idesc_f16(128, BN, fmt, 0);
       const uint32_t idesc_pv = umma_idesc_f16(128, kDvHalf, fmt, 1);
-      uint32_t g = 0;
-      int qi = 0;
-      bool ok = true;
-      auto issue_pv = [&](uint32_t t, bool first_of_piece) -> bool {
-        const int st = t % kStages;
-        const uint32_t pb = t & 1u;
-        if (!mbar_wait(smem_u32(&bars->p_full[pb]), (t >> 1) & 1, abort_flag, p.status,
-                       kDevTimeoutMma))
-          return false;
-        if (first_of_piece &&
-            !mbar_wait(smem_u32(&bars->o_empty), (qi & 1) ^ 1, abort_flag, p.status,
-                       kDevTimeoutMma))
-          return false;
-        tc_fence_after();
-        const uint32_t vb = kv_base + st * Cfg::kStageBytes;
+      TileCursor cq, cp;
+      cq.start(p, meta, n_pieces, kSparse);
+      cp.start(p, meta, n_pieces, kSparse);
+      long long t_last = 0;
+      uint32_t idle = 0;
+      while (cp.valid) {
+        bool did = false;
+        if (cp.g < cq.g) {
+          const uint32_t t = cp.g;
+          const int st = t % kStages;
+          const uint32_t pb = t & 1u;
+          const bool first = cp.tok == cp.tok0;
+          if (mbar_probe(smem_u32(&bars->p_full[pb]), (t >> 1) & 1) &&
+              (!first || mbar_probe(smem_u32(&bars->o_empty), (cp.qi & 1) ^ 1))) {
+            tc_fence_after();
+            const uint32_t vb = kv_base + st * Cfg::kStageBytes;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bdesc = smem_desc_sw128(vb + kk * 16 * kChunkBytesRow,
-                                                 Cfg::kKvChunkBytes, 1024);
-          umma_ts(tmem + Cfg::kColO, tmem + Cfg::kColP + pb * (BN / 2) + kk * 8, bdesc, idesc_pv,
-                  (first_of_piece && kk == 0) ? 0u : 1u);
+            for (int kk = 0; kk < BN / 16; ++kk) {
+              const uint64_t bdesc = smem_desc_sw128(vb + kk * 16 * kChunkBytesRow,
+                                                     Cfg::kKvChunkBytes, 1024);
+              umma_ts(tmem + Cfg::kColO, tmem + Cfg::kColP + pb * (BN / 2) + kk * 8, bdesc,
+                      idesc_pv, (first && kk == 0) ? 0u : 1u);
+            }
+            tc_commit(smem_u32(&bars->kv_empty[st]));
+            tc_commit(smem_u32(&bars->pv_done[pb]));
+            cp.advance(p, meta, n_pieces, kSparse, BN);
+            did = true;
+          }
         }
-        tc_commit(smem_u32(&bars->kv_empty[st]));
-        tc_commit(smem_u32(&bars->pv_done[pb]));
-        return true;
-      };
-      for (int i = 0; i < n_pieces && ok; ++i) {
-        const Piece pc = get_piece(p, meta, i, kSparse);
-        if (pc.tok_end <= pc.tok0) continue;
-        ok = mbar_wait(smem_u32(&bars->q_full), qi & 1, abort_flag, p.status, kDevTimeoutMma);
-        if (!ok) break;
-        const uint32_t g_first = g;
-        for (int tok = pc.tok0; tok < pc.tok_end && ok; tok += BN, ++g) {
+        if (cq.valid) {
+          const uint32_t g = cq.g;
           const int st = g % kStages;
           const uint32_t sb = g & 1u;
-          ok = mbar_wait(smem_u32(&bars->kv_full[st]), (g / kStages) & 1, abort_flag, p.status,
-                         kDevTimeoutMma);
-          if (ok)
-            ok = mbar_wait(smem_u32(&bars->s_empty[sb]), ((g >> 1) & 1) ^ 1, abort_flag, p.status,
-                           kDevTimeoutMma);
-          if (!ok) break;
-          if (kSparse) fence_proxy_async_smem();  // cp.async rows -> tensor-core reads
-          tc_fence_after();
-          const uint32_t kb = kv_base + st * Cfg::kStageBytes;
-          for (int c = 0; c < n_chunks; ++c) {
+          const bool first = cq.tok == cq.tok0;
+          if ((!first || mbar_probe(smem_u32(&bars->q_full), cq.qi & 1)) &&
+              mbar_probe(smem_u32(&bars->kv_full[st]), (g / kStages) & 1) &&
+              mbar_probe(smem_u32(&bars->s_empty[sb]), ((g >> 1) & 1) ^ 1)) {
+            if (kSparse) fence_proxy_async_smem();  // cp.async rows -> tensor-core reads
+            tc_fence_after();
+            const uint32_t kb = kv_base + st * Cfg::kStageBytes;
+            for (int c = 0; c < n_chunks; ++c) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t adesc = smem_desc_sw128(q_base + c * kQChunkBytes + kk * 32, 16, 1024);
-              const uint64_t bdesc =
-                  smem_desc_sw128(kb + c * Cfg::kKvChunkBytes + kk * 32, 16, 1024);
-              umma_ss(tmem + Cfg::kColS + sb * BN, adesc, bdesc, idesc_qk, (c | kk) ? 1u : 0u);
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t adesc =
+                    smem_desc_sw128(q_base + c * kQChunkBytes + kk * 32, 16, 1024);
+                const uint64_t bdesc =
+                    smem_desc_sw128(kb + c * Cfg::kKvChunkBytes + kk * 32, 16, 1024);
+                umma_ss(tmem + Cfg::kColS + sb * BN, adesc, bdesc, idesc_qk, (c | kk) ? 1u : 0u);
+              }
             }
+            tc_commit(smem_u32(&bars->s_full[sb]));
+            if (cq.tok + BN >= cq.tok_end) tc_commit(smem_u32(&bars->q_empty));
+            cq.advance(p, meta, n_pieces, kSparse, BN);
+            did = true;
           }
-          tc_commit(smem_u32(&bars->s_full[sb]));
-          if (tok + BN >= pc.tok_end) tc_commit(smem_u32(&bars->q_empty));
-          if (g > g_first) ok = issue_pv(g - 1, g - 1 == g_first);
         }
-        if (ok) ok = issue_pv(g - 1, g - 1 == g_first);
-        ++qi;
+        if (did) {
+          idle = 0;
+          t_last = 0;
+        } else if ((++idle & 63u) == 0) {
+          if (*abort_flag) break;
+          const long long now = clock64();
+          if (t_last == 0) {
+            t_last = now;
+          } else if (now - t_last > kWaitLimitCycles) {
+            *abort_flag = 1;
+            if (p.status) atomicExch(p.status, kDevTimeoutMma);
+            break;
+          }
+        }
       }
       // Make sure every issued MMA has finished before TMEM is released.
       tc_commit(smem_u32(&bars->drain));
