@@ -47,6 +47,36 @@ def page_range(num_pages, world, rank):
     return num_pages * rank // world, num_pages * (rank + 1) // world
 
 
+def shard_pages(block_table, seq_lens, page_size, world, rank):
+    """This rank's share of every sequence's KV pages, for KV-page sharding.
+
+    block_table [B, W] and seq_lens [B] (any int array-likes; numpy or CPU
+    torch).  Sequence b has ceil(len / page_size) pages; the rank keeps pages
+    ``page_range(n_pages, world, rank)`` of it, so the ranks' token ranges tile
+    [0, len) in order and only the last rank holding pages can hold a partial
+    page.  Returns (local_block_table int32 [B, W'] with the kept page ids
+    left-aligned, local_lens int32 [B]) -- page ids are unchanged, i.e. they
+    still index the pool the rank's pages live in.
+    """
+    import numpy as np
+    bt = np.asarray(block_table, np.int64)
+    lens = np.asarray(seq_lens, np.int64)
+    B = lens.shape[0]
+    spans = []
+    for b in range(B):
+        n_pages = -(-int(lens[b]) // page_size)
+        lo, hi = page_range(n_pages, world, rank)
+        n_tok = max(0, min(int(lens[b]), hi * page_size) - lo * page_size)
+        spans.append((lo, hi, n_tok))
+    width = max([1] + [hi - lo for lo, hi, _ in spans])
+    local_bt = np.zeros((B, width), np.int32)
+    local_lens = np.zeros((B,), np.int32)
+    for b, (lo, hi, n_tok) in enumerate(spans):
+        local_bt[b, :hi - lo] = bt[b, lo:hi]
+        local_lens[b] = n_tok
+    return local_bt, local_lens
+
+
 def new_group_with_timeout(backend, seconds, **kw):
     """init_process_group with a short timeout so a dead rank ends the
     collective with an error instead of hanging its peers."""
@@ -84,13 +114,13 @@ def merge_partials(all_o, all_lse, out_dtype=torch.bfloat16):
     return out, lse
 
 
-def long_context_decode(q, kcache, block_table, seq_lens, softmax_scale=None, group=None):
-    """Decode sequences whose KV pages are split across the ranks of ``group``.
+def decode_partial(q, kcache, block_table, seq_lens, softmax_scale=None):
+    """One rank's share of a KV-page-sharded decode: f32 partial (O, LSE).
 
-    Each rank passes its own shard: ``kcache`` / ``block_table`` / ``seq_lens``
-    describe the tokens it holds (from ``page_range``).  q [B, 1, h_q, 576] is
-    replicated.  Returns (out [B, 1, h_q, 512] of q's dtype, lse f32
-    [B, h_q, 1]) identical on every rank.
+    q [B, 1, h_q, 576] (replicated); kcache / block_table / seq_lens describe
+    the tokens this rank holds (``shard_pages``).  Returns (part_o f32
+    [B, 1, h_q, 512], part_lse f32 [B, 1, h_q]); a rank holding no token of a
+    sequence gives O = 0 and LSE = -inf there, which the merge ignores.
     """
     from flagattention_b200.mla import flash_mla_with_kvcache, get_mla_metadata
     B, s_q, h_q, _ = q.shape
@@ -100,7 +130,18 @@ def long_context_decode(q, kcache, block_table, seq_lens, softmax_scale=None, gr
     part_o = torch.empty((B, s_q, h_q, 512), dtype=torch.float32, device=q.device)
     _, lse = flash_mla_with_kvcache(q, kcache, block_table, seq_lens, 512, meta, splits,
                                     softmax_scale=softmax_scale, out=part_o)
-    lse_rows = lse.transpose(1, 2).contiguous()            # [B, s_q, h_q] like part_o rows
-    all_o, all_l = exchange_partials(part_o, lse_rows, group)
+    return part_o, lse.transpose(1, 2).contiguous()     # lse rows ordered like part_o
+
+
+def long_context_decode(q, kcache, block_table, seq_lens, softmax_scale=None, group=None):
+    """Decode sequences whose KV pages are split across the ranks of ``group``.
+
+    Each rank passes its own shard: ``kcache`` / ``block_table`` / ``seq_lens``
+    describe the tokens it holds (``shard_pages``).  q [B, 1, h_q, 576] is
+    replicated.  Returns (out [B, 1, h_q, 512] of q's dtype, lse f32
+    [B, h_q, 1]) identical on every rank.
+    """
+    part_o, part_lse = decode_partial(q, kcache, block_table, seq_lens, softmax_scale)
+    all_o, all_l = exchange_partials(part_o, part_lse, group)
     out, lse_m = merge_partials(all_o, all_l, q.dtype)
     return out, lse_m.transpose(1, 2).contiguous()

@@ -46,16 +46,18 @@ def flash_attention(q, k, v, causal, sm_scale=None, return_log_normalizer=False)
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     g = H // Hk
-    kk = np.repeat(k, g, axis=1) if g > 1 else k
-    vv = np.repeat(v, g, axis=1) if g > 1 else v
-    s = np.matmul(q, np.swapaxes(kk, 2, 3)) * np.float32(sm_scale)
+    # grouped heads: query head h reads kv head h // g.  Broadcasting over the
+    # group axis gives the same products as the reference's repeat_interleave
+    # without materialising g copies of K and V.
+    qg = q.reshape(B, Hk, g, M, D)
+    s = np.matmul(qg, np.swapaxes(k, 2, 3)[:, :, None]) * np.float32(sm_scale)  # [B,Hk,g,M,N]
     if causal:
         p_seq = N - M
         mask = (np.arange(M)[:, None] + p_seq) >= np.arange(N)[None, :]
         s = np.where(mask, s, -np.inf).astype(np.float32)
-    lse = _logsumexp_rows(s) if return_log_normalizer else None
+    lse = _logsumexp_rows(s).reshape(B, H, M) if return_log_normalizer else None
     p = _softmax_rows(s)
-    o = np.matmul(p, vv).astype(np.float32)
+    o = np.matmul(p, v[:, :, None]).astype(np.float32).reshape(B, H, M, v.shape[-1])
     if return_log_normalizer:
         return o, lse
     return o
@@ -88,13 +90,11 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, s
         pages = np.asarray(block_tables[i])[tok // page]
         keys = key_cache[pages, :, tok % page, :]      # [n, Hkv, D]
         vals = value_cache[pages, :, tok % page, :]    # [n, Hkv, Dv]
-        if g > 1:
-            keys = np.repeat(keys, g, axis=1)
-            vals = np.repeat(vals, g, axis=1)
-        qh = query[i][:, None, :]                      # [Hq, 1, D]
-        s = np.matmul(qh, np.transpose(keys, (1, 2, 0))) * np.float32(scale)
+        # head h uses kv head h // g (the reference's repeat_interleave)
+        qh = query[i].reshape(Hkv, g, -1)              # [Hkv, g, D]
+        s = np.matmul(qh, np.transpose(keys, (1, 2, 0))) * np.float32(scale)  # [Hkv, g, n]
         p = _softmax_rows(s)
-        out[i] = np.matmul(p, np.transpose(vals, (1, 0, 2)))[:, 0, :]
+        out[i] = np.matmul(p, np.transpose(vals, (1, 0, 2))).reshape(Hq, dv)
     return out
 
 

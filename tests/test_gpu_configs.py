@@ -1,0 +1,245 @@
+"""BASELINE configs 3-5 at full size on one B200, plus KV-page sharding.
+
+Inputs of this size are generated on the device (seeded torch generator) and
+only sampled sequences are copied back for the CPU oracle; the rest of the
+batch is covered by size-independent properties: any scheduler partition
+gives the same result, and a KV-page-sharded decode merged with the combine
+kernel equals the unsharded decode.  Tolerances: atol/rtol 2e-2 against the
+oracle (bf16 output and f32 LSE); 1e-3 between two f32 results of the GPU
+path that differ only in where the KV range is split.
+"""
+
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import flagattention_b200 as fa
+import oracle
+from flagattention_b200 import _torch as fat
+from flagattention_b200 import shard
+from inputs import paged_pool
+from mla_cases import D_QK, D_V, assert_close
+
+pytestmark = pytest.mark.gpu
+
+PAGE = 64
+SCALE = D_QK ** -0.5
+
+
+def _device_inputs(seed, lens, s_q, heads=128):
+    """bf16 N(0,1) q [B, s_q, H, 576] and a randomly permuted page pool, made
+    on the GPU; the block table is the shared host generator's."""
+    bt, npages = paged_pool(lens, PAGE, seed + 1)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    B = len(lens)
+    q = torch.randn((B, s_q, heads, D_QK), generator=g, device="cuda").to(torch.bfloat16)
+    kc = torch.empty((npages, PAGE, 1, D_QK), dtype=torch.bfloat16, device="cuda")
+    step = 8192
+    for lo in range(0, npages, step):
+        hi = min(npages, lo + step)
+        kc[lo:hi] = torch.randn((hi - lo, PAGE, 1, D_QK), generator=g, device="cuda")
+    return q, kc, bt
+
+
+def _seq_rows(kc, bt, b, n):
+    """Sequence b's n cache rows as float32 numpy [n, 576] (logical order)."""
+    npg = -(-n // PAGE)
+    pages = torch.from_numpy(bt[b, :npg].astype(np.int64)).cuda()
+    return kc[pages].reshape(-1, D_QK)[:n].float().cpu().numpy()
+
+
+def _oracle_seq(q_b, rows, causal=False):
+    """Oracle decode of one sequence given its rows (pool of exactly its pages)."""
+    n = rows.shape[0]
+    npg = -(-n // PAGE)
+    pool = np.zeros((npg * PAGE, D_QK), np.float32)
+    pool[:n] = rows
+    return oracle.mla_decode_dense(q_b[None], pool.reshape(npg, PAGE, 1, D_QK),
+                                   np.arange(npg, dtype=np.int32)[None],
+                                   np.array([n], np.int32), D_V, SCALE, causal)
+
+
+def _decode(q, kc, bt_dev, lens_dev, causal=False, parts=None, out=None, indices=None, topk=None):
+    s_q, h_q = q.shape[1], q.shape[2]
+    meta, splits = fa.get_mla_metadata(lens_dev, s_q * h_q, 1,
+                                       num_heads_q=h_q if indices is not None else None,
+                                       topk=topk, num_sm_parts_override=parts)
+    o, lse = fa.flash_mla_with_kvcache(q, kc, bt_dev, lens_dev, D_V, meta, splits,
+                                       softmax_scale=SCALE, causal=causal, indices=indices,
+                                       out=out)
+    torch.cuda.synchronize()
+    assert fat.read_status(q.device) == 0, "a bounded wait inside a kernel gave up"
+    return o, lse
+
+
+def test_config3_mtp_full_size_sampled():
+    """Config 3: B=128, s_q=2 causal, 128 heads, log-uniform ctx in [4096, 32768]."""
+    rs = np.random.RandomState(3)
+    lens = np.exp(rs.uniform(np.log(4096), np.log(32768), size=128)).astype(np.int32)
+    q, kc, bt = _device_inputs(30, lens, 2)
+    bt_dev, lens_dev = torch.from_numpy(bt).cuda(), torch.from_numpy(lens).cuda()
+    o, lse = _decode(q, kc, bt_dev, lens_dev, causal=True)
+    _, splits = fa.get_mla_metadata(lens_dev, 256, 1)
+    assert len(set(np.diff(splits.cpu().numpy()).tolist())) > 1      # num_splits varies
+    o_np, lse_np = o.float().cpu().numpy(), lse.cpu().numpy()
+    q_np = q.float().cpu().numpy()
+    for b in [0, 31, int(np.argmax(lens)), 127]:
+        want_o, want_l = _oracle_seq(q_np[b], _seq_rows(kc, bt, b, int(lens[b])), causal=True)
+        assert_close(f"out[{b}]", o_np[b:b + 1], want_o)
+        assert_close(f"lse[{b}]", lse_np[b:b + 1], want_l)
+    o2, lse2 = _decode(q, kc, bt_dev, lens_dev, causal=True, parts=13)
+    assert_close("split invariance out", o2.float().cpu().numpy(), o_np, atol=1e-2, rtol=1e-2)
+    assert_close("split invariance lse", lse2.cpu().numpy(), lse_np, atol=1e-3, rtol=1e-3)
+
+
+def test_config4_sparse_full_size_sampled():
+    """Config 4: B=64, topk=2048 sorted indices from ctx in [32768, 131072],
+    plus short sequences whose index tail is -1 padding."""
+    rs = np.random.RandomState(4)
+    lens = rs.randint(32768, 131073, size=64).astype(np.int32)
+    lens[[5, 50]] = [1000, 2047]                                     # padded tails
+    q, kc, bt = _device_inputs(40, lens, 1)
+    topk = 2048
+    idx = np.full((64, 1, topk), -1, np.int32)
+    for b, n in enumerate(lens):
+        k = min(int(n), topk)
+        pos = np.sort(rs.choice(int(n), size=k, replace=False))
+        idx[b, 0, :k] = bt[b][pos // PAGE] * PAGE + pos % PAGE
+    bt_dev, lens_dev = torch.from_numpy(bt).cuda(), torch.from_numpy(lens).cuda()
+    idx_dev = torch.from_numpy(idx).cuda()
+    o, lse = _decode(q, kc, bt_dev, lens_dev, indices=idx_dev, topk=topk)
+    o_np, lse_np = o.float().cpu().numpy(), lse.cpu().numpy()
+    q_np = q.float().cpu().numpy()
+    flat = kc.view(-1, D_QK)
+    for b in [0, 5, 50, 63]:
+        valid = idx[b, 0][idx[b, 0] >= 0]
+        rows = flat[torch.from_numpy(valid.astype(np.int64)).cuda()].float().cpu().numpy()
+        local = np.full((1, 1, topk), -1, np.int32)
+        local[0, 0, :valid.size] = np.arange(valid.size)
+        want_o, want_l = oracle.mla_decode_sparse(q_np[b:b + 1], rows, local, D_V, SCALE)
+        assert_close(f"out[{b}]", o_np[b:b + 1], want_o)
+        assert_close(f"lse[{b}]", lse_np[b:b + 1], want_l)
+    o2, lse2 = _decode(q, kc, bt_dev, lens_dev, parts=11, indices=idx_dev, topk=topk)
+    assert_close("split invariance out", o2.float().cpu().numpy(), o_np, atol=1e-2, rtol=1e-2)
+    assert_close("split invariance lse", lse2.cpu().numpy(), lse_np, atol=1e-3, rtol=1e-3)
+
+
+def _sharded_on_one_gpu(q, kc, bt, lens, world):
+    """KV-page sharding with the ranks run one after another on this GPU:
+    decode_partial per rank, partials stacked in rank order (what the
+    all-gather delivers), merged by the combine kernel in f32."""
+    parts_o, parts_l = [], []
+    for rank in range(world):
+        lbt, llen = shard.shard_pages(bt, lens, PAGE, world, rank)
+        po, pl = shard.decode_partial(q, kc, torch.from_numpy(lbt).cuda(),
+                                      torch.from_numpy(llen).cuda(), SCALE)
+        parts_o.append(po)
+        parts_l.append(pl)
+    out, lse = shard.merge_partials(torch.stack(parts_o), torch.stack(parts_l), torch.float32)
+    torch.cuda.synchronize()
+    return out, lse.transpose(1, 2)
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_kv_page_sharding_matches_oracle(world):
+    """Sharded long-context decode against the oracle at a size it finishes."""
+    lens = np.array([20000, 777], np.int32)
+    q, kc, bt = _device_inputs(50 + world, lens, 1)
+    out, lse = _sharded_on_one_gpu(q, kc, bt, lens, world)
+    q_np = q.float().cpu().numpy()
+    for b in range(len(lens)):
+        want_o, want_l = _oracle_seq(q_np[b], _seq_rows(kc, bt, b, int(lens[b])))
+        assert_close(f"out[{b}]", out[b:b + 1].cpu().numpy(), want_o)
+        assert_close(f"lse[{b}]", lse[b:b + 1].cpu().numpy(), want_l)
+
+
+def test_config5_long_context_full_size():
+    """Config 5: B=2, 1,048,576-token contexts, 128 heads.  Sharded over 2, 4
+    and 8 page ranges (merged on device) equals the unsharded decode; one
+    sequence is checked against the oracle, evaluated chunk by chunk (the
+    oracle's flash_attention on 128K-token chunks merged by its lse_combine)."""
+    n = 1 << 20
+    lens = np.array([n, n], np.int32)
+    q, kc, bt = _device_inputs(60, lens, 1)
+    bt_dev, lens_dev = torch.from_numpy(bt).cuda(), torch.from_numpy(lens).cuda()
+    full = torch.empty((2, 1, 128, D_V), dtype=torch.float32, device="cuda")
+    _, full_lse = _decode(q, kc, bt_dev, lens_dev, out=full)
+    full_np, full_lse_np = full.cpu().numpy(), full_lse.cpu().numpy()
+    for world in (2, 4, 8):
+        out, lse = _sharded_on_one_gpu(q, kc, bt, lens, world)
+        assert_close(f"world {world} out", out.cpu().numpy(), full_np, atol=1e-3, rtol=1e-3)
+        assert_close(f"world {world} lse", lse.cpu().numpy(), full_lse_np, atol=1e-3, rtol=1e-3)
+    b, chunk = 1, 1 << 17
+    qb = q[b, 0].float().cpu().numpy()[None, :, None, :]                 # [1, 128, 1, 576]
+    npg_chunk = chunk // PAGE
+    po, pl = [], []
+    for c in range(n // chunk):
+        pages = torch.from_numpy(bt[b, c * npg_chunk:(c + 1) * npg_chunk].astype(np.int64)).cuda()
+        rows = kc[pages].reshape(-1, D_QK).float().cpu().numpy()[None, None]
+        o_c, l_c = oracle.flash_attention(qb, rows, rows[..., :D_V], False, SCALE, True)
+        po.append(o_c[0, :, 0])
+        pl.append(l_c[0, :, 0])
+    want_o, want_l = oracle.lse_combine(np.stack(po), np.stack(pl))
+    assert_close("oracle out", full_np[b, 0], want_o)
+    assert_close("oracle lse", full_lse_np[b, :, 0], want_l)
+
+
+def _nccl_worker(rank, world, port, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    try:
+        torch.cuda.set_device(rank)
+        shard.new_group_with_timeout("nccl", 60, rank=rank, world_size=world,
+                                     device_id=torch.device("cuda", rank))
+        lens = np.array([65536, 1000], np.int32)
+        bt, npages = paged_pool(lens, PAGE, 71)
+        g = torch.Generator().manual_seed(70)                       # same values on every rank
+        q = torch.randn((2, 1, 128, D_QK), generator=g).to(torch.bfloat16).cuda()
+        kc = torch.randn((npages, PAGE, 1, D_QK), generator=g).to(torch.bfloat16).cuda()
+        lbt, llen = shard.shard_pages(bt, lens, PAGE, world, rank)
+        out, lse = shard.long_context_decode(q, kc, torch.from_numpy(lbt).cuda(),
+                                             torch.from_numpy(llen).cuda(), SCALE)
+        torch.cuda.synchronize()
+        np.savez(os.path.join(outdir, f"rank{rank}.npz"), out=out.float().cpu().numpy(),
+                 lse=lse.cpu().numpy(), q=q.float().cpu().numpy() if rank == 0 else 0)
+        torch.distributed.destroy_process_group()
+    except Exception:
+        with open(os.path.join(outdir, f"rank{rank}.err"), "w") as f:
+            f.write(traceback.format_exc())
+        raise
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_long_context_nccl_two_gpus(tmp_path):
+    """Real 2-rank KV-page sharding: NCCL all-gather of partials + combine."""
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    hung = [p for p in procs if p.is_alive()]
+    for p in hung:
+        p.kill()
+        p.join(10)
+    errs = [f.read_text() for f in tmp_path.glob("*.err")]
+    assert not hung and all(p.exitcode == 0 for p in procs), errs
+    z0, z1 = np.load(tmp_path / "rank0.npz"), np.load(tmp_path / "rank1.npz")
+    assert np.array_equal(z0["out"], z1["out"]) and np.array_equal(z0["lse"], z1["lse"])
+    lens = np.array([65536, 1000], np.int32)
+    bt, npages = paged_pool(lens, PAGE, 71)
+    g = torch.Generator().manual_seed(70)
+    torch.randn((2, 1, 128, D_QK), generator=g)
+    kc = torch.randn((npages, PAGE, 1, D_QK), generator=g).to(torch.bfloat16).float().numpy()
+    want_o, want_l = oracle.mla_decode_dense(z0["q"], kc, bt, lens, D_V, SCALE)
+    assert_close("out", z0["out"], want_o)
+    assert_close("lse", z0["lse"], want_l)
