@@ -23,7 +23,7 @@ void launch_mla_combine(const float *, const float *, const int32_t *, int, int,
                         int, int64_t, int64_t, int64_t, float *, cudaStream_t);
 cudaError_t launch_generic_decode(const fa_decode_args *, cudaStream_t);
 size_t generic_smem_bytes(int, int);
-cudaError_t launch_mla_tc(const CUtensorMap &, const CUtensorMap &, const fa_mla_args *, int, int,
+cudaError_t launch_mla_tc(const CUtensorMap &, const CUtensorMap &, const fa_mla_args *, int,
                           int64_t, cudaStream_t);
 }  // namespace fa
 
@@ -91,14 +91,6 @@ int encode_map(CUtensorMap *map, const void *base, int dtype, uint64_t d, uint64
                 (unsigned long long)groups, (unsigned long long)strides[0],
                 (unsigned long long)strides[1]);
   return FA_OK;
-}
-
-int mla_block_n() {
-  static int bn = [] {
-    const char *e = getenv("FA_MLA_BLOCK_N");
-    return (e && atoi(e) == 32) ? 32 : 64;
-  }();
-  return bn;
 }
 
 int validate_decode(const fa_decode_args *a) {
@@ -174,7 +166,7 @@ int validate_mla(const fa_mla_args *a) {
   if (a->q_stride_h % 8 || a->q_stride_b % 8 || a->q_stride_s % 8 || a->kv_stride_tok % 8 ||
       a->kv_stride_page % 8 || a->o_stride_b % 8 || a->o_stride_s % 8 || a->o_stride_h % 8)
     return fail(FA_ERR_INVALID_ARGUMENT, "strides must be multiples of 8 elements (16 bytes)");
-  if (!sparse && a->s_q > 1 && a->q_stride_s != static_cast<int64_t>(a->h_q) * a->q_stride_h)
+  if (a->s_q > 1 && a->q_stride_s != static_cast<int64_t>(a->h_q) * a->q_stride_h)
     return fail(FA_ERR_UNSUPPORTED, "q rows (s_q, h_q) must be contiguous: q_stride_s == h_q*q_stride_h");
   if (a->page_size <= 0 || a->page_size % 64 != 0)
     return fail(FA_ERR_UNSUPPORTED, "page_size must be a multiple of 64 (got %d)", a->page_size);
@@ -356,7 +348,7 @@ int fa_mla_decode_partial(const fa_mla_args *a, void *stream) {
   if (st != FA_OK) return st;
   if (a->batch == 0) return FA_OK;
   const bool sparse = a->indices != nullptr;
-  const int bn = mla_block_n();
+  const int bn = FA_MLA_BLOCK_N;
   const int m_blocks = mla_m_blocks(a->s_q, a->h_q, sparse);
   CUtensorMap qm, km;
   st = encode_map(&qm, a->q, a->dtype, 576, static_cast<uint64_t>(a->s_q) * a->h_q, a->batch,
@@ -371,7 +363,7 @@ int fa_mla_decode_partial(const fa_mla_args *a, void *stream) {
                     a->kv_stride_tok, a->kv_stride_page, bn);
   if (st != FA_OK) return st;
   const int64_t total_rows = static_cast<int64_t>(a->num_pages) * a->page_size;
-  cudaError_t e = fa::launch_mla_tc(qm, km, a, bn, m_blocks, total_rows,
+  cudaError_t e = fa::launch_mla_tc(qm, km, a, m_blocks, total_rows,
                                     static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FA_OK : cuda_fail(e, "MLA decode launch");
 }

@@ -15,9 +15,17 @@
 // then hold the same S = S0 + S1 (f32 addition commutes, so bit-identical),
 // run the same online softmax and accumulate their half of O in TMEM.
 //
-// Warp roles (256 threads): warp 0 = TMA producer, warp 1 = TMEM owner and
+// Resource plan (per CTA).  Shared memory is spent on key rows in flight:
+//   TMEM   O [0,256) | Q latent half, bf16 pairs [256,384) | S0, S1 [384,512)
+//   smem   rope Q (rank 1) 16 KB | 4 KV stages x 40 KB | score exchange 32 KB
+//          | P (bf16, UMMA K-major) 16 KB
+// QK runs with A = Q from TMEM (16 MMAs) plus, on rank 1, 4 MMAs with the
+// rope part of Q from shared memory; PV runs with A = P from shared memory.
+//
+// Warp roles (384 threads): warp 0 = TMA producer, warp 1 = TMEM owner and
 // MMA issuer, warps 2-3 = key-row gatherers (sparse only), warps 4-7 =
-// softmax / correction / epilogue (thread i owns query row i).
+// softmax / correction / epilogue (thread i owns query row i), warps 8-11 =
+// query loaders (copy each piece's latent Q rows into TMEM).
 // Every mbarrier wait is bounded (common.cuh); a timeout sets the device
 // status word and the kernel unwinds instead of hanging.
 #include "common.cuh"
@@ -26,43 +34,68 @@
 namespace fa {
 
 constexpr int kRows = 128;
-constexpr int kChunkBytesRow = 128;               // 64 dims x 2 bytes per swizzle row
-constexpr int kMaxChunks = 5;                     // rank 1 holds dims 256..575
-constexpr int kQChunkBytes = kRows * kChunkBytesRow;
-constexpr int kQBytes = kMaxChunks * kQChunkBytes;  // 80 KB
-constexpr int kDvHalf = 256;                      // output dims per CTA
-constexpr int kPvChunks = kDvHalf / 64;           // 4
-constexpr float kRescaleThreshold = 8.0f;         // log2 units (factor 256)
+constexpr int kBN = FA_MLA_BLOCK_N;                 // 64 key rows per tile
+constexpr int kStages = 4;
+constexpr int kThreads = 512;
+constexpr int kSoftmaxThreads = 256;                // 8 warps: 2 column halves x 128 rows
+constexpr int kChunkBytesRow = 128;                 // 64 dims x 2 bytes per swizzle row
+constexpr int kMaxChunks = 5;                       // rank 1 holds dims 256..575
+constexpr int kChunkBytes = kBN * kChunkBytesRow;   // 8 KB: 64 key rows x 64 dims
+constexpr int kStageBytes = kMaxChunks * kChunkBytes;
+constexpr int kRopeBytes = kRows * kChunkBytesRow;  // 16 KB: 128 query rows x 64 rope dims
+constexpr int kXBytes = kRows * kBN * 4;            // f32 partial scores of one tile
+constexpr int kPBytes = kRows * kBN * 2;            // bf16/f16 probabilities of one tile
+constexpr int kRedBytes = 2 * 2 * kRows * 4;        // row maxima of the column halves, 2 tiles
+constexpr int kOffRope = 0;
+constexpr int kOffKv = kOffRope + kRopeBytes;
+constexpr int kOffX = kOffKv + kStages * kStageBytes;
+constexpr int kOffP = kOffX + kXBytes;
+constexpr int kOffRed = kOffP + kPBytes;
+constexpr int kOffBar = kOffRed + kRedBytes;
+constexpr int kSmemUsed = kOffBar + 256;
+constexpr int kSmemBytes = 232448;                  // all of it; the rest absorbs base alignment
+constexpr int kDvHalf = 256;                        // output dims per CTA
+constexpr int kPvChunks = kDvHalf / 64;             // 4
+constexpr int kLatentHalf = 256;                    // latent Q/K dims per CTA
+constexpr uint32_t kColO = 0, kColQ = 256, kColS = 384, kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;           // log2 units (factor 256)
+static_assert(kSmemUsed <= kSmemBytes, "shared memory plan exceeds 227 KB");
 
-template <int BN>
-struct TileCfg {
-  static constexpr int kStages = BN == 64 ? 2 : 5;
-  static constexpr int kKvChunkBytes = BN * kChunkBytesRow;
-  static constexpr int kStageBytes = kMaxChunks * kKvChunkBytes;
-  static constexpr int kXBytes = kRows * BN * 4;  // f32 partial scores
-  static constexpr int kOffKv = kQBytes;
-  static constexpr int kOffX = kOffKv + kStages * kStageBytes;
-  static constexpr int kOffBar = kOffX + 2 * kXBytes;
-  static constexpr int kSmemBytes = kOffBar + 512 + 1024;  // barriers + alignment slack
-  // TMEM columns: O [0,256), S0, S1 (BN each), P0, P1 (BN/2 each)
-  static constexpr uint32_t kColO = 0;
-  static constexpr uint32_t kColS = 256;
-  static constexpr uint32_t kColP = 256 + 2 * BN;
-  static constexpr uint32_t kTmemCols = 512;
-};
+
+#ifdef FA_TRACE
+// Debug builds only: per-tile SM-clock timestamps of two parts (both ranks).
+__device__ long long g_trace[2][2][64][16];
+#define FA_TRACE_EV(slot, tile)                                                    \
+  do {                                                                             \
+    const int tp_ = (part == 0) ? 0 : (part == 37 ? 1 : -1);                       \
+    if (tp_ >= 0 && (tile) < 64) g_trace[tp_][rank][(tile)][(slot)] = clock64();   \
+  } while (0)
+#else
+#define FA_TRACE_EV(slot, tile) \
+  do {                          \
+  } while (0)
+#endif
 
 struct MlaBarriers {
   uint64_t q_full, q_empty;
-  uint64_t kv_full[8], kv_empty[8];
+  uint64_t kv_full[kStages], kv_empty[kStages];
   uint64_t s_full[2], s_empty[2];
-  uint64_t p_full[2], pv_done[2];
-  uint64_t x_full[2];
+  uint64_t p_full, pv_done;
+  uint64_t x_full, x_free;
   uint64_t o_empty, drain;
+  uint64_t pair[4];  // the two softmax warps that share 32 query rows
+#ifdef FA_TRACE
+  uint64_t dbg;
+#endif
   uint32_t tmem_base;
   int abort_flag;
 };
 
+static_assert(sizeof(MlaBarriers) <= 256, "barrier block");
+
 struct MlaParams {
+  const uint16_t *q;       // query loaders read rows directly
+  int64_t q_sb, q_ss, q_sh;
   const int32_t *block_table;
   int64_t bt_stride;
   const int32_t *seq_lens;
@@ -96,11 +129,11 @@ __device__ __forceinline__ Piece get_piece(const MlaParams &p, const int32_t *me
   Piece pc;
   pc.b = meta[0] + i;
   const int len = sparse ? p.topk : (p.seq_lens ? p.seq_lens[pc.b] : p.n_ctx);
-  const int nblk = len > 0 ? (len + FA_MLA_BLOCK_N - 1) / FA_MLA_BLOCK_N : 0;
+  const int nblk = len > 0 ? (len + kBN - 1) / kBN : 0;
   const int lo = (i == 0) ? meta[1] : 0;
   const int hi = (pc.b == meta[2]) ? meta[3] : nblk;
-  pc.tok0 = lo * FA_MLA_BLOCK_N;
-  pc.tok_end = min(hi * FA_MLA_BLOCK_N, max(len, 0));
+  pc.tok0 = lo * kBN;
+  pc.tok_end = min(hi * kBN, max(len, 0));
   pc.split_idx = (i == 0) ? meta[4] : 0;
   return pc;
 }
@@ -134,8 +167,8 @@ struct TileCursor {
     seek(p, meta, n_pieces, sparse);
   }
   __device__ __forceinline__ void advance(const MlaParams &p, const int32_t *meta, int n_pieces,
-                                          bool sparse, int bn) {
-    tok += bn;
+                                          bool sparse) {
+    tok += kBN;
     ++g;
     if (tok >= tok_end) {
       ++piece;
@@ -145,20 +178,23 @@ struct TileCursor {
   }
 };
 
-template <typename T, int BN, bool kSparse>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
+template <typename T, bool kSparse>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mla_decode_tc_kernel(const __grid_constant__ CUtensorMap q_map,
                          const __grid_constant__ CUtensorMap kv_map, const MlaParams p) {
-  using Cfg = TileCfg<BN>;
-  constexpr int kStages = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
-  MlaBarriers *bars = reinterpret_cast<MlaBarriers *>(smem + Cfg::kOffBar);
+  if (smem + kSmemUsed > smem_raw + kSmemBytes) {  // uniform over the cluster
+    if (threadIdx.x == 0 && p.status) atomicExch(p.status, kDevBadSmemAlign);
+    return;
+  }
+  MlaBarriers *bars = reinterpret_cast<MlaBarriers *>(smem + kOffBar);
   const uint32_t s_base = smem_u32(smem);
-  const uint32_t q_base = s_base;
-  const uint32_t kv_base = s_base + Cfg::kOffKv;
-  const uint32_t x_base = s_base + Cfg::kOffX;
+  const uint32_t rope_base = s_base + kOffRope;
+  const uint32_t kv_base = s_base + kOffKv;
+  const uint32_t x_base = s_base + kOffX;
+  const uint32_t p_base = s_base + kOffP;
   volatile int *abort_flag = &bars->abort_flag;
 
   const uint32_t rank = cluster_rank();
@@ -168,7 +204,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n_chunks = 4 + static_cast<int>(rank);
-  const int dim0 = static_cast<int>(rank) * 256;
+  const int dim0 = static_cast<int>(rank) * kLatentHalf;
   const int32_t *meta = p.tile_meta + static_cast<int64_t>(part) * FA_MLA_META_INTS;
   const int n_pieces = meta[5];
   // query rows of this m-block: dense = 128 consecutive (s, h) rows; sparse =
@@ -179,7 +215,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   const int fmt = sizeof(T) == 2 && !std::is_same<T, __half>::value ? 1 : 0;
 
   if (threadIdx.x == 0) {
-    mbar_init(smem_u32(&bars->q_full), 1);
+    mbar_init(smem_u32(&bars->q_full), 128 + rank);  // loaders (+ rope TMA on rank 1)
     mbar_init(smem_u32(&bars->q_empty), 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&bars->kv_full[s]), kSparse ? 64 : 1);
@@ -187,18 +223,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&bars->s_full[i]), 1);
-      mbar_init(smem_u32(&bars->s_empty[i]), 128);
-      mbar_init(smem_u32(&bars->p_full[i]), 128);
-      mbar_init(smem_u32(&bars->pv_done[i]), 1);
-      mbar_init(smem_u32(&bars->x_full[i]), 1);
+      mbar_init(smem_u32(&bars->s_empty[i]), kSoftmaxThreads);
     }
-    mbar_init(smem_u32(&bars->o_empty), 128);
+    mbar_init(smem_u32(&bars->p_full), kSoftmaxThreads);
+    mbar_init(smem_u32(&bars->pv_done), 1);
+    mbar_init(smem_u32(&bars->x_full), 1);
+    mbar_init(smem_u32(&bars->x_free), kSoftmaxThreads / 32);  // the peer's softmax warps
+    mbar_init(smem_u32(&bars->o_empty), kSoftmaxThreads);
     mbar_init(smem_u32(&bars->drain), 1);
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&bars->pair[i]), 64);
+#ifdef FA_TRACE
+    mbar_init(smem_u32(&bars->dbg), 1);
+#endif
     bars->abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(&bars->tmem_base), Cfg::kTmemCols);
+    tmem_alloc(smem_u32(&bars->tmem_base), kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -206,11 +247,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   cluster_sync();  // the peer's barriers exist before any remote access
+  if (threadIdx.x == 0) FA_TRACE_EV(11, 0);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      tma_prefetch_desc(&q_map);
+      if (rank == 1) tma_prefetch_desc(&q_map);
       if (!kSparse) tma_prefetch_desc(&kv_map);
       uint32_t g = 0;
       int qi = 0;
@@ -218,19 +260,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       for (int i = 0; i < n_pieces && ok; ++i) {
         const Piece pc = get_piece(p, meta, i, kSparse);
         if (pc.tok_end <= pc.tok0) continue;
-        ok = mbar_wait(smem_u32(&bars->q_empty), (qi & 1) ^ 1, abort_flag, p.status,
-                       kDevTimeoutProducer);
-        if (!ok) break;
-        mbar_arrive_expect_tx(smem_u32(&bars->q_full), n_chunks * kQChunkBytes);
-        for (int c = 0; c < n_chunks; ++c)
-          tma_load_3d(q_base + c * kQChunkBytes, &q_map, smem_u32(&bars->q_full), dim0 + 64 * c,
-                      row0, pc.b);
+        if (rank == 1) {  // rope part of Q -> shared memory
+          ok = mbar_wait(smem_u32(&bars->q_empty), (qi & 1) ^ 1, abort_flag, p.status,
+                         kDevTimeoutProducer);
+          if (!ok) break;
+          mbar_arrive_expect_tx(smem_u32(&bars->q_full), kRopeBytes);
+          tma_load_3d(rope_base, &q_map, smem_u32(&bars->q_full), 512, row0, pc.b);
+        }
         ++qi;
         if (kSparse) {
-          g += (pc.tok_end - pc.tok0 + BN - 1) / BN;
+          g += (pc.tok_end - pc.tok0 + kBN - 1) / kBN;
           continue;
         }
-        for (int tok = pc.tok0; tok < pc.tok_end; tok += BN, ++g) {
+        for (int tok = pc.tok0; tok < pc.tok_end; tok += kBN, ++g) {
           const int st = g % kStages;
           const uint32_t n = g / kStages;
           int c1, c2;
@@ -245,16 +287,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
                          kDevTimeoutProducer);
           if (!ok) break;
           const uint32_t full = smem_u32(&bars->kv_full[st]);
-          mbar_arrive_expect_tx(full, n_chunks * Cfg::kKvChunkBytes);
-          const uint32_t dst = kv_base + st * Cfg::kStageBytes;
+          FA_TRACE_EV(0, g);
+          mbar_arrive_expect_tx(full, n_chunks * kChunkBytes);
+          const uint32_t dst = kv_base + st * kStageBytes;
           for (int c = 0; c < n_chunks; ++c)
-            tma_load_3d(dst + c * Cfg::kKvChunkBytes, &kv_map, full, dim0 + 64 * c, c1, c2);
+            tma_load_3d(dst + c * kChunkBytes, &kv_map, full, dim0 + 64 * c, c1, c2);
         }
       }
       // Drain: copies still in flight must land before the CTA may exit.
       if (*abort_flag) {
         volatile int never = 0;
-        if (qi > 0) mbar_wait(smem_u32(&bars->q_full), (qi - 1) & 1, &never, nullptr, 0);
+        if (rank == 1 && qi > 0)
+          mbar_wait(smem_u32(&bars->q_full), (qi - 1) & 1, &never, nullptr, 0);
         for (uint32_t t = g > kStages ? g - kStages : 0; t < g; ++t)
           mbar_wait(smem_u32(&bars->kv_full[t % kStages]), (t / kStages) & 1, &never, nullptr, 0);
       }
@@ -265,34 +309,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     // Two cursors walk the part's tiles: QK(g) may run ahead of PV; whichever
     // is ready is issued (PV first: it frees a KV stage for the producer).
     if (lane == 0) {
-      const uint32_t idesc_qk = umma_idesc_f16(128, BN, fmt, 0);
+      const uint32_t idesc_qk = umma_idesc_f16(128, kBN, fmt, 0);
       const uint32_t idesc_pv = umma_idesc_f16(128, kDvHalf, fmt, 1);
       TileCursor cq, cp;
       cq.start(p, meta, n_pieces, kSparse);
       cp.start(p, meta, n_pieces, kSparse);
       long long t_last = 0;
       uint32_t idle = 0;
+#ifdef FA_TRACE
+      uint32_t dbg_n = 0;
+#endif
       while (cp.valid) {
         bool did = false;
         if (cp.g < cq.g) {
           const uint32_t t = cp.g;
           const int st = t % kStages;
-          const uint32_t pb = t & 1u;
           const bool first = cp.tok == cp.tok0;
-          if (mbar_probe(smem_u32(&bars->p_full[pb]), (t >> 1) & 1) &&
+          if (mbar_probe(smem_u32(&bars->p_full), t & 1) &&
               (!first || mbar_probe(smem_u32(&bars->o_empty), (cp.qi & 1) ^ 1))) {
             tc_fence_after();
-            const uint32_t vb = kv_base + st * Cfg::kStageBytes;
+            FA_TRACE_EV(2, t);
+            const uint32_t vb = kv_base + st * kStageBytes;
 #pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk) {
-              const uint64_t bdesc = smem_desc_sw128(vb + kk * 16 * kChunkBytesRow,
-                                                     Cfg::kKvChunkBytes, 1024);
-              umma_ts(tmem + Cfg::kColO, tmem + Cfg::kColP + pb * (BN / 2) + kk * 8, bdesc,
-                      idesc_pv, (first && kk == 0) ? 0u : 1u);
+            for (int kk = 0; kk < kBN / 16; ++kk) {
+              const uint64_t adesc = smem_desc_sw128(p_base + kk * 32, 16, 1024);
+              const uint64_t bdesc = smem_desc_sw128(vb + kk * 16 * kChunkBytesRow, kChunkBytes, 1024);
+              umma_ss(tmem + kColO, adesc, bdesc, idesc_pv, (first && kk == 0) ? 0u : 1u);
             }
             tc_commit(smem_u32(&bars->kv_empty[st]));
-            tc_commit(smem_u32(&bars->pv_done[pb]));
-            cp.advance(p, meta, n_pieces, kSparse, BN);
+            tc_commit(smem_u32(&bars->pv_done));
+#ifdef FA_TRACE
+            {  // debug: wait for this tile's PV to finish
+              volatile int never = 0;
+              tc_commit(smem_u32(&bars->dbg));
+              mbar_wait(smem_u32(&bars->dbg), dbg_n & 1, &never, nullptr, 0);
+              ++dbg_n;
+              FA_TRACE_EV(13, t);
+            }
+#endif
+            cp.advance(p, meta, n_pieces, kSparse);
             did = true;
           }
         }
@@ -306,20 +361,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
               mbar_probe(smem_u32(&bars->s_empty[sb]), ((g >> 1) & 1) ^ 1)) {
             if (kSparse) fence_proxy_async_smem();  // cp.async rows -> tensor-core reads
             tc_fence_after();
-            const uint32_t kb = kv_base + st * Cfg::kStageBytes;
-            for (int c = 0; c < n_chunks; ++c) {
+            FA_TRACE_EV(1, g);
+            const uint32_t kb = kv_base + st * kStageBytes;
+            const uint32_t sd = tmem + kColS + sb * kBN;
+#pragma unroll
+            for (int c = 0; c < kLatentHalf / 64; ++c) {
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t adesc =
-                    smem_desc_sw128(q_base + c * kQChunkBytes + kk * 32, 16, 1024);
-                const uint64_t bdesc =
-                    smem_desc_sw128(kb + c * Cfg::kKvChunkBytes + kk * 32, 16, 1024);
-                umma_ss(tmem + Cfg::kColS + sb * BN, adesc, bdesc, idesc_qk, (c | kk) ? 1u : 0u);
+                const uint64_t bdesc = smem_desc_sw128(kb + c * kChunkBytes + kk * 32, 16, 1024);
+                umma_ts(sd, tmem + kColQ + (c * 4 + kk) * 8, bdesc, idesc_qk, (c | kk) ? 1u : 0u);
+              }
+            }
+            if (rank == 1) {
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t adesc = smem_desc_sw128(rope_base + kk * 32, 16, 1024);
+                const uint64_t bdesc = smem_desc_sw128(kb + 4 * kChunkBytes + kk * 32, 16, 1024);
+                umma_ss(sd, adesc, bdesc, idesc_qk, 1u);
               }
             }
             tc_commit(smem_u32(&bars->s_full[sb]));
-            if (cq.tok + BN >= cq.tok_end) tc_commit(smem_u32(&bars->q_empty));
-            cq.advance(p, meta, n_pieces, kSparse, BN);
+            if (cq.tok + kBN >= cq.tok_end) tc_commit(smem_u32(&bars->q_empty));
+#ifdef FA_TRACE
+            {  // debug: wait for this tile's QK to finish
+              volatile int never = 0;
+              tc_commit(smem_u32(&bars->dbg));
+              mbar_wait(smem_u32(&bars->dbg), dbg_n & 1, &never, nullptr, 0);
+              ++dbg_n;
+              FA_TRACE_EV(12, g);
+            }
+#endif
+            cq.advance(p, meta, n_pieces, kSparse);
             did = true;
           }
         }
@@ -355,14 +427,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const Piece pc = get_piece(p, meta, i, kSparse);
         if (pc.tok_end <= pc.tok0) continue;
         const int32_t *idx = p.indices + pc.b * p.idx_sb + s_tok * p.idx_ss;
-        for (int tok = pc.tok0; tok < pc.tok_end; tok += BN, ++g) {
+        for (int tok = pc.tok0; tok < pc.tok_end; tok += kBN, ++g) {
           const int st = g % kStages;
           ok = mbar_wait(smem_u32(&bars->kv_empty[st]), ((g / kStages) & 1) ^ 1, abort_flag,
                          p.status, kDevTimeoutProducer);
           if (!ok) break;
-          const uint32_t dst = kv_base + st * Cfg::kStageBytes;
+          const uint32_t dst = kv_base + st * kStageBytes;
           const int units = n_chunks * 8;  // 16-byte units per row
-          for (int k = gt; k < BN * units; k += 64) {
+          for (int k = gt; k < kBN * units; k += 64) {
             const int r = k / units;
             const int rem = k - r * units;
             const int c = rem >> 3, w = rem & 7;
@@ -375,31 +447,178 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
               const int64_t pg = row / p.page_size, off = row % p.page_size;
               src += (pg * p.kv_sp + off * p.kv_st + dim0 + c * 64 + w * 8) * 2;
             }
-            cp_async_16(dst + c * Cfg::kKvChunkBytes + r * kChunkBytesRow + ((w ^ (r & 7)) << 4),
-                        src, valid ? 16u : 0u);
+            cp_async_16(dst + c * kChunkBytes + r * kChunkBytesRow + ((w ^ (r & 7)) << 4), src,
+                        valid ? 16u : 0u);
           }
           cp_async_arrive(smem_u32(&bars->kv_full[st]));
         }
       }
       asm volatile("cp.async.wait_all;" ::: "memory");
     }
-  } else {
+  } else if (warp >= 12) {
+    // ------------------------------------------------------- query loaders
+    // Thread t copies query row t's latent half (256 dims) into TMEM columns
+    // [kColQ, kColQ + 128) as bf16/f16 pairs: the A operand of the QK MMAs.
+    // The first half of the next piece's row is fetched into registers while
+    // the current piece is in use.
+    const int t = (warp & 3) * 32 + lane;
+    const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const bool row_ok = t < n_rows;
+    const int flat = row0 + t;
+    const int s_tok = kSparse ? mb : (row_ok ? flat / p.h_q : 0);
+    const int h = kSparse ? t : (row_ok ? flat % p.h_q : 0);
+    uint32_t qr[kLatentHalf / 4];
+    auto next_piece = [&](int from) {
+      for (int j = from; j < n_pieces; ++j) {
+        const Piece pc = get_piece(p, meta, j, kSparse);
+        if (pc.tok_end > pc.tok0) return j;
+      }
+      return n_pieces;
+    };
+    auto fetch = [&](int j, int half) {  // dims [dim0 + 128 half, +128) -> qr
+      const Piece pc = get_piece(p, meta, j, kSparse);
+      const uint4 *src = reinterpret_cast<const uint4 *>(p.q + pc.b * p.q_sb + s_tok * p.q_ss +
+                                                         h * p.q_sh + dim0 + half * 128);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const uint4 v = row_ok ? __ldg(src + u) : make_uint4(0u, 0u, 0u, 0u);
+        qr[4 * u] = v.x;
+        qr[4 * u + 1] = v.y;
+        qr[4 * u + 2] = v.z;
+        qr[4 * u + 3] = v.w;
+      }
+    };
+    auto store = [&](int half) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t w[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) w[j] = qr[c * 16 + j];
+        tmem_st16(trow + kColQ + half * 64 + c * 16, w);
+      }
+    };
+    int qi = 0;
+    int i = next_piece(0);
+    if (i < n_pieces) fetch(i, 0);
+    while (i < n_pieces) {
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->q_empty), (qi & 1) ^ 1,
+                                                        abort_flag, p.status, kDevTimeoutProducer));
+      if (!ok) break;
+      tc_fence_after();
+      store(0);
+      fetch(i, 1);
+      store(1);
+      tmem_wait_st();
+      tc_fence_before();
+      if (t == 0) FA_TRACE_EV(10, qi);
+      mbar_arrive(smem_u32(&bars->q_full));
+      ++qi;
+      i = next_piece(i + 1);
+      if (i < n_pieces) fetch(i, 0);
+    }
+  } else if (warp >= 4) {
     // ------------------------------------------ softmax / correction / out
-    const int t = threadIdx.x - 128;  // query row within the m-block
-    const uint32_t lane_off = static_cast<uint32_t>((t >> 5) * 32) << 16;
-    const uint32_t trow = tmem + lane_off;
+    // 8 warps: warp w owns query rows 32 (w % 4) .. +31 (its TMEM lanes) and
+    // score columns [32 ch, 32 ch + 32) of every tile, ch = (w - 4) / 4.  The
+    // two warps of a row combine their row maxima through shared memory.
+    // The score exchange runs one tile ahead of the softmax math: tile g+1's
+    // partial scores travel to the peer while tile g's probabilities are
+    // computed.
+    const int ch = (warp - 4) >> 2;
+    const int t = (warp & 3) * 32 + lane;  // query row within the m-block
+    const int tt = ch * kRows + t;         // 0..255, splits shared work
+    const int c0 = ch * (kBN / 2);         // first score column of this thread
+    // bounded rendezvous of the two warps that share rows t (an mbarrier, so
+    // an aborting partner cannot leave this warp waiting forever)
+    const uint32_t pair_bar = smem_u32(&bars->pair[warp & 3]);
+    uint32_t pair_uses = 0;
+    auto pair_sync = [&]() -> bool {
+      mbar_arrive(pair_bar);
+      const bool r = __all_sync(0xffffffffu, mbar_wait(pair_bar, pair_uses & 1, abort_flag,
+                                                       p.status, kDevTimeoutSoftmax));
+      ++pair_uses;
+      return r;
+    };
+    const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    float *red = reinterpret_cast<float *>(smem + kOffRed);  // [tile parity][ch][row]
     const int flat = row0 + t;
     const bool row_ok = t < n_rows;
     const int s_tok = kSparse ? mb : (row_ok ? flat / p.h_q : 0);
     const int h = kSparse ? t : (row_ok ? flat % p.h_q : 0);
     const int out_flat = s_tok * p.h_q + h;
-    const uint32_t x_local[2] = {x_base, x_base + Cfg::kXBytes};
-    const uint32_t x_remote[2] = {map_to_rank(x_base, peer), map_to_rank(x_base + Cfg::kXBytes, peer)};
-    const uint32_t xf_local[2] = {smem_u32(&bars->x_full[0]), smem_u32(&bars->x_full[1])};
-    const uint32_t xf_remote[2] = {map_to_rank(xf_local[0], peer), map_to_rank(xf_local[1], peer)};
+    const uint32_t x_remote = map_to_rank(x_base, peer);
+    const uint32_t xf_local = smem_u32(&bars->x_full);
+    const uint32_t xf_remote = map_to_rank(xf_local, peer);
+    const uint32_t xfree_remote = map_to_rank(smem_u32(&bars->x_free), peer);
+    const float4 *xr = reinterpret_cast<const float4 *>(smem + kOffX);
+    bool ok = true;
+
+    // ---- score exchange, tile gx: own partial -> peer; peer's partial + own
+    TileCursor cx;
+    cx.start(p, meta, n_pieces, kSparse);
+    float so[kBN / 2];  // own partial scores of tile cx.g (in flight)
+    float sc[kBN / 2];  // full scores of the tile being processed
+    auto x_begin = [&]() -> bool {
+      const uint32_t gx = cx.g, sb = gx & 1u;
+      if (t == 0 && ch == 0) FA_TRACE_EV(14, gx);
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->s_full[sb]), (gx >> 1) & 1,
+                                             abort_flag, p.status, kDevTimeoutSoftmax)))
+        return false;
+      if (t == 0 && ch == 0) FA_TRACE_EV(3, gx);
+      tc_fence_after();
+      {
+        float v[16];
+        tmem_ld16(trow + kColS + sb * kBN + c0, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) so[j] = v[j];
+        tmem_ld16(trow + kColS + sb * kBN + c0 + 16, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) so[16 + j] = v[j];
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&bars->s_empty[sb]));
+      // the peer's buffer must have been drained of tile gx-1
+      if (!__all_sync(0xffffffffu, mbar_wait<true>(smem_u32(&bars->x_free), (gx & 1) ^ 1,
+                                                   abort_flag, p.status, kDevTimeoutExchange)))
+        return false;
+      if (t == 0 && ch == 0) {
+        FA_TRACE_EV(4, gx);
+        mbar_arrive_expect_tx(xf_local, kXBytes);
+      }
+#pragma unroll
+      for (int c = 0; c < kBN / 8; ++c)
+        st_async_v4(x_remote + ((ch * (kBN / 8) + c) * kRows + t) * 16, so[4 * c], so[4 * c + 1],
+                    so[4 * c + 2], so[4 * c + 3], xf_remote);
+      if (t == 0 && ch == 0) FA_TRACE_EV(5, gx);
+      return true;
+    };
+    auto x_end = [&]() -> bool {
+      const uint32_t gx = cx.g;
+      if (!__all_sync(0xffffffffu, mbar_wait<true>(xf_local, gx & 1, abort_flag, p.status,
+                                                   kDevTimeoutExchange)))
+        return false;
+      if (t == 0 && ch == 0) FA_TRACE_EV(6, gx);
+#pragma unroll
+      for (int c = 0; c < kBN / 8; ++c) {
+        const float4 o = xr[(ch * (kBN / 8) + c) * kRows + t];
+        sc[4 * c] = so[4 * c] + o.x;
+        sc[4 * c + 1] = so[4 * c + 1] + o.y;
+        sc[4 * c + 2] = so[4 * c + 2] + o.z;
+        sc[4 * c + 3] = so[4 * c + 3] + o.w;
+      }
+      // the loads above have returned (their values are summed), so the
+      // buffer may be refilled: no release ordering is needed for the signal
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote_relaxed(xfree_remote);
+      if (t == 0 && ch == 0) FA_TRACE_EV(15, gx);
+      cx.advance(p, meta, n_pieces, kSparse);
+      return true;
+    };
+    if (cx.valid) ok = x_begin() && x_end();
+
     uint32_t g = 0;
     int qi = 0;
-    bool ok = true;
     for (int i = 0; i < n_pieces && ok; ++i) {
       const Piece pc = get_piece(p, meta, i, kSparse);
       const int first_slot = p.num_splits[pc.b];
@@ -407,66 +626,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       const int slot = first_slot + pc.split_idx;
       const int len = kSparse ? p.topk : (p.seq_lens ? p.seq_lens[pc.b] : p.n_ctx);
       const int row_len = (p.causal && !kSparse) ? len - (p.s_q - 1 - s_tok) : len;
-      float m_run = -INFINITY, l_run = 0.f;
+      float m_run = -INFINITY, l_half = 0.f;
       const int32_t *idx = kSparse ? p.indices + pc.b * p.idx_sb + s_tok * p.idx_ss : nullptr;
       const bool has_tiles = pc.tok_end > pc.tok0;
-      for (int tok = pc.tok0; tok < pc.tok_end && ok; tok += BN, ++g) {
-        const uint32_t sb = g & 1u;
-        const uint32_t n = g >> 1;
+      for (int tok = pc.tok0; tok < pc.tok_end && ok; tok += kBN, ++g) {
         const bool first = tok == pc.tok0;
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->s_full[sb]), n & 1, abort_flag,
-                                               p.status, kDevTimeoutSoftmax));
-        if (!ok) break;
-        tc_fence_after();
-        float s[BN];
-#pragma unroll
-        for (int c = 0; c < BN / 16; ++c) {
-          float v[16];
-          tmem_ld16(trow + Cfg::kColS + sb * BN + c * 16, v);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) s[c * 16 + j] = v[j];
-        }
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(smem_u32(&bars->s_empty[sb]));
-        // exchange partial scores with the peer CTA
-        if (t == 0) mbar_arrive_expect_tx(xf_local[sb], Cfg::kXBytes);
-#pragma unroll
-        for (int c = 0; c < BN / 4; ++c)
-          st_async_v4(x_remote[sb] + (c * 128 + t) * 16, s[4 * c], s[4 * c + 1], s[4 * c + 2],
-                      s[4 * c + 3], xf_remote[sb]);
-        ok = __all_sync(0xffffffffu, mbar_wait<true>(xf_local[sb], n & 1, abort_flag, p.status,
-                                                     kDevTimeoutExchange));
-        if (!ok) break;
-        const float4 *xr = reinterpret_cast<const float4 *>(smem + Cfg::kOffX + sb * Cfg::kXBytes);
-#pragma unroll
-        for (int c = 0; c < BN / 4; ++c) {
-          const float4 o = xr[c * 128 + t];
-          s[4 * c] += o.x;
-          s[4 * c + 1] += o.y;
-          s[4 * c + 2] += o.z;
-          s[4 * c + 3] += o.w;
-        }
-        // mask and scale to log2 units
-        float mt = -INFINITY;
+        const bool more = cx.valid;  // tile g+1 exists
+        if (more && !(ok = x_begin())) break;
+        // mask: sparse rows by index, dense rows past the sequence / causal end
         if (kSparse) {
 #pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            const int pos = tok + c;
+          for (int c = 0; c < kBN / 2; ++c) {
+            const int pos = tok + c0 + c;
             const int64_t row = pos < pc.tok_end ? idx[pos] : -1;
-            const bool valid = row >= 0 && row < p.total_rows;
-            s[c] = valid ? s[c] * p.scale_log2 : -INFINITY;
-            mt = fmaxf(mt, s[c]);
+            if (!(row >= 0 && row < p.total_rows)) sc[c] = -INFINITY;
           }
-        } else {
+        } else if (tok + kBN > pc.tok_end || tok + kBN > row_len) {
+          const int lim = min(pc.tok_end, row_len) - tok - c0;
 #pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            const bool valid = tok + c < row_len && tok + c < pc.tok_end;
-            s[c] = valid ? s[c] * p.scale_log2 : -INFINITY;
-            mt = fmaxf(mt, s[c]);
-          }
+          for (int c = 0; c < kBN / 2; ++c)
+            if (c >= lim) sc[c] = -INFINITY;
         }
-        // online softmax with a lazily updated running max
+        float mx[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) mx[j] = sc[j];
+#pragma unroll
+        for (int c = 4; c < kBN / 2; c += 4) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) mx[j] = fmaxf(mx[j], sc[c + j]);
+        }
+        float mraw = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        float *rslot = red + (g & 1u) * 2 * kRows;
+        rslot[ch * kRows + t] = mraw;
+        if (!(ok = pair_sync())) break;
+        mraw = fmaxf(mraw, rslot[(ch ^ 1) * kRows + t]);
+        // online softmax with a lazily updated running max (log2 units)
+        const float mt = mraw * p.scale_log2;
         float alpha = 1.f;
         bool rescale = false;
         if (mt > -INFINITY && (m_run == -INFINITY || mt > m_run + kRescaleThreshold)) {
@@ -475,89 +670,104 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           m_run = mt;
         }
         const float ms = (m_run == -INFINITY) ? 0.f : m_run;
-        float psum = 0.f;
-        uint32_t pk[BN / 2];
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[kBN / 4];
 #pragma unroll
-        for (int c = 0; c < BN; c += 2) {
-          const float p0 = fast_exp2(s[c] - ms);
-          const float p1 = fast_exp2(s[c + 1] - ms);
-          psum += p0 + p1;
+        for (int c = 0; c < kBN / 2; c += 2) {
+          const float p0 = fast_exp2(fmaf(sc[c], p.scale_log2, -ms));
+          const float p1 = fast_exp2(fmaf(sc[c + 1], p.scale_log2, -ms));
+          ps[(c >> 1) & 3] += p0 + p1;
           pk[c / 2] = Elem<T>::pack2(p0, p1);
         }
-        l_run = l_run * alpha + psum;
-        // P buffer sb is free once PV of tile g-2 has finished
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done[sb]), (n & 1) ^ 1,
-                                               abort_flag, p.status, kDevTimeoutSoftmax));
+        l_half = l_half * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+        if (t == 0 && ch == 0) FA_TRACE_EV(7, g);
+        // the P buffer is free once PV of tile g-1 has finished (which also
+        // makes O safe to rescale)
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done), (g & 1) ^ 1, abort_flag,
+                                               p.status, kDevTimeoutSoftmax));
         if (!ok) break;
+        if (t == 0 && ch == 0) FA_TRACE_EV(8, g);
         if (__any_sync(0xffffffffu, rescale)) {
-          const uint32_t pt = g - 1;
-          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done[pt & 1u]), (pt >> 1) & 1,
-                                                 abort_flag, p.status, kDevTimeoutSoftmax));
-          if (!ok) break;
           tc_fence_after();
           const float a = rescale ? alpha : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < kDvHalf / 16; ++c) {
+          for (int c = 0; c < kDvHalf / 32; ++c) {
+            const uint32_t col = kColO + ch * (kDvHalf / 2) + c * 16;
             float v[16];
-            tmem_ld16(trow + Cfg::kColO + c * 16, v);
+            tmem_ld16(trow + col, v);
             tmem_wait_ld();
             uint32_t w[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) w[j] = __float_as_uint(v[j] * a);
-            tmem_st16(trow + Cfg::kColO + c * 16, w);
+            tmem_st16(trow + col, w);
+          }
+          tmem_wait_st();
+        }
+        // P row t, columns c0.. -> UMMA K-major SW128: 16-byte unit u at u ^ (t & 7)
+        {
+          uint8_t *prow = smem + kOffP + t * kChunkBytesRow;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int unit = ch * 4 + u;
+            *reinterpret_cast<uint4 *>(prow + ((unit ^ (t & 7)) << 4)) =
+                make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
           }
         }
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t w[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) w[j] = pk[c * 16 + j];
-          tmem_st16(trow + Cfg::kColP + sb * (BN / 2) + c * 16, w);
-        }
-        tmem_wait_st();
-        if (!kSparse && pc.tok_end - tok < BN) {
+        if (!kSparse && pc.tok_end - tok < kBN) {
           // rows past the sequence end may hold any bits (even NaN); P is 0
           // there but 0 * NaN is not, so clear them before the PV product.
           const int kv_valid = pc.tok_end - tok;
-          const int units = (BN - kv_valid) * kPvChunks * 8;
-          uint8_t *stage = smem + Cfg::kOffKv + (g % kStages) * Cfg::kStageBytes;
-          for (int u = t; u < units; u += 128) {
+          const int units = (kBN - kv_valid) * kPvChunks * 8;
+          uint8_t *stage = smem + kOffKv + (g % kStages) * kStageBytes;
+          for (int u = tt; u < units; u += kSoftmaxThreads) {
             const int r = kv_valid + u / (kPvChunks * 8);
             const int rem = u % (kPvChunks * 8);
-            *reinterpret_cast<uint4 *>(stage + (rem >> 3) * Cfg::kKvChunkBytes +
-                                       r * kChunkBytesRow + (rem & 7) * 16) =
-                make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4 *>(stage + (rem >> 3) * kChunkBytes + r * kChunkBytesRow +
+                                       (rem & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
           }
-          fence_proxy_async_smem();
         }
+        fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(smem_u32(&bars->p_full[sb]));
+        if (t == 0 && ch == 0) FA_TRACE_EV(9, g);
+        mbar_arrive(smem_u32(&bars->p_full));
+        if (more && !(ok = x_end())) break;
       }
       if (!ok) break;
       // -------------------------------------------------------- epilogue
+      // row sum = both column halves' sums (through the parity slot of the
+      // last tile, once the partner has read that tile's maximum)
+      float l_run = l_half;
+      if (has_tiles) {
+        float *rslot = red + ((g - 1) & 1u) * 2 * kRows;
+        if (!(ok = pair_sync())) break;
+        rslot[ch * kRows + t] = l_half;
+        if (!(ok = pair_sync())) break;
+        l_run = l_half + rslot[(ch ^ 1) * kRows + t];
+      }
       const bool final_out = n_split == 1;
       const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
       const float ms = (m_run == -INFINITY) ? 0.f : m_run;
       const float lse = l_run > 0.f ? ms * 0.69314718055994531f + logf(l_run) : -INFINITY;
       if (has_tiles) {
         const uint32_t lt = g - 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done[lt & 1u]), (lt >> 1) & 1,
-                                               abort_flag, p.status, kDevTimeoutSoftmax));
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done), lt & 1, abort_flag,
+                                               p.status, kDevTimeoutSoftmax));
         if (!ok) break;
         tc_fence_after();
       }
 #pragma unroll 1
-      for (int c = 0; c < kDvHalf / 16; ++c) {
+      for (int c = 0; c < kDvHalf / 32; ++c) {
+        const int col = ch * (kDvHalf / 2) + c * 16;
         float v[16];
         if (has_tiles) {
-          tmem_ld16(trow + Cfg::kColO + c * 16, v);
+          tmem_ld16(trow + kColO + col, v);
           tmem_wait_ld();
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = 0.f;
         }
         if (!row_ok) continue;
-        const int d = static_cast<int>(rank) * kDvHalf + c * 16;
+        const int d = static_cast<int>(rank) * kDvHalf + col;
         if (final_out && p.out_f32) {
           float4 *o = reinterpret_cast<float4 *>(static_cast<float *>(p.out) + pc.b * p.o_sb +
                                                  s_tok * p.o_ss + h * p.o_sh + d);
@@ -592,7 +802,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         mbar_arrive(smem_u32(&bars->o_empty));
         ++qi;
       }
-      if (rank == 0 && row_ok) {
+      if (rank == 0 && ch == 0 && row_ok) {
         if (final_out)
           p.lse[(static_cast<int64_t>(pc.b) * p.h_q + h) * p.s_q + s_tok] = lse;
         else
@@ -607,29 +817,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   cluster_sync();  // the peer no longer touches this CTA's shared memory
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, Cfg::kTmemCols);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
-template <typename T, int BN, bool kSparse>
+template <typename T, bool kSparse>
 static cudaError_t launch_mla_t(const CUtensorMap &qm, const CUtensorMap &km, const MlaParams &p,
                                 int num_parts, int m_blocks, cudaStream_t stream) {
-  auto kern = mla_decode_tc_kernel<T, BN, kSparse>;
-  const int smem = TileCfg<BN>::kSmemBytes;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  auto kern = mla_decode_tc_kernel<T, kSparse>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
   dim3 grid(2 * num_parts, m_blocks);
-  kern<<<grid, 256, smem, stream>>>(qm, km, p);
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(qm, km, p);
   return cudaGetLastError();
 }
 
-size_t mla_tc_smem_bytes(int block_n) {
-  return block_n == 64 ? TileCfg<64>::kSmemBytes : TileCfg<32>::kSmemBytes;
-}
-
 cudaError_t launch_mla_tc(const CUtensorMap &qm, const CUtensorMap &km, const fa_mla_args *a,
-                          int block_n, int m_blocks, int64_t total_rows, cudaStream_t stream) {
+                          int m_blocks, int64_t total_rows, cudaStream_t stream) {
   MlaParams p;
+  p.q = static_cast<const uint16_t *>(a->q);
+  p.q_sb = a->q_stride_b;
+  p.q_ss = a->q_stride_s;
+  p.q_sh = a->q_stride_h;
   p.block_table = a->block_table;
   p.bt_stride = a->bt_stride;
   p.seq_lens = a->seq_lens;
@@ -663,16 +872,19 @@ cudaError_t launch_mla_tc(const CUtensorMap &qm, const CUtensorMap &km, const fa
   p.status = a->status;
   const bool sparse = a->indices != nullptr;
   const bool f16 = a->dtype == FA_DTYPE_F16;
-#define FA_LAUNCH(T_, BN_, SP_) return launch_mla_t<T_, BN_, SP_>(qm, km, p, a->num_sm_parts, m_blocks, stream)
-  if (block_n == 64) {
-    if (f16) { if (sparse) FA_LAUNCH(__half, 64, true); FA_LAUNCH(__half, 64, false); }
-    if (sparse) FA_LAUNCH(__nv_bfloat16, 64, true);
-    FA_LAUNCH(__nv_bfloat16, 64, false);
+  if (f16) {
+    if (sparse) return launch_mla_t<__half, true>(qm, km, p, a->num_sm_parts, m_blocks, stream);
+    return launch_mla_t<__half, false>(qm, km, p, a->num_sm_parts, m_blocks, stream);
   }
-  if (f16) { if (sparse) FA_LAUNCH(__half, 32, true); FA_LAUNCH(__half, 32, false); }
-  if (sparse) FA_LAUNCH(__nv_bfloat16, 32, true);
-  FA_LAUNCH(__nv_bfloat16, 32, false);
-#undef FA_LAUNCH
+  if (sparse) return launch_mla_t<__nv_bfloat16, true>(qm, km, p, a->num_sm_parts, m_blocks, stream);
+  return launch_mla_t<__nv_bfloat16, false>(qm, km, p, a->num_sm_parts, m_blocks, stream);
 }
+
+#ifdef FA_TRACE
+extern "C" int fa_debug_trace_read(void *dst, size_t bytes) {
+  return cudaMemcpyFromSymbol(dst, g_trace, bytes < sizeof(g_trace) ? bytes : sizeof(g_trace)) ==
+                 cudaSuccess ? 0 : -1;
+}
+#endif
 
 }  // namespace fa
