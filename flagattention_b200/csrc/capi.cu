@@ -23,8 +23,8 @@ void launch_mla_combine(const float *, const float *, const int32_t *, int, int,
                         int, int64_t, int64_t, int64_t, float *, cudaStream_t);
 cudaError_t launch_generic_decode(const fa_decode_args *, cudaStream_t);
 size_t generic_smem_bytes(int, int);
-cudaError_t launch_mla_tc(const CUtensorMap &, const CUtensorMap &, const fa_mla_args *, int,
-                          int64_t, cudaStream_t);
+cudaError_t launch_mla_tc(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
+                          const fa_mla_args *, int, int64_t, cudaStream_t);
 }  // namespace fa
 
 namespace {
@@ -68,21 +68,23 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// 3-D bf16/f16 map {d, rows, groups} with a {64, box_rows, 1} box, 128-byte
-// swizzle (the UMMA K-major / MN-major SW128 canonical layout).
+// 3-D bf16/f16 map {d, rows, groups} with a {box_inner, box_rows, 1} box and
+// the swizzle that matches the box width: 64 dims -> 128-byte swizzle, 32
+// dims -> 64-byte swizzle (the UMMA SW128 / SW64 canonical layouts).
 int encode_map(CUtensorMap *map, const void *base, int dtype, uint64_t d, uint64_t rows,
                uint64_t groups, uint64_t row_stride_elems, uint64_t group_stride_elems,
-               uint32_t box_rows) {
+               uint32_t box_rows, uint32_t box_inner = 64) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {d, rows, groups};
   cuuint64_t strides[2] = {row_stride_elems * 2, group_stride_elems * 2};
-  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = enc(map, dtype == FA_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                               : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                    3, const_cast<void *>(base), dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   box_inner == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(FA_ERR_INVALID_ARGUMENT,
@@ -293,6 +295,7 @@ int fa_lse_combine(const float *part_o, const float *part_lse, int num_parts, in
                    int d_v, void *o, int dtype, float *lse, void *stream) {
   if (!part_o || !part_lse || !o || num_parts < 1 || rows < 0 || d_v <= 0 || d_v % 4)
     return fail(FA_ERR_INVALID_ARGUMENT, "bad combine arguments");
+  if (d_v > 512) return fail(FA_ERR_UNSUPPORTED, "combine supports d_v <= 512 (got %d)", d_v);
   if (!aligned16(part_o)) return fail(FA_ERR_INVALID_ARGUMENT, "part_o must be 16-byte aligned");
   fa::launch_lse_combine(part_o, part_lse, num_parts, rows, 1, 1, d_v, o, dtype, d_v, 0, 0, lse,
                          static_cast<cudaStream_t>(stream));
@@ -350,20 +353,21 @@ int fa_mla_decode_partial(const fa_mla_args *a, void *stream) {
   const bool sparse = a->indices != nullptr;
   const int bn = FA_MLA_BLOCK_N;
   const int m_blocks = mla_m_blocks(a->s_q, a->h_q, sparse);
-  CUtensorMap qm, km;
-  st = encode_map(&qm, a->q, a->dtype, 576, static_cast<uint64_t>(a->s_q) * a->h_q, a->batch,
-                  a->q_stride_h, a->q_stride_b, 128);
+  CUtensorMap qrm, km, krm;
+  st = encode_map(&qrm, a->q, a->dtype, 576, static_cast<uint64_t>(a->s_q) * a->h_q, a->batch,
+                  a->q_stride_h, a->q_stride_b, 128, 32);
   if (st != FA_OK) return st;
   const bool paged = a->block_table != nullptr;
-  if (sparse || paged)
-    st = encode_map(&km, a->kcache, a->dtype, 576, a->page_size, a->num_pages, a->kv_stride_tok,
-                    a->kv_stride_page, bn);
-  else
-    st = encode_map(&km, a->kcache, a->dtype, 576, a->n_ctx > 0 ? a->n_ctx : 1, a->batch,
-                    a->kv_stride_tok, a->kv_stride_page, bn);
+  const uint64_t kv_rows = (sparse || paged) ? a->page_size : (a->n_ctx > 0 ? a->n_ctx : 1);
+  const uint64_t kv_groups = (sparse || paged) ? a->num_pages : a->batch;
+  st = encode_map(&km, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
+                  a->kv_stride_page, bn, 64);
+  if (st != FA_OK) return st;
+  st = encode_map(&krm, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
+                  a->kv_stride_page, bn, 32);
   if (st != FA_OK) return st;
   const int64_t total_rows = static_cast<int64_t>(a->num_pages) * a->page_size;
-  cudaError_t e = fa::launch_mla_tc(qm, km, a, m_blocks, total_rows,
+  cudaError_t e = fa::launch_mla_tc(qrm, km, krm, a, m_blocks, total_rows,
                                     static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FA_OK : cuda_fail(e, "MLA decode launch");
 }

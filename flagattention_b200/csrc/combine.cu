@@ -2,8 +2,8 @@
 //
 // Same algebra as the reference's _fwd_combine_kv_splits (split_kv.py:198-228):
 //   lse = m + log(sum_s exp(lse_s - m)),  o = sum_s exp(lse_s - lse) * o_s
-// with f32 partials.  One warp per output row; lanes stride over the value
-// dims with 16-byte loads, so the kernel streams the partials at HBM rate.
+// with f32 partials.  One warp per output row (d_v <= 512); lanes stride over
+// the value dims with 16-byte loads.
 #include "common.cuh"
 #include "flagattn_b200.h"
 
@@ -41,19 +41,36 @@ __device__ __forceinline__ float merge_row(const float *__restrict__ part_o,
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
   const float lse = (z > 0.f) ? msafe + __logf(z) : -INFINITY;
-  for (int d = lane * 4; d < d_v; d += 128) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < n; ++s) {
-      const float ls = part_lse[(first_slot + s) * lse_slot_stride + lse_row];
-      const float w = (lse == -INFINITY || ls == -INFINITY) ? 0.f : __expf(ls - lse);
-      const float4 v = *reinterpret_cast<const float4 *>(part_o + (first_slot + s) * o_slot_stride +
-                                                         o_row_off + d);
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
+  // Each lane owns up to 4 float4 columns (d = 4 lane + 128 k).  All of a
+  // partial's loads are issued before they are used, and two partials are
+  // in flight at a time, so the warp keeps ~8 loads outstanding per lane.
+  float4 acc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
+  for (int s = 0; s < n; ++s) {
+    const float ls = part_lse[(first_slot + s) * lse_slot_stride + lse_row];
+    const float w = (lse == -INFINITY || ls == -INFINITY) ? 0.f : __expf(ls - lse);
+    const float *src = part_o + (first_slot + s) * o_slot_stride + o_row_off;
+    float4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int d = lane * 4 + k * 128;
+      v[k] = d < d_v ? __ldg(reinterpret_cast<const float4 *>(src + d))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    store4<T>(out + d, acc);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      acc[k].x += w * v[k].x;
+      acc[k].y += w * v[k].y;
+      acc[k].z += w * v[k].z;
+      acc[k].w += w * v[k].w;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int d = lane * 4 + k * 128;
+    if (d < d_v) store4<T>(out + d, acc[k]);
   }
   return lse;
 }

@@ -303,6 +303,17 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   d |= 2ull << 61;  // SWIZZLE_128B
   return d;
 }
+// K-major operand in the 64-byte swizzle layout (rows of 32 bf16/f16 dims,
+// 8-row atoms of 512 bytes): SBO = 512.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;  // version
+  d |= 4ull << 61;  // SWIZZLE_64B
+  return d;
+}
 // Instruction descriptor, kind::f16 with f32 accumulation.
 // fmt: 0 = f16, 1 = bf16; b_mn_major: B operand stored N-contiguous.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, int fmt, int b_mn_major) {

@@ -14,18 +14,21 @@
 // st.async (distributed shared memory) and adds the peer's partial: both CTAs
 // then hold the same S = S0 + S1 (f32 addition commutes, so bit-identical),
 // run the same online softmax and accumulate their half of O in TMEM.
+// Precisely, rank r takes latent dims [256 r, 256 r + 256) and rope dims
+// [512 + 32 r, 512 + 32 r + 32), so both ranks move 36 KB per 64-row tile.
 //
 // Resource plan (per CTA).  Shared memory is spent on key rows in flight:
-//   TMEM   O [0,256) | Q latent half, bf16 pairs [256,384) | S0, S1 [384,512)
-//   smem   rope Q (rank 1) 16 KB | 4 KV stages x 40 KB | score exchange 32 KB
-//          | P (bf16, UMMA K-major) 16 KB
-// QK runs with A = Q from TMEM (16 MMAs) plus, on rank 1, 4 MMAs with the
-// rope part of Q from shared memory; PV runs with A = P from shared memory.
+//   TMEM   O [0,256) | Q latent half, bf16 pairs [256,384) | S [384,448)
+//          | P0, P1 (bf16 pairs) [448,512)
+//   smem   rope Q 8 KB | 4 KV stages x 36 KB | 2 score-exchange slots x 32 KB
+// QK runs with A = Q from TMEM (16 MMAs) plus 2 MMAs with the rope part of Q
+// from shared memory (64-byte swizzle); PV runs with A = P from TMEM.
 //
-// Warp roles (384 threads): warp 0 = TMA producer, warp 1 = TMEM owner and
-// MMA issuer, warps 2-3 = key-row gatherers (sparse only), warps 4-7 =
-// softmax / correction / epilogue (thread i owns query row i), warps 8-11 =
-// query loaders (copy each piece's latent Q rows into TMEM).
+// Warp roles (512 threads): warp 0 = TMA producer, warp 1 = TMEM owner and
+// MMA issuer, warps 2-3 = key-row gatherers (sparse only), warps 4-11 =
+// softmax / correction / epilogue (2 warps per 32 query rows, one per half of
+// the tile's columns), warps 12-15 = query loaders (copy each piece's latent
+// Q rows into TMEM).
 // Every mbarrier wait is bounded (common.cuh); a timeout sets the device
 // status word and the kernel unwinds instead of hanging.
 #include "common.cuh"
@@ -39,27 +42,30 @@ constexpr int kStages = 4;
 constexpr int kThreads = 512;
 constexpr int kSoftmaxThreads = 256;                // 8 warps: 2 column halves x 128 rows
 constexpr int kChunkBytesRow = 128;                 // 64 dims x 2 bytes per swizzle row
-constexpr int kMaxChunks = 5;                       // rank 1 holds dims 256..575
+constexpr int kLatentChunks = 4;                    // latent dims per CTA / 64
 constexpr int kChunkBytes = kBN * kChunkBytesRow;   // 8 KB: 64 key rows x 64 dims
-constexpr int kStageBytes = kMaxChunks * kChunkBytes;
-constexpr int kRopeBytes = kRows * kChunkBytesRow;  // 16 KB: 128 query rows x 64 rope dims
+constexpr int kRopeDims = 32;                       // rope dims per CTA
+constexpr int kRopeRowBytes = kRopeDims * 2;        // 64-byte swizzle rows
+constexpr int kKvRopeBytes = kBN * kRopeRowBytes;   // 4 KB
+constexpr int kStageBytes = kLatentChunks * kChunkBytes + kKvRopeBytes;  // 36 KB
+constexpr int kQRopeBytes = kRows * kRopeRowBytes;  // 8 KB: 128 query rows x 32 rope dims
 constexpr int kXBytes = kRows * kBN * 4;            // f32 partial scores of one tile
-constexpr int kPBytes = kRows * kBN * 2;            // bf16/f16 probabilities of one tile
 constexpr int kRedBytes = 2 * 2 * kRows * 4;        // row maxima of the column halves, 2 tiles
 constexpr int kOffRope = 0;
-constexpr int kOffKv = kOffRope + kRopeBytes;
+constexpr int kOffKv = kOffRope + kQRopeBytes;
 constexpr int kOffX = kOffKv + kStages * kStageBytes;
-constexpr int kOffP = kOffX + kXBytes;
-constexpr int kOffRed = kOffP + kPBytes;
+constexpr int kOffRed = kOffX + 2 * kXBytes;
 constexpr int kOffBar = kOffRed + kRedBytes;
 constexpr int kSmemUsed = kOffBar + 256;
-constexpr int kSmemBytes = 232448;                  // all of it; the rest absorbs base alignment
+constexpr int kSmemBytes = kSmemUsed + 1024;        // + base alignment slack
 constexpr int kDvHalf = 256;                        // output dims per CTA
 constexpr int kPvChunks = kDvHalf / 64;             // 4
 constexpr int kLatentHalf = 256;                    // latent Q/K dims per CTA
-constexpr uint32_t kColO = 0, kColQ = 256, kColS = 384, kTmemCols = 512;
+constexpr uint32_t kColO = 0, kColQ = 256, kColS = 384, kColP = 448, kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;           // log2 units (factor 256)
-static_assert(kSmemUsed <= kSmemBytes, "shared memory plan exceeds 227 KB");
+static_assert(kSmemBytes <= 232448, "shared memory plan exceeds 227 KB");
+static_assert(kOffKv % 1024 == 0 && kStageBytes % 1024 == 0 && kOffX % 1024 == 0,
+              "swizzled operands need 1024-byte alignment");
 
 
 #ifdef FA_TRACE
@@ -79,9 +85,9 @@ __device__ long long g_trace[2][2][64][16];
 struct MlaBarriers {
   uint64_t q_full, q_empty;
   uint64_t kv_full[kStages], kv_empty[kStages];
-  uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, pv_done;
-  uint64_t x_full, x_free;
+  uint64_t s_full, s_empty;
+  uint64_t p_full[2], pv_done[2];
+  uint64_t x_full[2];
   uint64_t o_empty, drain;
   uint64_t pair[4];  // the two softmax warps that share 32 query rows
 #ifdef FA_TRACE
@@ -180,8 +186,9 @@ struct TileCursor {
 
 template <typename T, bool kSparse>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    mla_decode_tc_kernel(const __grid_constant__ CUtensorMap q_map,
-                         const __grid_constant__ CUtensorMap kv_map, const MlaParams p) {
+    mla_decode_tc_kernel(const __grid_constant__ CUtensorMap q_rope_map,
+                         const __grid_constant__ CUtensorMap kv_map,
+                         const __grid_constant__ CUtensorMap kv_rope_map, const MlaParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
@@ -194,7 +201,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t rope_base = s_base + kOffRope;
   const uint32_t kv_base = s_base + kOffKv;
   const uint32_t x_base = s_base + kOffX;
-  const uint32_t p_base = s_base + kOffP;
   volatile int *abort_flag = &bars->abort_flag;
 
   const uint32_t rank = cluster_rank();
@@ -203,8 +209,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int mb = blockIdx.y;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_chunks = 4 + static_cast<int>(rank);
-  const int dim0 = static_cast<int>(rank) * kLatentHalf;
+  const int dim0 = static_cast<int>(rank) * kLatentHalf;        // latent dims of this CTA
+  const int rope0 = 512 + static_cast<int>(rank) * kRopeDims;   // rope dims of this CTA
   const int32_t *meta = p.tile_meta + static_cast<int64_t>(part) * FA_MLA_META_INTS;
   const int n_pieces = meta[5];
   // query rows of this m-block: dense = 128 consecutive (s, h) rows; sparse =
@@ -215,20 +221,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int fmt = sizeof(T) == 2 && !std::is_same<T, __half>::value ? 1 : 0;
 
   if (threadIdx.x == 0) {
-    mbar_init(smem_u32(&bars->q_full), 128 + rank);  // loaders (+ rope TMA on rank 1)
+    mbar_init(smem_u32(&bars->q_full), 128 + 1);  // loaders + the rope TMA
     mbar_init(smem_u32(&bars->q_empty), 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&bars->kv_full[s]), kSparse ? 64 : 1);
       mbar_init(smem_u32(&bars->kv_empty[s]), 1);
     }
+    mbar_init(smem_u32(&bars->s_full), 1);
+    mbar_init(smem_u32(&bars->s_empty), kSoftmaxThreads);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&bars->s_full[i]), 1);
-      mbar_init(smem_u32(&bars->s_empty[i]), kSoftmaxThreads);
+      mbar_init(smem_u32(&bars->p_full[i]), kSoftmaxThreads);
+      mbar_init(smem_u32(&bars->pv_done[i]), 1);
+      mbar_init(smem_u32(&bars->x_full[i]), 1);
     }
-    mbar_init(smem_u32(&bars->p_full), kSoftmaxThreads);
-    mbar_init(smem_u32(&bars->pv_done), 1);
-    mbar_init(smem_u32(&bars->x_full), 1);
-    mbar_init(smem_u32(&bars->x_free), kSoftmaxThreads / 32);  // the peer's softmax warps
     mbar_init(smem_u32(&bars->o_empty), kSoftmaxThreads);
     mbar_init(smem_u32(&bars->drain), 1);
     for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&bars->pair[i]), 64);
@@ -252,21 +257,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      if (rank == 1) tma_prefetch_desc(&q_map);
-      if (!kSparse) tma_prefetch_desc(&kv_map);
+      tma_prefetch_desc(&q_rope_map);
+      if (!kSparse) {
+        tma_prefetch_desc(&kv_map);
+        tma_prefetch_desc(&kv_rope_map);
+      }
       uint32_t g = 0;
       int qi = 0;
       bool ok = true;
       for (int i = 0; i < n_pieces && ok; ++i) {
         const Piece pc = get_piece(p, meta, i, kSparse);
         if (pc.tok_end <= pc.tok0) continue;
-        if (rank == 1) {  // rope part of Q -> shared memory
-          ok = mbar_wait(smem_u32(&bars->q_empty), (qi & 1) ^ 1, abort_flag, p.status,
-                         kDevTimeoutProducer);
-          if (!ok) break;
-          mbar_arrive_expect_tx(smem_u32(&bars->q_full), kRopeBytes);
-          tma_load_3d(rope_base, &q_map, smem_u32(&bars->q_full), 512, row0, pc.b);
-        }
+        // rope part of Q -> shared memory
+        ok = mbar_wait(smem_u32(&bars->q_empty), (qi & 1) ^ 1, abort_flag, p.status,
+                       kDevTimeoutProducer);
+        if (!ok) break;
+        mbar_arrive_expect_tx(smem_u32(&bars->q_full), kQRopeBytes);
+        tma_load_3d(rope_base, &q_rope_map, smem_u32(&bars->q_full), rope0, row0, pc.b);
         ++qi;
         if (kSparse) {
           g += (pc.tok_end - pc.tok0 + kBN - 1) / kBN;
@@ -288,17 +295,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (!ok) break;
           const uint32_t full = smem_u32(&bars->kv_full[st]);
           FA_TRACE_EV(0, g);
-          mbar_arrive_expect_tx(full, n_chunks * kChunkBytes);
+          mbar_arrive_expect_tx(full, kStageBytes);
           const uint32_t dst = kv_base + st * kStageBytes;
-          for (int c = 0; c < n_chunks; ++c)
+          for (int c = 0; c < kLatentChunks; ++c)
             tma_load_3d(dst + c * kChunkBytes, &kv_map, full, dim0 + 64 * c, c1, c2);
+          tma_load_3d(dst + kLatentChunks * kChunkBytes, &kv_rope_map, full, rope0, c1, c2);
         }
       }
       // Drain: copies still in flight must land before the CTA may exit.
       if (*abort_flag) {
         volatile int never = 0;
-        if (rank == 1 && qi > 0)
-          mbar_wait(smem_u32(&bars->q_full), (qi - 1) & 1, &never, nullptr, 0);
+        if (qi > 0) mbar_wait(smem_u32(&bars->q_full), (qi - 1) & 1, &never, nullptr, 0);
         for (uint32_t t = g > kStages ? g - kStages : 0; t < g; ++t)
           mbar_wait(smem_u32(&bars->kv_full[t % kStages]), (t / kStages) & 1, &never, nullptr, 0);
       }
@@ -316,7 +323,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       cp.start(p, meta, n_pieces, kSparse);
       long long t_last = 0;
       uint32_t idle = 0;
-#ifdef FA_TRACE
+#ifdef FA_TRACE_MMA
       uint32_t dbg_n = 0;
 #endif
       while (cp.valid) {
@@ -325,20 +332,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t t = cp.g;
           const int st = t % kStages;
           const bool first = cp.tok == cp.tok0;
-          if (mbar_probe(smem_u32(&bars->p_full), t & 1) &&
+          const uint32_t ps = t & 1u;  // P slot in TMEM
+          if (mbar_probe(smem_u32(&bars->p_full[ps]), (t >> 1) & 1) &&
               (!first || mbar_probe(smem_u32(&bars->o_empty), (cp.qi & 1) ^ 1))) {
             tc_fence_after();
             FA_TRACE_EV(2, t);
             const uint32_t vb = kv_base + st * kStageBytes;
 #pragma unroll
             for (int kk = 0; kk < kBN / 16; ++kk) {
-              const uint64_t adesc = smem_desc_sw128(p_base + kk * 32, 16, 1024);
               const uint64_t bdesc = smem_desc_sw128(vb + kk * 16 * kChunkBytesRow, kChunkBytes, 1024);
-              umma_ss(tmem + kColO, adesc, bdesc, idesc_pv, (first && kk == 0) ? 0u : 1u);
+              umma_ts(tmem + kColO, tmem + kColP + ps * (kBN / 2) + kk * 8, bdesc, idesc_pv,
+                      (first && kk == 0) ? 0u : 1u);
             }
             tc_commit(smem_u32(&bars->kv_empty[st]));
-            tc_commit(smem_u32(&bars->pv_done));
-#ifdef FA_TRACE
+            tc_commit(smem_u32(&bars->pv_done[ps]));
+#ifdef FA_TRACE_MMA
             {  // debug: wait for this tile's PV to finish
               volatile int never = 0;
               tc_commit(smem_u32(&bars->dbg));
@@ -354,35 +362,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (cq.valid) {
           const uint32_t g = cq.g;
           const int st = g % kStages;
-          const uint32_t sb = g & 1u;
           const bool first = cq.tok == cq.tok0;
           if ((!first || mbar_probe(smem_u32(&bars->q_full), cq.qi & 1)) &&
               mbar_probe(smem_u32(&bars->kv_full[st]), (g / kStages) & 1) &&
-              mbar_probe(smem_u32(&bars->s_empty[sb]), ((g >> 1) & 1) ^ 1)) {
+              mbar_probe(smem_u32(&bars->s_empty), (g & 1) ^ 1)) {
             if (kSparse) fence_proxy_async_smem();  // cp.async rows -> tensor-core reads
             tc_fence_after();
             FA_TRACE_EV(1, g);
             const uint32_t kb = kv_base + st * kStageBytes;
-            const uint32_t sd = tmem + kColS + sb * kBN;
+            const uint32_t sd = tmem + kColS;
 #pragma unroll
-            for (int c = 0; c < kLatentHalf / 64; ++c) {
+            for (int c = 0; c < kLatentChunks; ++c) {
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk) {
                 const uint64_t bdesc = smem_desc_sw128(kb + c * kChunkBytes + kk * 32, 16, 1024);
                 umma_ts(sd, tmem + kColQ + (c * 4 + kk) * 8, bdesc, idesc_qk, (c | kk) ? 1u : 0u);
               }
             }
-            if (rank == 1) {
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t adesc = smem_desc_sw128(rope_base + kk * 32, 16, 1024);
-                const uint64_t bdesc = smem_desc_sw128(kb + 4 * kChunkBytes + kk * 32, 16, 1024);
-                umma_ss(sd, adesc, bdesc, idesc_qk, 1u);
-              }
+            for (int kk = 0; kk < kRopeDims / 16; ++kk) {
+              const uint64_t adesc = smem_desc_sw64(rope_base + kk * 32, 16, 512);
+              const uint64_t bdesc = smem_desc_sw64(kb + kLatentChunks * kChunkBytes + kk * 32, 16, 512);
+              umma_ss(sd, adesc, bdesc, idesc_qk, 1u);
             }
-            tc_commit(smem_u32(&bars->s_full[sb]));
+            tc_commit(smem_u32(&bars->s_full));
             if (cq.tok + kBN >= cq.tok_end) tc_commit(smem_u32(&bars->q_empty));
-#ifdef FA_TRACE
+#ifdef FA_TRACE_MMA
             {  // debug: wait for this tile's QK to finish
               volatile int never = 0;
               tc_commit(smem_u32(&bars->dbg));
@@ -398,7 +403,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (did) {
           idle = 0;
           t_last = 0;
-        } else if ((++idle & 63u) == 0) {
+          continue;
+        }
+        // nothing ready: back off briefly so the polling does not take issue
+        // slots from the softmax warps that share this SM sub-partition
+        __nanosleep(32);
+        if ((++idle & 63u) == 0) {
           if (*abort_flag) break;
           const long long now = clock64();
           if (t_last == 0) {
@@ -433,22 +443,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                          p.status, kDevTimeoutProducer);
           if (!ok) break;
           const uint32_t dst = kv_base + st * kStageBytes;
-          const int units = n_chunks * 8;  // 16-byte units per row
+          // 16-byte units per key row: 4 latent chunks x 8 (128-byte swizzle
+          // rows) then 4 rope units (64-byte swizzle rows)
+          constexpr int units = kLatentChunks * 8 + kRopeRowBytes / 16;
           for (int k = gt; k < kBN * units; k += 64) {
             const int r = k / units;
             const int rem = k - r * units;
-            const int c = rem >> 3, w = rem & 7;
             const int pos = tok + r;
             int64_t row = -1;
             if (pos < pc.tok_end) row = idx[pos];
             const bool valid = row >= 0 && row < p.total_rows;
+            int dim;
+            uint32_t off_s;
+            if (rem < kLatentChunks * 8) {
+              const int c = rem >> 3, w = rem & 7;
+              dim = dim0 + c * 64 + w * 8;
+              off_s = c * kChunkBytes + r * kChunkBytesRow + ((w ^ (r & 7)) << 4);
+            } else {
+              const int w = rem - kLatentChunks * 8;
+              dim = rope0 + w * 8;
+              off_s = kLatentChunks * kChunkBytes + r * kRopeRowBytes + ((w ^ ((r >> 1) & 3)) << 4);
+            }
             const uint8_t *src = p.kcache;
             if (valid) {
               const int64_t pg = row / p.page_size, off = row % p.page_size;
-              src += (pg * p.kv_sp + off * p.kv_st + dim0 + c * 64 + w * 8) * 2;
+              src += (pg * p.kv_sp + off * p.kv_st + dim) * 2;
             }
-            cp_async_16(dst + c * kChunkBytes + r * kChunkBytesRow + ((w ^ (r & 7)) << 4), src,
-                        valid ? 16u : 0u);
+            cp_async_16(dst + off_s, src, valid ? 16u : 0u);
           }
           cp_async_arrive(smem_u32(&bars->kv_full[st]));
         }
@@ -546,11 +567,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int s_tok = kSparse ? mb : (row_ok ? flat / p.h_q : 0);
     const int h = kSparse ? t : (row_ok ? flat % p.h_q : 0);
     const int out_flat = s_tok * p.h_q + h;
+    // Two exchange slots: tile gx travels through slot gx & 1.  A slot is
+    // rewritten (tile gx + 2) only after the peer has received tile gx + 1
+    // from this CTA, which this CTA sends after it has read tile gx from the
+    // slot -- so the slots need no "free" handshake.
     const uint32_t x_remote = map_to_rank(x_base, peer);
-    const uint32_t xf_local = smem_u32(&bars->x_full);
-    const uint32_t xf_remote = map_to_rank(xf_local, peer);
-    const uint32_t xfree_remote = map_to_rank(smem_u32(&bars->x_free), peer);
-    const float4 *xr = reinterpret_cast<const float4 *>(smem + kOffX);
+    const uint32_t xf_local[2] = {smem_u32(&bars->x_full[0]), smem_u32(&bars->x_full[1])};
+    const uint32_t xf_remote[2] = {map_to_rank(xf_local[0], peer), map_to_rank(xf_local[1], peer)};
     bool ok = true;
 
     // ---- score exchange, tile gx: own partial -> peer; peer's partial + own
@@ -559,46 +582,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     float so[kBN / 2];  // own partial scores of tile cx.g (in flight)
     float sc[kBN / 2];  // full scores of the tile being processed
     auto x_begin = [&]() -> bool {
-      const uint32_t gx = cx.g, sb = gx & 1u;
+      const uint32_t gx = cx.g, xs = gx & 1u;
       if (t == 0 && ch == 0) FA_TRACE_EV(14, gx);
-      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->s_full[sb]), (gx >> 1) & 1,
-                                             abort_flag, p.status, kDevTimeoutSoftmax)))
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->s_full), gx & 1, abort_flag,
+                                             p.status, kDevTimeoutSoftmax)))
         return false;
       if (t == 0 && ch == 0) FA_TRACE_EV(3, gx);
       tc_fence_after();
       {
         float v[16];
-        tmem_ld16(trow + kColS + sb * kBN + c0, v);
+        tmem_ld16(trow + kColS + c0, v);
 #pragma unroll
         for (int j = 0; j < 16; ++j) so[j] = v[j];
-        tmem_ld16(trow + kColS + sb * kBN + c0 + 16, v);
+        tmem_ld16(trow + kColS + c0 + 16, v);
 #pragma unroll
         for (int j = 0; j < 16; ++j) so[16 + j] = v[j];
       }
       tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(smem_u32(&bars->s_empty[sb]));
-      // the peer's buffer must have been drained of tile gx-1
-      if (!__all_sync(0xffffffffu, mbar_wait<true>(smem_u32(&bars->x_free), (gx & 1) ^ 1,
-                                                   abort_flag, p.status, kDevTimeoutExchange)))
-        return false;
+      mbar_arrive(smem_u32(&bars->s_empty));
       if (t == 0 && ch == 0) {
         FA_TRACE_EV(4, gx);
-        mbar_arrive_expect_tx(xf_local, kXBytes);
+        mbar_arrive_expect_tx(xf_local[xs], kXBytes);
       }
+      const uint32_t dst = x_remote + xs * kXBytes;
 #pragma unroll
       for (int c = 0; c < kBN / 8; ++c)
-        st_async_v4(x_remote + ((ch * (kBN / 8) + c) * kRows + t) * 16, so[4 * c], so[4 * c + 1],
-                    so[4 * c + 2], so[4 * c + 3], xf_remote);
+        st_async_v4(dst + ((ch * (kBN / 8) + c) * kRows + t) * 16, so[4 * c], so[4 * c + 1],
+                    so[4 * c + 2], so[4 * c + 3], xf_remote[xs]);
       if (t == 0 && ch == 0) FA_TRACE_EV(5, gx);
       return true;
     };
     auto x_end = [&]() -> bool {
-      const uint32_t gx = cx.g;
-      if (!__all_sync(0xffffffffu, mbar_wait<true>(xf_local, gx & 1, abort_flag, p.status,
-                                                   kDevTimeoutExchange)))
+      const uint32_t gx = cx.g, xs = gx & 1u;
+      if (!__all_sync(0xffffffffu, mbar_wait<true>(xf_local[xs], (gx >> 1) & 1, abort_flag,
+                                                   p.status, kDevTimeoutExchange)))
         return false;
       if (t == 0 && ch == 0) FA_TRACE_EV(6, gx);
+      const float4 *xr = reinterpret_cast<const float4 *>(smem + kOffX + xs * kXBytes);
 #pragma unroll
       for (int c = 0; c < kBN / 8; ++c) {
         const float4 o = xr[(ch * (kBN / 8) + c) * kRows + t];
@@ -607,10 +628,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         sc[4 * c + 2] = so[4 * c + 2] + o.z;
         sc[4 * c + 3] = so[4 * c + 3] + o.w;
       }
-      // the loads above have returned (their values are summed), so the
-      // buffer may be refilled: no release ordering is needed for the signal
-      __syncwarp();
-      if (lane == 0) mbar_arrive_remote_relaxed(xfree_remote);
       if (t == 0 && ch == 0) FA_TRACE_EV(15, gx);
       cx.advance(p, meta, n_pieces, kSparse);
       return true;
@@ -681,13 +698,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         l_half = l_half * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
         if (t == 0 && ch == 0) FA_TRACE_EV(7, g);
-        // the P buffer is free once PV of tile g-1 has finished (which also
-        // makes O safe to rescale)
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done), (g & 1) ^ 1, abort_flag,
-                                               p.status, kDevTimeoutSoftmax));
+        // P slot g & 1 is free once PV of tile g-2 has finished
+        const uint32_t ps_slot = g & 1u;
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done[ps_slot]),
+                                               ((g >> 1) & 1) ^ 1, abort_flag, p.status,
+                                               kDevTimeoutSoftmax));
         if (!ok) break;
         if (t == 0 && ch == 0) FA_TRACE_EV(8, g);
         if (__any_sync(0xffffffffu, rescale)) {
+          // O may be rescaled once PV of tile g-1 (its last update) has finished
+          const uint32_t pt = g - 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done[pt & 1u]),
+                                                 (pt >> 1) & 1, abort_flag, p.status,
+                                                 kDevTimeoutSoftmax));
+          if (!ok) break;
           tc_fence_after();
           const float a = rescale ? alpha : 1.f;
 #pragma unroll 1
@@ -703,17 +727,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           tmem_wait_st();
         }
-        // P row t, columns c0.. -> UMMA K-major SW128: 16-byte unit u at u ^ (t & 7)
-        {
-          uint8_t *prow = smem + kOffP + t * kChunkBytesRow;
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int unit = ch * 4 + u;
-            *reinterpret_cast<uint4 *>(prow + ((unit ^ (t & 7)) << 4)) =
-                make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-          }
-        }
-        if (!kSparse && pc.tok_end - tok < kBN) {
+        // P row t, columns c0.. -> TMEM P slot as bf16/f16 pairs (PV's A operand)
+        tmem_st16(trow + kColP + ps_slot * (kBN / 2) + ch * (kBN / 4), pk);
+        const bool tail = !kSparse && pc.tok_end - tok < kBN;
+        if (tail) {
           // rows past the sequence end may hold any bits (even NaN); P is 0
           // there but 0 * NaN is not, so clear them before the PV product.
           const int kv_valid = pc.tok_end - tok;
@@ -725,11 +742,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             *reinterpret_cast<uint4 *>(stage + (rem >> 3) * kChunkBytes + r * kChunkBytesRow +
                                        (rem & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
           }
+          fence_proxy_async_smem();
         }
-        fence_proxy_async_smem();
+        tmem_wait_st();
         tc_fence_before();
         if (t == 0 && ch == 0) FA_TRACE_EV(9, g);
-        mbar_arrive(smem_u32(&bars->p_full));
+        mbar_arrive(smem_u32(&bars->p_full[ps_slot]));
         if (more && !(ok = x_end())) break;
       }
       if (!ok) break;
@@ -750,8 +768,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const float lse = l_run > 0.f ? ms * 0.69314718055994531f + logf(l_run) : -INFINITY;
       if (has_tiles) {
         const uint32_t lt = g - 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done), lt & 1, abort_flag,
-                                               p.status, kDevTimeoutSoftmax));
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done[lt & 1u]), (lt >> 1) & 1,
+                                               abort_flag, p.status, kDevTimeoutSoftmax));
         if (!ok) break;
         tc_fence_after();
       }
@@ -814,6 +832,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // -------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) FA_TRACE_EV(11, 1);
   cluster_sync();  // the peer no longer touches this CTA's shared memory
   if (warp == 1) {
     tc_fence_after();
@@ -822,18 +841,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 template <typename T, bool kSparse>
-static cudaError_t launch_mla_t(const CUtensorMap &qm, const CUtensorMap &km, const MlaParams &p,
-                                int num_parts, int m_blocks, cudaStream_t stream) {
+static cudaError_t launch_mla_t(const CUtensorMap &qrm, const CUtensorMap &km, const CUtensorMap &krm,
+                                const MlaParams &p, int num_parts, int m_blocks, cudaStream_t stream) {
   auto kern = mla_decode_tc_kernel<T, kSparse>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
   dim3 grid(2 * num_parts, m_blocks);
-  kern<<<grid, kThreads, kSmemBytes, stream>>>(qm, km, p);
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(qrm, km, krm, p);
   return cudaGetLastError();
 }
 
-cudaError_t launch_mla_tc(const CUtensorMap &qm, const CUtensorMap &km, const fa_mla_args *a,
-                          int m_blocks, int64_t total_rows, cudaStream_t stream) {
+// qrm: query rope map (box 32 dims x 128 rows, 64-byte swizzle); km / krm:
+// key latent map (box 64 x 64, 128-byte swizzle) and key rope map (box 32 x
+// 64, 64-byte swizzle) over the same cache.
+cudaError_t launch_mla_tc(const CUtensorMap &qrm, const CUtensorMap &km, const CUtensorMap &krm,
+                          const fa_mla_args *a, int m_blocks, int64_t total_rows,
+                          cudaStream_t stream) {
   MlaParams p;
   p.q = static_cast<const uint16_t *>(a->q);
   p.q_sb = a->q_stride_b;
@@ -873,11 +896,11 @@ cudaError_t launch_mla_tc(const CUtensorMap &qm, const CUtensorMap &km, const fa
   const bool sparse = a->indices != nullptr;
   const bool f16 = a->dtype == FA_DTYPE_F16;
   if (f16) {
-    if (sparse) return launch_mla_t<__half, true>(qm, km, p, a->num_sm_parts, m_blocks, stream);
-    return launch_mla_t<__half, false>(qm, km, p, a->num_sm_parts, m_blocks, stream);
+    if (sparse) return launch_mla_t<__half, true>(qrm, km, krm, p, a->num_sm_parts, m_blocks, stream);
+    return launch_mla_t<__half, false>(qrm, km, krm, p, a->num_sm_parts, m_blocks, stream);
   }
-  if (sparse) return launch_mla_t<__nv_bfloat16, true>(qm, km, p, a->num_sm_parts, m_blocks, stream);
-  return launch_mla_t<__nv_bfloat16, false>(qm, km, p, a->num_sm_parts, m_blocks, stream);
+  if (sparse) return launch_mla_t<__nv_bfloat16, true>(qrm, km, krm, p, a->num_sm_parts, m_blocks, stream);
+  return launch_mla_t<__nv_bfloat16, false>(qrm, km, krm, p, a->num_sm_parts, m_blocks, stream);
 }
 
 #ifdef FA_TRACE

@@ -128,7 +128,8 @@ int fa_split_kv_attention(const fa_decode_args *args, void *stream);
 /* Merge `num_parts` partial results by log-sum-exp:
  *   lse = log(sum_s exp(lse_s)),  o = sum_s exp(lse_s - lse) * o_s
  * part_o: f32 [num_parts][rows][d_v] (row stride d_v), part_lse: f32
- * [num_parts][rows]; o: dtype [rows][d_v]; lse (nullable): f32 [rows]. */
+ * [num_parts][rows]; o: dtype [rows][d_v]; lse (nullable): f32 [rows].
+ * d_v must be a multiple of 4 and at most 512. */
 int fa_lse_combine(const float *part_o, const float *part_lse, int num_parts,
                    int64_t rows, int d_v, void *o, int dtype, float *lse,
                    void *stream);

@@ -77,5 +77,9 @@ def test_invalid_arguments_are_rejected_on_host():
     assert lib.fa_paged_attention(ctypes.byref(d), None) == _lib.FA_ERR_INVALID_ARGUMENT
     assert lib.fa_lse_combine(None, None, 0, 0, 0, None, 0, None, None) == \
         _lib.FA_ERR_INVALID_ARGUMENT
+    # value widths above 512 are refused before anything is launched
+    fake = ctypes.c_void_p(1 << 20)
+    assert lib.fa_lse_combine(fake, fake, 2, 4, 516, fake, 0, None, None) == \
+        _lib.FA_ERR_UNSUPPORTED
     with pytest.raises(_lib.InvalidArgument):
         _lib.check(_lib.FA_ERR_INVALID_ARGUMENT, "x")
