@@ -83,21 +83,63 @@ def profiled_traffic():
 
 # ----------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons of one GPU, sampled during the timed
+    region.  NVML (read-only queries) from a background thread every 2 ms,
+    so even a timed region of a few tens of milliseconds gets samples;
+    nvidia-smi is the fallback when NVML is missing."""
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, bus_id):
-        self.proc = None
-        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.sm, self.reasons, self.max_mhz = [], set(), None
+        self.proc = self.thread = None
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", bus_id], stdout=self.tmp, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            import threading
+
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus_id)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.stop_evt = threading.Event()
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.thread = None
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", "100", "-i", bus_id], stdout=self.tmp, stderr=subprocess.DEVNULL)
+            except OSError:
+                self.proc = None
+
+    def _poll(self):
+        nv = self.nvml
+        while not self.stop_evt.is_set():
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                for name, const in self.REASONS:
+                    if mask & getattr(nv, const, 0):
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self.stop_evt.wait(0.002)
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_evt.set()
+            self.thread.join(timeout=5)
+            return {"sm_mhz": statistics.median(self.sm) if self.sm else None,
+                    "sm_max_mhz": float(self.max_mhz) if self.max_mhz else None,
+                    "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -107,16 +149,15 @@ class ClockSampler:
         os.unlink(self.tmp.name)
         sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = set()
         for r in rows:
             if len(r) >= 9:
-                for name, val in zip(names, r[5:9]):
+                for (name, _), val in zip(self.REASONS, r[5:9]):
                     if val.strip() == "Active":
                         reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ---------------------------------------------------------------- our arm
