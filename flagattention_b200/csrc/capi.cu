@@ -25,6 +25,8 @@ cudaError_t launch_generic_decode(const fa_decode_args *, cudaStream_t);
 size_t generic_smem_bytes(int, int);
 cudaError_t launch_mla_tc(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                           const fa_mla_args *, int, int64_t, cudaStream_t);
+cudaError_t launch_mla_sv(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
+                          const fa_mla_args *, int, cudaStream_t);
 }  // namespace fa
 
 namespace {
@@ -353,13 +355,29 @@ int fa_mla_decode_partial(const fa_mla_args *a, void *stream) {
   const bool sparse = a->indices != nullptr;
   const int bn = FA_MLA_BLOCK_N;
   const int m_blocks = mla_m_blocks(a->s_q, a->h_q, sparse);
+  const bool paged = a->block_table != nullptr;
+  const uint64_t kv_rows = (sparse || paged) ? a->page_size : (a->n_ctx > 0 ? a->n_ctx : 1);
+  const uint64_t kv_groups = (sparse || paged) ? a->num_pages : a->batch;
+  if (!sparse) {
+    // dense: score / value CTA kernel (query box 64 dims x 128 rows, key
+    // rows in 64-row boxes, value rows in 32-row boxes)
+    CUtensorMap qm, km, vm;
+    st = encode_map(&qm, a->q, a->dtype, 576, static_cast<uint64_t>(a->s_q) * a->h_q, a->batch,
+                    a->q_stride_h, a->q_stride_b, 128, 64);
+    if (st != FA_OK) return st;
+    st = encode_map(&km, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
+                    a->kv_stride_page, bn, 64);
+    if (st != FA_OK) return st;
+    st = encode_map(&vm, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
+                    a->kv_stride_page, 32, 64);
+    if (st != FA_OK) return st;
+    cudaError_t e = fa::launch_mla_sv(qm, km, vm, a, m_blocks, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? FA_OK : cuda_fail(e, "MLA decode launch");
+  }
   CUtensorMap qrm, km, krm;
   st = encode_map(&qrm, a->q, a->dtype, 576, static_cast<uint64_t>(a->s_q) * a->h_q, a->batch,
                   a->q_stride_h, a->q_stride_b, 128, 32);
   if (st != FA_OK) return st;
-  const bool paged = a->block_table != nullptr;
-  const uint64_t kv_rows = (sparse || paged) ? a->page_size : (a->n_ctx > 0 ? a->n_ctx : 1);
-  const uint64_t kv_groups = (sparse || paged) ? a->num_pages : a->batch;
   st = encode_map(&km, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
                   a->kv_stride_page, bn, 64);
   if (st != FA_OK) return st;

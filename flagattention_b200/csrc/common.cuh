@@ -185,6 +185,22 @@ __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float a, floa
       : "memory");
 }
 
+__device__ __forceinline__ void st_async_v4_u32(uint32_t cluster_addr, uint32_t a, uint32_t b,
+                                                uint32_t c, uint32_t d, uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::
+          "r"(cluster_addr),
+      "r"(a), "r"(b), "r"(c), "r"(d), "r"(cluster_bar)
+      : "memory");
+}
+__device__ __forceinline__ void st_async_u32(uint32_t cluster_addr, uint32_t a,
+                                             uint32_t cluster_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+                   cluster_addr),
+               "r"(a), "r"(cluster_bar)
+               : "memory");
+}
+
 // --------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
                                             int c0, int c1, int c2) {
@@ -234,6 +250,15 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
                    bar)
                : "memory");
 }
+// Arrive once on the mbarrier at the same shared-memory offset in every CTA
+// of `cta_mask` (cluster ranks) when all tcgen05.mma issued so far end.
+__device__ __forceinline__ void tc_commit_mc(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
 // D(tmem) (+)= A(smem desc) * B(smem desc)^T
 __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                         uint32_t idesc, uint32_t accumulate) {
@@ -252,6 +277,60 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Warp-wide forms: every lane of the warp executes the call with the same
+// (warp-uniform) operands and one lane, chosen by elect.sync, issues the
+// instruction.  Keeping the issuing loop on the whole warp lets the compiler
+// hold descriptors and TMEM addresses in uniform registers; a loop run by one
+// thread pays a register move per MMA.
+__device__ __forceinline__ void umma_ss_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Copy a 128-row x 256-bit tile (one K-step of 16 bf16/f16 per row) from
+// shared memory, described like an MMA operand, into TMEM lanes 0..127 at
+// column taddr .. taddr+7.  Executes in order with the issuing thread's MMAs.
+__device__ __forceinline__ void tmem_cp_128x256b_warp(uint32_t taddr, uint64_t s_desc) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.cp.cta_group::1.128x256b [%0], %1;\n\t}" ::"r"(taddr),
+      "l"(s_desc)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_warp(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          bar)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_mc_warp(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;\n\t}" ::"r"(bar),
+      "h"(cta_mask)
       : "memory");
 }
 

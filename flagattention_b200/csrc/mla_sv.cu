@@ -1,0 +1,938 @@
+// mla_sv.cu -- dense MLA decode on tcgen05 with a score CTA and a value CTA.
+//
+// Problem: 128 query rows (query tokens x heads) share one latent key head of
+// 576 dims; values are the first 512 dims of the same rows.  The reference
+// computes it per page with tl.dot (paged.py:296-336): S = Q K^T, online
+// softmax, O += P V.
+//
+// The f32 accumulator O[128 x 512] alone fills one SM's 512 TMEM columns, so
+// a work unit runs on a 2-CTA cluster with a functional split:
+//   rank 0, the score CTA: latent Q (512 dims) in TMEM as the A operand, two
+//     128-column score buffers, S = Q K^T for 128-token tiles (N = 128), the
+//     online softmax, and P sent as bf16/f16 into the value CTA's shared
+//     memory with st.async (16 KB per 64 tokens, one direction);
+//   rank 1, the value CTA: O in all 512 TMEM columns, O += P V with P and V
+//     from shared memory.
+// Both CTAs read the key rows they need with their own TMA: the value CTA's
+// 512 dims of a row are an L2 hit after the score CTA's 576 (or the other way
+// round), so HBM sees each row about once.  Nothing travels back from the
+// value CTA except "slot free" arrivals (tcgen05.commit multicast).
+//
+// Score CTA (512 threads): warp 0 TMA producer (latent Q chunks and key
+// chunks through one 11-slot ring of 16 KB = 128 rows x 64 dims, rope Q in
+// two 16 KB buffers), warp 1 MMA issuer (also copies the latent Q chunks from
+// the ring into TMEM with tcgen05.cp), warps 4-11 softmax (two warps per 32
+// query rows, one per 64-token block of the tile).
+// Value CTA (512 threads): warp 0 TMA producer (V in 32-token stages of
+// 8 x 4 KB), warp 1 MMA issuer, warps 4-11 O rescaling, tail clearing and the
+// epilogue (two warps per 32 rows, one per 256 output dims; stores staged
+// through shared memory so that each store instruction writes whole rows).
+// Every mbarrier wait is bounded (common.cuh); a timeout sets the device
+// status word and the kernel unwinds instead of hanging.
+#include "common.cuh"
+#include "flagattn_b200.h"
+
+namespace fa {
+namespace sv {
+
+constexpr int kRows = 128;
+constexpr int kBlk = FA_MLA_BLOCK_N;                 // 64 tokens: scheduler block, one page box
+constexpr int kThreads = 512;
+constexpr int kRowBytes = 128;                      // 64 dims x 2 bytes (one 128-byte swizzle row)
+constexpr int kBoxBytes = kBlk * kRowBytes;         // 8 KB
+constexpr int kChunkBytes = 2 * kBoxBytes;          // 16 KB: 128 rows x 64 dims
+constexpr int kQChunks = 8;                         // latent Q, 512 dims
+constexpr int kKChunks = 9;                         // key: 512 latent + 64 rope dims
+constexpr int kRing = 11;
+constexpr int kVRows = 32;                          // tokens per V stage
+constexpr int kVChunkBytes = kVRows * kRowBytes;    // 4 KB: 32 rows x 64 dims
+constexpr int kVStageBytes = 8 * kVChunkBytes;      // 32 KB: 512 dims
+constexpr int kVStages = 4;
+constexpr int kPBytes = kRows * kRowBytes;          // 16 KB: P of one 64-token block
+constexpr int kMetaAlpha = kPBytes;                 // f32[128] O rescale factors
+constexpr int kMetaFlags = kPBytes + 512;           // int[4] "rows of quadrant q rescale"
+constexpr int kMetaInvL = kPBytes + 1024;           // f32[128] 1 / row sum (last block)
+constexpr int kPSlotBytes = kPBytes + 2048;         // 18 KB
+constexpr int kPSlots = 3;
+constexpr uint32_t kColQ = 0, kColS = 256, kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;           // log2 units (factor 256)
+
+constexpr int kOffBar = 0;
+constexpr int kOffData = 1024;
+// score CTA
+constexpr int kOffQRope = kOffData;                         // 2 x 16 KB
+constexpr int kOffRing = kOffQRope + 2 * kChunkBytes;       // 11 x 16 KB
+constexpr int kOffRed = kOffRing + kRing * kChunkBytes;     // 2 KB row maxima / sums
+constexpr int kSmemScore = kOffRed + 2048;
+// value CTA
+constexpr int kOffV = kOffData;                             // 4 x 32 KB
+constexpr int kOffP = kOffV + kVStages * kVStageBytes;      // 3 x 18 KB
+constexpr int kStageWarpBytes = 32 * 128;                   // epilogue staging per warp
+constexpr int kOffStage = kOffP + kPSlots * kPSlotBytes;    // 8 x 4 KB
+constexpr int kSmemValue = kOffStage + 8 * kStageWarpBytes;
+constexpr int kSmemUsed = kSmemScore > kSmemValue ? kSmemScore : kSmemValue;
+constexpr int kSmemBytes = kSmemUsed + 1024;                // + base alignment slack
+static_assert(kSmemBytes <= 232448, "shared memory plan exceeds 227 KB");
+static_assert(kOffRing % 1024 == 0 && kOffQRope % 1024 == 0 && kOffV % 1024 == 0 &&
+                  kOffP % 1024 == 0 && kPSlotBytes % 1024 == 0,
+              "swizzled operands need 1024-byte alignment");
+
+// One block of barriers at the same offset in both CTAs, so a barrier of the
+// peer is addressed by mapping the local offset (mapa / commit multicast).
+struct Bars {
+  // score CTA
+  uint64_t rope_full[2], rope_empty[2];
+  uint64_t ch_full[kRing], ch_empty[kRing];
+  uint64_t s_full[2], s_empty[2];
+  uint64_t pair[4];
+  uint64_t p_free[kPSlots];  // arrived by the value CTA's PV commit
+  // value CTA
+  uint64_t v_full[kVStages], v_empty[kVStages];
+  uint64_t p_full[kPSlots];  // the score CTA's st.async complete here
+  uint64_t m_read[kPSlots];  // epilogue warps are done with the slot's metadata
+  uint64_t pv_done[kPSlots];
+  uint64_t o_empty;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Bars) <= kOffData, "barrier block");
+
+#ifdef FA_TRACE
+// Debug builds only: SM-clock timestamps of pipeline events of two parts
+// (index: tile for score-CTA events, 64-token block for value-CTA events).
+__device__ long long g_sv_trace[2][2][128][16];
+#define SV_TRACE(ev, idx)                                                             \
+  do {                                                                               \
+    const int tp_ = (part == 0 && mb == 0) ? 0 : ((part == 37 && mb == 0) ? 1 : -1); \
+    if (tp_ >= 0 && (idx) < 128) g_sv_trace[tp_][rank][(idx)][(ev)] = clock64();     \
+  } while (0)
+__device__ long long g_sv_epi[2][8][4];
+#define EPI_TRACE(ev)                                                                  \
+  do {                                                                                 \
+    if (part == 0 && mb == 0 && tt == 0 && i < 2 && c0 / cols_it < 8)                  \
+      g_sv_epi[i][c0 / cols_it][(ev)] = clock64();                                     \
+  } while (0)
+#else
+#define EPI_TRACE(ev) \
+  do {                \
+  } while (0)
+#define SV_TRACE(ev, idx) \
+  do {                    \
+  } while (0)
+#endif
+
+struct Params {
+  const int32_t *block_table;
+  int64_t bt_stride;
+  const int32_t *seq_lens;
+  int32_t n_ctx;
+  int32_t page_size;
+  const int32_t *tile_meta;
+  const int32_t *num_splits;
+  void *out;
+  int64_t o_sb, o_ss, o_sh;
+  float *lse;
+  float *part_o;
+  float *part_lse;
+  int32_t batch, s_q, h_q, d_v;
+  int32_t causal, paged, out_f32;
+  float scale_log2;
+  int32_t *status;
+};
+
+struct Piece {
+  int b, tok0, tok_end, split_idx;
+};
+
+__device__ __forceinline__ int seq_len(const Params &p, int b) {
+  return p.seq_lens ? p.seq_lens[b] : p.n_ctx;
+}
+
+// Piece i of a part (tile_meta row: begin batch, begin block, end batch, end
+// block, split index of the first piece, number of pieces).
+__device__ __forceinline__ Piece get_piece(const Params &p, const int32_t *meta, int i) {
+  Piece pc;
+  pc.b = meta[0] + i;
+  const int len = seq_len(p, pc.b);
+  const int nblk = len > 0 ? (len + kBlk - 1) / kBlk : 0;
+  const int lo = (i == 0) ? meta[1] : 0;
+  const int hi = (pc.b == meta[2]) ? meta[3] : nblk;
+  pc.tok0 = lo * kBlk;
+  pc.tok_end = min(hi * kBlk, max(len, 0));
+  pc.split_idx = (i == 0) ? meta[4] : 0;
+  return pc;
+}
+
+// TMA coordinates (row in page, page) of token t of sequence b.
+__device__ __forceinline__ void kv_coord(const Params &p, int b, int t, int &c1, int &c2) {
+  if (p.paged) {
+    c2 = p.block_table[static_cast<int64_t>(b) * p.bt_stride + t / p.page_size];
+    c1 = t % p.page_size;
+  } else {
+    c2 = b;
+    c1 = t;
+  }
+}
+
+// 32 lanes x 32 columns of 32-bit TMEM words.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    mla_decode_sv_kernel(const __grid_constant__ CUtensorMap q_map,
+                         const __grid_constant__ CUtensorMap kv_map,
+                         const __grid_constant__ CUtensorMap v_map, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  if (smem + kSmemUsed > smem_raw + kSmemBytes) {  // uniform over the cluster
+    if (threadIdx.x == 0 && p.status) atomicExch(p.status, kDevBadSmemAlign);
+    return;
+  }
+  Bars *bars = reinterpret_cast<Bars *>(smem + kOffBar);
+  const uint32_t s_base = smem_u32(smem);
+  volatile int *abort_flag = &bars->abort_flag;
+  const uint32_t rank = cluster_rank();
+  const int part = blockIdx.x >> 1;
+  const int mb = blockIdx.y;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int32_t *meta = p.tile_meta + static_cast<int64_t>(part) * FA_MLA_META_INTS;
+  const int n_pieces = meta[5];
+  const int rows_total = p.s_q * p.h_q;
+  const int row0 = mb * kRows;
+  const int n_rows = min(kRows, rows_total - row0);
+  constexpr int fmt = std::is_same<T, __half>::value ? 0 : 1;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&bars->rope_full[i]), 1);
+      mbar_init(smem_u32(&bars->rope_empty[i]), 1);
+      mbar_init(smem_u32(&bars->s_full[i]), 1);
+      mbar_init(smem_u32(&bars->s_empty[i]), 256);
+    }
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(smem_u32(&bars->ch_full[i]), 1);
+      mbar_init(smem_u32(&bars->ch_empty[i]), 1);
+    }
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&bars->pair[i]), 64);
+    for (int i = 0; i < kPSlots; ++i) {
+      mbar_init(smem_u32(&bars->p_free[i]), 1);
+      mbar_init(smem_u32(&bars->p_full[i]), 1);
+      mbar_init(smem_u32(&bars->m_read[i]), 256);
+      mbar_init(smem_u32(&bars->pv_done[i]), 1);
+    }
+    for (int i = 0; i < kVStages; ++i) {
+      mbar_init(smem_u32(&bars->v_full[i]), 1);
+      mbar_init(smem_u32(&bars->v_empty[i]), 1);
+    }
+    mbar_init(smem_u32(&bars->o_empty), 256);
+    mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&bars->tmem_base), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  cluster_sync();  // the peer's barriers exist before any remote access
+  if (threadIdx.x == 0) SV_TRACE(11, 127);
+#ifdef FA_TRACE
+  if (threadIdx.x == 0 && part == 0 && mb == 0) g_sv_trace[0][rank][126][0] = static_cast<long long>(global_ns());
+#endif
+
+  if (rank == 0) {
+    // ================================================================ score CTA
+    const uint32_t ring = s_base + kOffRing;
+    const uint32_t qrope = s_base + kOffQRope;
+    if (warp == 0) {
+      // ---------------------------------------------------------- producer
+      if (lane == 0) {
+        tma_prefetch_desc(&q_map);
+        tma_prefetch_desc(&kv_map);
+        uint32_t rc = 0, tg = 0;
+        int qi = 0;
+        bool ok = true;
+        for (int i = 0; i < n_pieces && ok; ++i) {
+          const Piece pc = get_piece(p, meta, i);
+          if (pc.tok_end <= pc.tok0) continue;
+          // latent Q: 8 chunks of 64 dims x 128 rows through the ring
+          for (int c = 0; c < kQChunks; ++c, ++rc) {
+            const int slot = rc % kRing;
+            ok = mbar_wait(smem_u32(&bars->ch_empty[slot]), ((rc / kRing) & 1) ^ 1, abort_flag,
+                           p.status, kDevTimeoutProducer);
+            if (!ok) break;
+            const uint32_t full = smem_u32(&bars->ch_full[slot]);
+            mbar_arrive_expect_tx(full, kChunkBytes);
+            tma_load_3d(ring + slot * kChunkBytes, &q_map, full, 64 * c, row0, pc.b);
+          }
+          if (!ok) break;
+          // rope Q (dims 512..575) -> buffer qi & 1
+          ok = mbar_wait(smem_u32(&bars->rope_empty[qi & 1]), ((qi >> 1) & 1) ^ 1, abort_flag,
+                         p.status, kDevTimeoutProducer);
+          if (!ok) break;
+          mbar_arrive_expect_tx(smem_u32(&bars->rope_full[qi & 1]), kChunkBytes);
+          tma_load_3d(qrope + (qi & 1) * kChunkBytes, &q_map, smem_u32(&bars->rope_full[qi & 1]),
+                      512, row0, pc.b);
+          ++qi;
+          for (int tok = pc.tok0; tok < pc.tok_end && ok; tok += 2 * kBlk, ++tg) {
+            const int n_blk = (pc.tok_end - tok > kBlk) ? 2 : 1;
+            int c1[2], c2[2];
+            for (int j = 0; j < n_blk; ++j) kv_coord(p, pc.b, tok + j * kBlk, c1[j], c2[j]);
+            for (int c = 0; c < kKChunks; ++c, ++rc) {
+              const int slot = rc % kRing;
+              ok = mbar_wait(smem_u32(&bars->ch_empty[slot]), ((rc / kRing) & 1) ^ 1, abort_flag,
+                             p.status, kDevTimeoutProducer);
+              if (!ok) break;
+              const uint32_t full = smem_u32(&bars->ch_full[slot]);
+              if (c == 0) SV_TRACE(0, tg);
+              if (c == kKChunks - 1) SV_TRACE(1, tg);
+              mbar_arrive_expect_tx(full, n_blk * kBoxBytes);
+              for (int j = 0; j < n_blk; ++j)
+                tma_load_3d(ring + slot * kChunkBytes + j * kBoxBytes, &kv_map, full, 64 * c,
+                            c1[j], c2[j]);
+            }
+          }
+        }
+        if (*abort_flag) {  // copies in flight must land before the CTA may exit
+          volatile int never = 0;
+          for (uint32_t t = rc > kRing ? rc - kRing : 0; t < rc; ++t)
+            mbar_wait(smem_u32(&bars->ch_full[t % kRing]), (t / kRing) & 1, &never, nullptr, 0);
+          if (qi > 0)
+            mbar_wait(smem_u32(&bars->rope_full[(qi - 1) & 1]), ((qi - 1) >> 1) & 1, &never,
+                      nullptr, 0);
+        }
+      }
+      __syncwarp();
+    } else if (warp == 1) {
+      // -------------------------------------------------------- MMA issuer
+      // The whole warp runs the loop (warp-uniform operands); one elected
+      // lane issues each MMA / commit.
+      // The instruction descriptor must be a compile-time constant: a runtime
+      // one costs about 40 extra cycles per MMA.  Full tiles (N = 128) and
+      // the half tile at a piece end (N = 64) get separate loops.
+      constexpr uint32_t kIdesc128 = umma_idesc_f16(128, 128, fmt, 0);
+      constexpr uint32_t kIdesc64 = umma_idesc_f16(128, 64, fmt, 0);
+      const uint64_t ring_desc = smem_desc_sw128(ring, 16, 1024);
+      const uint64_t rope_desc = smem_desc_sw128(qrope, 16, 1024);
+      auto wait = [&](uint32_t bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma));
+      };
+      uint32_t rc = 0, g = 0;
+      int qi = 0;
+      bool ok = true;
+#ifdef FA_TRACE
+      long long wait_acc = 0;
+#endif
+      // QK of one tile into S buffer sd: 8 latent chunks (A = Q from TMEM)
+      // and the rope chunk (A = rope Q from shared memory).
+      auto qk_tile = [&](auto idesc_tag, uint32_t sd, uint64_t rope_a) -> bool {
+        constexpr uint32_t idesc = decltype(idesc_tag)::value;
+        for (int c = 0; c < kKChunks; ++c, ++rc) {
+          const uint32_t slot = rc % kRing;
+#ifdef FA_TRACE
+          const long long w0_ = clock64();
+#endif
+          if (!wait(smem_u32(&bars->ch_full[slot]), (rc / kRing) & 1)) return false;
+#ifdef FA_TRACE
+          wait_acc += clock64() - w0_;
+#endif
+          tc_fence_after();
+          const uint64_t kdesc = ring_desc + static_cast<uint64_t>((slot * kChunkBytes) >> 4);
+          if (c < kQChunks) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_ts_warp(sd, tmem + kColQ + c * 32 + kk * 8, kdesc + 2 * kk, idesc,
+                           (c | kk) ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) umma_ss_warp(sd, rope_a + 2 * kk, kdesc + 2 * kk, idesc, 1u);
+          }
+          tc_commit_warp(smem_u32(&bars->ch_empty[slot]));
+        }
+        return true;
+      };
+      for (int i = 0; i < n_pieces && ok; ++i) {
+        const Piece pc = get_piece(p, meta, i);
+        if (pc.tok_end <= pc.tok0) continue;
+        // latent Q -> TMEM columns [0, 256): tcgen05.cp runs in order with
+        // this warp's MMAs, so it starts after the previous piece's last QK
+        for (int c = 0; c < kQChunks && ok; ++c, ++rc) {
+          const uint32_t slot = rc % kRing;
+          ok = wait(smem_u32(&bars->ch_full[slot]), (rc / kRing) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t qdesc = ring_desc + static_cast<uint64_t>((slot * kChunkBytes) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) tmem_cp_128x256b_warp(tmem + kColQ + c * 32 + kk * 8, qdesc + 2 * kk);
+          tc_commit_warp(smem_u32(&bars->ch_empty[slot]));
+        }
+        ok = ok && wait(smem_u32(&bars->rope_full[qi & 1]), (qi >> 1) & 1);
+        if (!ok) break;
+        SV_TRACE(9, qi);
+        const uint64_t rope_a = rope_desc + static_cast<uint64_t>(((qi & 1) * kChunkBytes) >> 4);
+        for (int tok = pc.tok0; tok < pc.tok_end && ok; tok += 2 * kBlk, ++g) {
+          const uint32_t buf = g & 1u;
+          const uint32_t sd = tmem + kColS + buf * 128;
+          ok = wait(smem_u32(&bars->s_empty[buf]), ((g >> 1) & 1) ^ 1);
+          if (!ok) break;
+          SV_TRACE(2, g);
+          if (pc.tok_end - tok > kBlk)
+            ok = qk_tile(std::integral_constant<uint32_t, kIdesc128>{}, sd, rope_a);
+          else
+            ok = qk_tile(std::integral_constant<uint32_t, kIdesc64>{}, sd, rope_a);
+          if (!ok) break;
+          SV_TRACE(3, g);
+#ifdef FA_TRACE
+          if (part == 0 && mb == 0 && g < 128) g_sv_trace[0][0][g][10] = wait_acc;
+          wait_acc = 0;
+#endif
+          tc_commit_warp(smem_u32(&bars->s_full[buf]));
+        }
+        if (!ok) break;
+        tc_commit_warp(smem_u32(&bars->rope_empty[qi & 1]));
+        ++qi;
+      }
+      // every issued MMA must finish before TMEM is released
+      tc_commit_warp(smem_u32(&bars->drain));
+      volatile int never = 0;
+      mbar_wait(smem_u32(&bars->drain), 0, &never, p.status, kDevTimeoutDrain);
+      __syncwarp();
+    } else if (warp >= 4 && warp < 12) {
+      // --------------------------------------------------------- softmax
+      // warp w: query rows 32 (w % 4) .. +31 (its TMEM lanes) and block
+      // ch = (w - 4) / 4 of every tile (score columns 64 ch .. 64 ch + 63).
+      const int ch = (warp - 4) >> 2;
+      const int q4 = warp & 3;
+      const int t = q4 * 32 + lane;
+      const uint32_t trow = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+      const uint32_t pair_bar = smem_u32(&bars->pair[q4]);
+      uint32_t pair_uses = 0;
+      auto pair_sync = [&]() -> bool {
+        mbar_arrive(pair_bar);
+        const bool r = __all_sync(0xffffffffu, mbar_wait(pair_bar, pair_uses & 1, abort_flag,
+                                                         p.status, kDevTimeoutSoftmax));
+        ++pair_uses;
+        return r;
+      };
+      float *red = reinterpret_cast<float *>(smem + kOffRed);  // [tile parity][ch][row]
+      const int flat = row0 + t;
+      const bool row_ok = t < n_rows;
+      const int s_tok = row_ok ? flat / p.h_q : 0;
+      const int h = row_ok ? flat % p.h_q : 0;
+      const int out_flat = s_tok * p.h_q + h;
+      const uint32_t p_remote = map_to_rank(s_base + kOffP, 1);
+      const uint32_t pfull_remote = map_to_rank(smem_u32(&bars->p_full[0]), 1);
+      bool ok = true;
+      uint32_t g = 0, gb = 0;
+      for (int i = 0; i < n_pieces && ok; ++i) {
+        const Piece pc = get_piece(p, meta, i);
+        const int first_slot = p.num_splits[pc.b];
+        const int n_split = p.num_splits[pc.b + 1] - first_slot;
+        const int slot_o = first_slot + pc.split_idx;
+        const int len = seq_len(p, pc.b);
+        const int row_len = p.causal ? len - (p.s_q - 1 - s_tok) : len;
+        float m_run = -INFINITY, l_half = 0.f, l_run = 0.f;
+        for (int tok = pc.tok0; tok < pc.tok_end && ok; tok += 2 * kBlk, ++g) {
+          const bool first = tok == pc.tok0;
+          const bool last = tok + 2 * kBlk >= pc.tok_end;
+          const int n_blk = (pc.tok_end - tok > kBlk) ? 2 : 1;
+          const uint32_t buf = g & 1u;
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->s_full[buf]), (g >> 1) & 1,
+                                                  abort_flag, p.status, kDevTimeoutSoftmax));
+          if (!ok) break;
+          if (lane == 0 && q4 == 0) SV_TRACE(4 + ch, g);
+          tc_fence_after();
+          float sc[64];
+          {
+            float v0[32], v1[32];
+            tmem_ld32(trow + kColS + buf * 128 + ch * 64, v0);
+            tmem_ld32(trow + kColS + buf * 128 + ch * 64 + 32, v1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              sc[j] = v0[j];
+              sc[32 + j] = v1[j];
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(smem_u32(&bars->s_empty[buf]));
+          // mask columns past the sequence / causal end (select: NaN-safe)
+          const int lim = min(pc.tok_end, row_len) - tok - ch * kBlk;
+          if (lim < kBlk) {
+#pragma unroll
+            for (int c = 0; c < kBlk; ++c)
+              if (c >= lim) sc[c] = -INFINITY;
+          }
+          float mx[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) mx[j] = sc[j];
+#pragma unroll
+          for (int c = 4; c < kBlk; c += 4) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) mx[j] = fmaxf(mx[j], sc[c + j]);
+          }
+          float mraw = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+          float *rslot = red + (g & 1u) * 2 * kRows;
+          rslot[ch * kRows + t] = mraw;
+          if (!(ok = pair_sync())) break;
+          if (t == 0 && ch == 0) SV_TRACE(6, g);
+          mraw = fmaxf(mraw, rslot[(ch ^ 1) * kRows + t]);
+          // online softmax with a lazily updated running max (log2 units)
+          const float mt = mraw * p.scale_log2;
+          float alpha = 1.f;
+          bool rescale = false;
+          if (mt > -INFINITY && (m_run == -INFINITY || mt > m_run + kRescaleThreshold)) {
+            alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - mt);
+            rescale = !first && m_run != -INFINITY;
+            m_run = mt;
+          }
+          const float ms = (m_run == -INFINITY) ? 0.f : m_run;
+          float ps[4] = {0.f, 0.f, 0.f, 0.f};
+          uint32_t pk[kBlk / 2];
+#pragma unroll
+          for (int c = 0; c < kBlk; c += 2) {
+            const float p0 = fast_exp2(fmaf(sc[c], p.scale_log2, -ms));
+            const float p1 = fast_exp2(fmaf(sc[c + 1], p.scale_log2, -ms));
+            ps[(c >> 1) & 3] += p0 + p1;
+            pk[c / 2] = Elem<T>::pack2(p0, p1);
+          }
+          l_half = l_half * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+          // P of this warp's block -> the value CTA's slot (gb + ch) % kPSlots
+          const uint32_t pb = gb + ch;
+          const uint32_t pslot = pb % kPSlots;
+          const uint32_t pdst = p_remote + pslot * kPSlotBytes;
+          const uint32_t pbar = pfull_remote + pslot * 8;
+          if (ch < n_blk) {
+            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->p_free[pslot]),
+                                                   ((pb / kPSlots) & 1) ^ 1, abort_flag, p.status,
+                                                   kDevTimeoutSoftmax));
+            if (!ok) break;
+            if (lane == 0 && q4 == 0) SV_TRACE(7 + ch, g);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              st_async_v4_u32(pdst + t * kRowBytes + ((u ^ (t & 7)) << 4), pk[4 * u],
+                              pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3], pbar);
+            if (ch == 0) {
+              st_async_u32(pdst + kMetaAlpha + 4 * t, __float_as_uint(rescale ? alpha : 1.f), pbar);
+              const bool any = __any_sync(0xffffffffu, rescale);
+              if (lane == 0) st_async_u32(pdst + kMetaFlags + 4 * q4, any ? 1u : 0u, pbar);
+            }
+          }
+          if (last) {
+            // row sum = both blocks' sums (through this tile's parity slot,
+            // once the partner has read the tile maximum)
+            if (!(ok = pair_sync())) break;
+            rslot[ch * kRows + t] = l_half;
+            if (!(ok = pair_sync())) break;
+            l_run = l_half + rslot[(ch ^ 1) * kRows + t];
+            if (ch == n_blk - 1)
+              st_async_u32(pdst + kMetaInvL + 4 * t, __float_as_uint(l_run > 0.f ? 1.f / l_run : 0.f),
+                           pbar);
+          }
+          gb += n_blk;
+        }
+        if (!ok) break;
+        // LSE of the piece (natural log of the scaled row sum)
+        const float ms = (m_run == -INFINITY) ? 0.f : m_run;
+        const float lse = l_run > 0.f ? ms * 0.69314718055994531f + logf(l_run) : -INFINITY;
+        if (ch == 0 && row_ok) {
+          if (n_split == 1)
+            p.lse[(static_cast<int64_t>(pc.b) * p.h_q + h) * p.s_q + s_tok] = lse;
+          else
+            p.part_lse[static_cast<int64_t>(slot_o) * rows_total + out_flat] = lse;
+        }
+      }
+    }
+  } else {
+    // ================================================================ value CTA
+    const uint32_t vbase = s_base + kOffV;
+    const uint32_t pbase = s_base + kOffP;
+    if (warp == 0) {
+      // ------------------------------------------------------- V producer
+      if (lane == 0) {
+        tma_prefetch_desc(&v_map);
+        uint32_t vs = 0, vbk = 0xffffffffu;
+        bool ok = true;
+        for (int i = 0; i < n_pieces && ok; ++i) {
+          const Piece pc = get_piece(p, meta, i);
+          for (int bt = pc.tok0; bt < pc.tok_end && ok; bt += kBlk) {
+            const int vb = min(kBlk, pc.tok_end - bt);
+            const int n_sub = vb > kVRows ? 2 : 1;
+            int c1, c2;
+            kv_coord(p, pc.b, bt, c1, c2);
+            ++vbk;
+            for (int j = 0; j < n_sub; ++j, ++vs) {
+              const int st = vs % kVStages;
+              ok = mbar_wait(smem_u32(&bars->v_empty[st]), ((vs / kVStages) & 1) ^ 1, abort_flag,
+                             p.status, kDevTimeoutProducer);
+              if (!ok) break;
+              if (j == 0) SV_TRACE(14, vbk);
+              const uint32_t full = smem_u32(&bars->v_full[st]);
+              mbar_arrive_expect_tx(full, kVStageBytes);
+#pragma unroll
+              for (int d = 0; d < 8; ++d)
+                tma_load_3d(vbase + st * kVStageBytes + d * kVChunkBytes, &v_map, full, 64 * d,
+                            c1 + kVRows * j, c2);
+            }
+          }
+        }
+        if (*abort_flag) {
+          volatile int never = 0;
+          for (uint32_t t = vs > kVStages ? vs - kVStages : 0; t < vs; ++t)
+            mbar_wait(smem_u32(&bars->v_full[t % kVStages]), (t / kVStages) & 1, &never, nullptr,
+                      0);
+        }
+      }
+      __syncwarp();
+    } else if (warp == 1) {
+      // ----------------------------------------------------- PV MMA issuer
+      // Whole warp runs the loop; one elected lane issues (see the score CTA).
+      constexpr uint32_t idesc = umma_idesc_f16(128, 256, fmt, 1);
+      const uint64_t p_desc = smem_desc_sw128(pbase, 16, 1024);
+      const uint64_t v_desc = smem_desc_sw128(vbase, kVChunkBytes, 1024);
+      auto wait = [&](uint32_t bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma));
+      };
+      uint32_t vs = 0, gb = 0;
+      int pi = 0;
+      bool ok = true;
+      for (int i = 0; i < n_pieces && ok; ++i) {
+        const Piece pc = get_piece(p, meta, i);
+        if (pc.tok_end <= pc.tok0) continue;
+        bool first_blk = true;
+        for (int bt = pc.tok0; bt < pc.tok_end && ok; bt += kBlk, ++gb) {
+          const int vb = min(kBlk, pc.tok_end - bt);
+          const int n_sub = vb > kVRows ? 2 : 1;
+          const bool tile_first = ((bt - pc.tok0) & (2 * kBlk - 1)) == 0;
+          const bool piece_last = bt + kBlk >= pc.tok_end;
+          const uint32_t ps = gb % kPSlots;
+          const uint32_t ph = (gb / kPSlots) & 1;
+          if (lane == 0)
+            mbar_arrive_expect_tx(smem_u32(&bars->p_full[ps]),
+                                  kPBytes + (tile_first ? 512 + 16 : 0) + (piece_last ? 512 : 0));
+          ok = wait(smem_u32(&bars->p_full[ps]), ph);
+          SV_TRACE(10, gb);
+          ok = ok && wait(smem_u32(&bars->m_read[ps]), ph);
+          SV_TRACE(11, gb);
+          if (ok && first_blk) ok = wait(smem_u32(&bars->o_empty), (pi & 1) ^ 1);
+          if (!ok) break;
+          fence_proxy_async_smem();  // st.async / cleared rows -> tensor-core reads
+          tc_fence_after();
+          const uint64_t pa = p_desc + static_cast<uint64_t>((ps * kPSlotBytes) >> 4);
+          for (int j = 0; j < n_sub; ++j, ++vs) {
+            const uint32_t st = vs % kVStages;
+            ok = wait(smem_u32(&bars->v_full[st]), (vs / kVStages) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t vd = v_desc + static_cast<uint64_t>((st * kVStageBytes) >> 4);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+              const uint64_t adesc = pa + static_cast<uint64_t>(((2 * j + kk) * 32) >> 4);
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh)
+                umma_ss_warp(tmem + 256 * hh, adesc,
+                             vd + static_cast<uint64_t>((hh * 4 * kVChunkBytes + kk * 16 * kRowBytes) >> 4),
+                             idesc, (first_blk && j == 0 && kk == 0) ? 0u : 1u);
+            }
+            tc_commit_warp(smem_u32(&bars->v_empty[st]));
+          }
+          if (!ok) break;
+          SV_TRACE(12, gb);
+          tc_commit_warp(smem_u32(&bars->pv_done[ps]));
+          tc_commit_mc_warp(smem_u32(&bars->p_free[ps]), 0x1);  // the score CTA may refill the slot
+          first_blk = false;
+        }
+        ++pi;
+      }
+      tc_commit_warp(smem_u32(&bars->drain));
+      volatile int never = 0;
+      mbar_wait(smem_u32(&bars->drain), 0, &never, p.status, kDevTimeoutDrain);
+      __syncwarp();
+    } else if (warp >= 4 && warp < 12) {
+      // ---------------------------------- O rescale, tail rows, epilogue
+      // warp w: rows 32 (w % 4) .. +31, output dims [256 ch, 256 ch + 256)
+      const int ch = (warp - 4) >> 2;
+      const int q4 = warp & 3;
+      const int t = q4 * 32 + lane;
+      const int tt = ch * kRows + t;  // 0..255
+      const uint32_t trow = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+      uint32_t vs = 0, gb = 0;
+      bool ok = true;
+      for (int i = 0; i < n_pieces && ok; ++i) {
+        const Piece pc = get_piece(p, meta, i);
+        const int first_slot = p.num_splits[pc.b];
+        const int n_split = p.num_splits[pc.b + 1] - first_slot;
+        const int slot_o = first_slot + pc.split_idx;
+        const bool has_tiles = pc.tok_end > pc.tok0;
+        float inv_l = 0.f;
+        for (int bt = pc.tok0; bt < pc.tok_end && ok; bt += kBlk, ++gb) {
+          const int vb = min(kBlk, pc.tok_end - bt);
+          const int n_sub = vb > kVRows ? 2 : 1;
+          const bool tile_first = ((bt - pc.tok0) & (2 * kBlk - 1)) == 0;
+          const int ps = gb % kPSlots;
+          const uint32_t ph = (gb / kPSlots) & 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->p_full[ps]), ph, abort_flag,
+                                                  p.status, kDevTimeoutSoftmax));
+          if (!ok) break;
+          if (tt == 0) SV_TRACE(13, gb);
+          const uint8_t *slotp = smem + kOffP + ps * kPSlotBytes;
+          if (tile_first && bt != pc.tok0) {
+            const int *fl = reinterpret_cast<const int *>(slotp + kMetaFlags);
+            if (fl[0] | fl[1] | fl[2] | fl[3]) {
+              // O may be rescaled once the previous block's PV has finished
+              const uint32_t pg = gb - 1;
+              ok = __all_sync(0xffffffffu,
+                              mbar_wait(smem_u32(&bars->pv_done[pg % kPSlots]), (pg / kPSlots) & 1,
+                                        abort_flag, p.status, kDevTimeoutSoftmax));
+              if (!ok) break;
+              if (fl[q4]) {
+                tc_fence_after();
+                const float a = reinterpret_cast<const float *>(slotp + kMetaAlpha)[t];
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+                  const uint32_t col = ch * 256 + c * 32;
+                  float v[32];
+                  tmem_ld32(trow + col, v);
+                  tmem_wait_ld();
+                  uint32_t w0[16], w1[16];
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) {
+                    w0[j] = __float_as_uint(v[j] * a);
+                    w1[j] = __float_as_uint(v[16 + j] * a);
+                  }
+                  tmem_st16(trow + col, w0);
+                  tmem_st16(trow + col + 16, w1);
+                }
+                tmem_wait_st();
+              }
+            }
+          }
+          if (bt + kBlk >= pc.tok_end) inv_l = reinterpret_cast<const float *>(slotp + kMetaInvL)[t];
+          if (vb < kBlk) {
+            // rows past the sequence end may hold any bits (even NaN); P is 0
+            // there but 0 * NaN is not, so clear them before the PV product.
+            for (int j = 0; j < n_sub; ++j) {
+              const int lo = max(vb - kVRows * j, 0);
+              if (lo >= kVRows) continue;
+              const uint32_t sv = vs + j;
+              const int st = sv % kVStages;
+              ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->v_full[st]), (sv / kVStages) & 1,
+                                                      abort_flag, p.status, kDevTimeoutSoftmax));
+              if (!ok) break;
+              uint8_t *stage = smem + kOffV + st * kVStageBytes;
+              const int units = (kVRows - lo) * 64;  // 8 chunks x 8 16-byte units per row
+              for (int u = tt; u < units; u += 256) {
+                const int r = lo + (u >> 6);
+                const int rem = u & 63;
+                *reinterpret_cast<uint4 *>(stage + (rem >> 3) * kVChunkBytes + r * kRowBytes +
+                                           (rem & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
+              }
+            }
+            if (!ok) break;
+            fence_proxy_async_smem();
+          }
+          tc_fence_before();
+          if (tt == 0) SV_TRACE(15, gb);
+          mbar_arrive(smem_u32(&bars->m_read[ps]));
+          vs += n_sub;
+        }
+        if (!ok) break;
+        if (tt == 0) SV_TRACE(0, 120 + i);
+        if (has_tiles) {
+          const uint32_t lg = gb - 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done[lg % kPSlots]),
+                                                 (lg / kPSlots) & 1, abort_flag, p.status,
+                                                 kDevTimeoutSoftmax));
+          if (!ok) break;
+          tc_fence_after();
+        }
+        // O / l -> out (final) or the f32 split workspace.  Each warp stages
+        // 32 rows x 128 bytes in shared memory (16-byte units XOR-swizzled by
+        // row) and writes them back four whole rows per store instruction.
+        const bool final_out = n_split == 1;
+        const bool f32_out = !final_out || p.out_f32;
+        const int esz = f32_out ? 4 : 2;
+        const int cols_it = 128 / esz;  // output dims per 128-byte row segment
+        uint8_t *stg = smem + kOffStage + (warp - 4) * kStageWarpBytes;
+        const uint32_t stg_s = smem_u32(stg);
+        int64_t row_off[8];  // byte offset of this lane's rows (4 k + lane / 8), -1 if absent
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int tr = q4 * 32 + 4 * k + (lane >> 3);
+          const int fl = row0 + tr;
+          if (tr >= n_rows) {
+            row_off[k] = -1;
+          } else if (final_out) {
+            const int st_ = fl / p.h_q, hh = fl % p.h_q;
+            row_off[k] = (pc.b * p.o_sb + st_ * p.o_ss + hh * p.o_sh) * esz;
+          } else {
+            row_off[k] = (static_cast<int64_t>(slot_o) * rows_total + fl) * p.d_v * 4;
+          }
+        }
+        uint8_t *obase = final_out ? static_cast<uint8_t *>(p.out) : reinterpret_cast<uint8_t *>(p.part_o);
+        if (tt == 0) SV_TRACE(1, 120 + i);
+#pragma unroll 1
+        for (int c0 = 0; c0 < 256; c0 += cols_it) {
+          const int col = ch * 256 + c0;
+          EPI_TRACE(0);
+          uint32_t w[32];
+          if (f32_out) {
+            float v[32];
+            if (has_tiles) {
+              tmem_ld32(trow + col, v);
+              tmem_wait_ld();
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j] * inv_l);
+          } else {
+            float v0[32], v1[32];
+            if (has_tiles) {
+              tmem_ld32(trow + col, v0);
+              tmem_ld32(trow + col + 32, v1);
+              tmem_wait_ld();
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v0[j] = v1[j] = 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              w[j] = Elem<T>::pack2(v0[2 * j] * inv_l, v0[2 * j + 1] * inv_l);
+              w[16 + j] = Elem<T>::pack2(v1[2 * j] * inv_l, v1[2 * j + 1] * inv_l);
+            }
+          }
+          EPI_TRACE(1);
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                             stg_s + lane * 128 + ((u ^ (lane & 7)) << 4)),
+                         "r"(w[4 * u]), "r"(w[4 * u + 1]), "r"(w[4 * u + 2]), "r"(w[4 * u + 3])
+                         : "memory");
+          __syncwarp();
+          EPI_TRACE(2);
+          const int j = lane & 7;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int r = 4 * k + (lane >> 3);
+            uint4 val;
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
+                         : "r"(stg_s + r * 128 + ((j ^ (r & 7)) << 4))
+                         : "memory");
+            if (row_off[k] >= 0)
+              *reinterpret_cast<uint4 *>(obase + row_off[k] + static_cast<int64_t>(col) * esz + j * 16) = val;
+          }
+          EPI_TRACE(3);
+          __syncwarp();
+        }
+        if (tt == 0) SV_TRACE(2, 120 + i);
+        if (has_tiles) {
+          tc_fence_before();
+          mbar_arrive(smem_u32(&bars->o_empty));
+        }
+      }
+    }
+  }
+
+  // -------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) SV_TRACE(12, 127);
+#ifdef FA_TRACE
+  if (threadIdx.x == 0 && part == 0 && mb == 0) g_sv_trace[0][rank][126][1] = static_cast<long long>(global_ns());
+#endif
+  cluster_sync();  // the peer no longer touches this CTA's shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace sv
+
+#ifdef FA_TRACE
+extern "C" int fa_debug_sv_epi_read(void *dst, size_t bytes) {
+  return cudaMemcpyFromSymbol(dst, sv::g_sv_epi,
+                              bytes < sizeof(sv::g_sv_epi) ? bytes : sizeof(sv::g_sv_epi)) ==
+                 cudaSuccess ? 0 : -1;
+}
+extern "C" int fa_debug_sv_trace_read(void *dst, size_t bytes) {
+  return cudaMemcpyFromSymbol(dst, sv::g_sv_trace,
+                              bytes < sizeof(sv::g_sv_trace) ? bytes : sizeof(sv::g_sv_trace)) ==
+                 cudaSuccess ? 0 : -1;
+}
+#endif
+
+// q_map: query (box 64 dims x 128 rows), kv_map: key rows (box 64 x 64),
+// v_map: value rows (box 64 x 32); all 128-byte swizzle over the same layouts
+// as the reference's caches ([pages, page, 1, 576]).
+cudaError_t launch_mla_sv(const CUtensorMap &qm, const CUtensorMap &km, const CUtensorMap &vm,
+                          const fa_mla_args *a, int m_blocks, cudaStream_t stream) {
+  sv::Params p;
+  p.block_table = a->block_table;
+  p.bt_stride = a->bt_stride;
+  p.seq_lens = a->seq_lens;
+  p.n_ctx = a->n_ctx;
+  p.page_size = a->page_size;
+  p.tile_meta = a->tile_meta;
+  p.num_splits = a->num_splits;
+  p.out = a->out;
+  p.o_sb = a->o_stride_b;
+  p.o_ss = a->o_stride_s;
+  p.o_sh = a->o_stride_h;
+  p.lse = a->lse;
+  p.part_o = a->part_o;
+  p.part_lse = a->part_lse;
+  p.batch = a->batch;
+  p.s_q = a->s_q;
+  p.h_q = a->h_q;
+  p.d_v = a->d_v;
+  p.causal = a->causal;
+  p.paged = a->block_table != nullptr;
+  p.out_f32 = a->out_dtype == FA_DTYPE_F32;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.status = a->status;
+  const dim3 grid(2 * a->num_sm_parts, m_blocks);
+  cudaError_t e;
+  if (a->dtype == FA_DTYPE_F16) {
+    auto kern = sv::mla_decode_sv_kernel<__half>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sv::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, sv::kThreads, sv::kSmemBytes, stream>>>(qm, km, vm, p);
+  } else {
+    auto kern = sv::mla_decode_sv_kernel<__nv_bfloat16>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sv::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, sv::kThreads, sv::kSmemBytes, stream>>>(qm, km, vm, p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace fa
