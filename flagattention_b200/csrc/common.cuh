@@ -201,6 +201,17 @@ __device__ __forceinline__ void st_async_u32(uint32_t cluster_addr, uint32_t a,
                : "memory");
 }
 
+// Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory into a
+// peer CTA's shared memory, completing on the peer's mbarrier.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t cluster_dst, uint32_t local_src,
+                                                  uint32_t bytes, uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(cluster_dst),
+      "r"(local_src), "r"(bytes), "r"(cluster_bar)
+      : "memory");
+}
+
 // --------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
                                             int c0, int c1, int c2) {
@@ -209,6 +220,11 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+// Bring [src, src + bytes) into L2 without touching shared memory (16-byte
+// aligned address, size a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -304,6 +320,12 @@ __device__ __forceinline__ void umma_ts_warp(uint32_t d_tmem, uint32_t a_tmem, u
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+// Copy a 128-row x 256-bit tile (one K-step of 16 bf16/f16 per row) from
+// shared memory into TMEM lanes 0..127, columns taddr .. taddr+7 (issued by
+// the calling thread; in order with its MMAs).
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t s_desc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(s_desc) : "memory");
 }
 // Copy a 128-row x 256-bit tile (one K-step of 16 bf16/f16 per row) from
 // shared memory, described like an MMA operand, into TMEM lanes 0..127 at

@@ -43,7 +43,7 @@ constexpr int kBoxBytes = kBlk * kRowBytes;         // 8 KB
 constexpr int kChunkBytes = 2 * kBoxBytes;          // 16 KB: 128 rows x 64 dims
 constexpr int kQChunks = 8;                         // latent Q, 512 dims
 constexpr int kKChunks = 9;                         // key: 512 latent + 64 rope dims
-constexpr int kRing = 11;
+constexpr int kRing = 9;
 constexpr int kVRows = 32;                          // tokens per V stage
 constexpr int kVChunkBytes = kVRows * kRowBytes;    // 4 KB: 32 rows x 64 dims
 constexpr int kVStageBytes = 8 * kVChunkBytes;      // 32 KB: 512 dims
@@ -56,14 +56,42 @@ constexpr int kPSlotBytes = kPBytes + 2048;         // 18 KB
 constexpr int kPSlots = 3;
 constexpr uint32_t kColQ = 0, kColS = 256, kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;           // log2 units (factor 256)
+// MMA issue: one thread (default) or the whole warp with elect.sync.
+#ifndef FA_SV_SINGLE_ISSUE
+#define FA_SV_SINGLE_ISSUE 0
+#endif
+#if FA_SV_SINGLE_ISSUE
+#define SV_UMMA_TS umma_ts
+#define SV_UMMA_SS umma_ss
+#define SV_COMMIT tc_commit
+#define SV_COMMIT_MC tc_commit_mc
+#define SV_TMEM_CP tmem_cp_128x256b
+#define SV_ISSUER (lane == 0)
+#define SV_VOTE(x) (x)
+#else
+#define SV_UMMA_TS umma_ts_warp
+#define SV_UMMA_SS umma_ss_warp
+#define SV_COMMIT tc_commit_warp
+#define SV_COMMIT_MC tc_commit_mc_warp
+#define SV_TMEM_CP tmem_cp_128x256b_warp
+#define SV_ISSUER true
+#define SV_VOTE(x) __all_sync(0xffffffffu, (x))
+#endif
+
+#ifndef FA_SV_PREFETCH_TILES
+#define FA_SV_PREFETCH_TILES 0
+#endif
+// Distance, in 128-token tiles, of the value CTA's L2 prefetch of key rows.
+constexpr int kPrefetchTiles = FA_SV_PREFETCH_TILES;
 
 constexpr int kOffBar = 0;
 constexpr int kOffData = 1024;
 // score CTA
 constexpr int kOffQRope = kOffData;                         // 2 x 16 KB
-constexpr int kOffRing = kOffQRope + 2 * kChunkBytes;       // 11 x 16 KB
+constexpr int kOffRing = kOffQRope + 2 * kChunkBytes;       // 9 x 16 KB
 constexpr int kOffRed = kOffRing + kRing * kChunkBytes;     // 2 KB row maxima / sums
-constexpr int kSmemScore = kOffRed + 2048;
+constexpr int kOffStgP = kOffRed + 2048;                    // 2 x 16 KB P staging
+constexpr int kSmemScore = kOffStgP + 2 * kPBytes;
 // value CTA
 constexpr int kOffV = kOffData;                             // 4 x 32 KB
 constexpr int kOffP = kOffV + kVStages * kVStageBytes;      // 3 x 18 KB
@@ -74,6 +102,7 @@ constexpr int kSmemUsed = kSmemScore > kSmemValue ? kSmemScore : kSmemValue;
 constexpr int kSmemBytes = kSmemUsed + 1024;                // + base alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory plan exceeds 227 KB");
 static_assert(kOffRing % 1024 == 0 && kOffQRope % 1024 == 0 && kOffV % 1024 == 0 &&
+                  kOffStgP % 1024 == 0 &&
                   kOffP % 1024 == 0 && kPSlotBytes % 1024 == 0,
               "swizzled operands need 1024-byte alignment");
 
@@ -85,6 +114,7 @@ struct Bars {
   uint64_t ch_full[kRing], ch_empty[kRing];
   uint64_t s_full[2], s_empty[2];
   uint64_t pair[4];
+  uint64_t stg_ready[2];     // the 128 rows of a P block are staged (one per block half)
   uint64_t p_free[kPSlots];  // arrived by the value CTA's PV commit
   // value CTA
   uint64_t v_full[kVStages], v_empty[kVStages];
@@ -108,6 +138,15 @@ __device__ long long g_sv_trace[2][2][128][16];
     if (tp_ >= 0 && (idx) < 128) g_sv_trace[tp_][rank][(idx)][(ev)] = clock64();     \
   } while (0)
 __device__ long long g_sv_epi[2][8][4];
+__device__ long long g_sv_mma[4][9][4];
+#define MMA_TRACE(c, ev)                                     \
+  do {                                                       \
+    const long long now_ = clock64();                        \
+    if ((ev) == 0) acc_w += now_ - t_mark;                   \
+    if ((ev) == 1) acc_i += now_ - t_mark;                   \
+    if ((ev) == 2) acc_c += now_ - t_mark;                   \
+    t_mark = now_;                                           \
+  } while (0)
 #define EPI_TRACE(ev)                                                                  \
   do {                                                                                 \
     if (part == 0 && mb == 0 && tt == 0 && i < 2 && c0 / cols_it < 8)                  \
@@ -117,12 +156,19 @@ __device__ long long g_sv_epi[2][8][4];
 #define EPI_TRACE(ev) \
   do {                \
   } while (0)
+#define MMA_TRACE(c, ev) \
+  do {                   \
+  } while (0)
 #define SV_TRACE(ev, idx) \
   do {                    \
   } while (0)
 #endif
 
 struct Params {
+  const uint8_t *kcache;  // L2 prefetch of whole 64-token blocks (rows of 576 contiguous)
+  int64_t kv_sp, kv_st;   // page / token strides in elements
+  const uint8_t *q;       // L2 prefetch of a piece's query rows
+  int64_t q_sb, q_sh;
   const int32_t *block_table;
   int64_t bt_stride;
   const int32_t *seq_lens;
@@ -167,13 +213,69 @@ __device__ __forceinline__ Piece get_piece(const Params &p, const int32_t *meta,
 // TMA coordinates (row in page, page) of token t of sequence b.
 __device__ __forceinline__ void kv_coord(const Params &p, int b, int t, int &c1, int &c2) {
   if (p.paged) {
-    c2 = p.block_table[static_cast<int64_t>(b) * p.bt_stride + t / p.page_size];
+    c2 = __ldg(p.block_table + static_cast<int64_t>(b) * p.bt_stride + t / p.page_size);
     c1 = t % p.page_size;
   } else {
     c2 = b;
     c1 = t;
   }
 }
+
+// Position in a ring of kRing slots: slot index and the parity of its phase.
+struct RingPos {
+  uint32_t slot = 0, phase = 0;
+  __device__ __forceinline__ void next() {
+    if (++slot == kRing) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+// Tiles of a part in order, for the producer's L2 prefetch that runs
+// kPrefetchTiles tiles ahead of its loads.
+struct PrefetchCursor {
+  int i = 0, tok = 0, tok_end = 0, b = 0;
+  bool first = false, valid = false;
+  __device__ __forceinline__ void seek(const Params &p, const int32_t *meta, int n_pieces) {
+    for (; i < n_pieces; ++i) {
+      const Piece pc = get_piece(p, meta, i);
+      if (pc.tok_end > pc.tok0) {
+        tok = pc.tok0;
+        tok_end = pc.tok_end;
+        b = pc.b;
+        first = valid = true;
+        return;
+      }
+    }
+    valid = false;
+  }
+  // Prefetch the cursor's tile (and the piece's query rows on its first
+  // tile), then step to the next tile.
+  __device__ __forceinline__ void issue(const Params &p, const int32_t *meta, int n_pieces,
+                                        int row0, int n_rows) {
+    if (!valid) return;
+    if (first && p.q_sh == 576)
+      bulk_prefetch_l2(p.q + (static_cast<int64_t>(b) * p.q_sb + static_cast<int64_t>(row0) * 576) * 2,
+                       n_rows * 1152);
+    first = false;
+    if (p.paged && p.kv_st == 576) {  // a 64-row block lies inside one page
+      for (int j = 0; j < 2 && tok + j * kBlk < tok_end; ++j) {
+        const int t = tok + j * kBlk;
+        int c1, c2;
+        kv_coord(p, b, t, c1, c2);
+        const int rows = min(kBlk, tok_end - t);
+        bulk_prefetch_l2(p.kcache + (static_cast<int64_t>(c2) * p.kv_sp + static_cast<int64_t>(c1) * 576) * 2,
+                         rows * 1152);
+      }
+    }
+    tok += 2 * kBlk;
+    if (tok >= tok_end) {
+      ++i;
+      seek(p, meta, n_pieces);
+    }
+  }
+};
 
 // 32 lanes x 32 columns of 32-bit TMEM words.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
@@ -236,6 +338,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&bars->ch_empty[i]), 1);
     }
     for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&bars->pair[i]), 64);
+    for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bars->stg_ready[i]), 128);
     for (int i = 0; i < kPSlots; ++i) {
       mbar_init(smem_u32(&bars->p_free[i]), 1);
       mbar_init(smem_u32(&bars->p_full[i]), 1);
@@ -274,21 +377,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         tma_prefetch_desc(&q_map);
         tma_prefetch_desc(&kv_map);
-        uint32_t rc = 0, tg = 0;
+        RingPos rp;
+        uint32_t issued = 0, tg = 0;
         int qi = 0;
         bool ok = true;
+        auto next_slot = [&](uint32_t bytes) -> uint32_t {  // wait for a free slot, arm it
+          if (!mbar_wait(smem_u32(&bars->ch_empty[rp.slot]), rp.phase ^ 1, abort_flag, p.status,
+                         kDevTimeoutProducer))
+            return 0xffffffffu;
+          const uint32_t full = smem_u32(&bars->ch_full[rp.slot]);
+          mbar_arrive_expect_tx(full, bytes);
+          ++issued;
+          return full;
+        };
         for (int i = 0; i < n_pieces && ok; ++i) {
           const Piece pc = get_piece(p, meta, i);
           if (pc.tok_end <= pc.tok0) continue;
           // latent Q: 8 chunks of 64 dims x 128 rows through the ring
-          for (int c = 0; c < kQChunks; ++c, ++rc) {
-            const int slot = rc % kRing;
-            ok = mbar_wait(smem_u32(&bars->ch_empty[slot]), ((rc / kRing) & 1) ^ 1, abort_flag,
-                           p.status, kDevTimeoutProducer);
-            if (!ok) break;
-            const uint32_t full = smem_u32(&bars->ch_full[slot]);
-            mbar_arrive_expect_tx(full, kChunkBytes);
-            tma_load_3d(ring + slot * kChunkBytes, &q_map, full, 64 * c, row0, pc.b);
+          for (int c = 0; c < kQChunks; ++c) {
+            const uint32_t full = next_slot(kChunkBytes);
+            if (!(ok = full != 0xffffffffu)) break;
+            tma_load_3d(ring + rp.slot * kChunkBytes, &q_map, full, 64 * c, row0, pc.b);
+            rp.next();
           }
           if (!ok) break;
           // rope Q (dims 512..575) -> buffer qi & 1
@@ -299,28 +409,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tma_load_3d(qrope + (qi & 1) * kChunkBytes, &q_map, smem_u32(&bars->rope_full[qi & 1]),
                       512, row0, pc.b);
           ++qi;
+          // page coordinates of the next tile are looked up one tile ahead
+          int nc1[2], nc2[2];
+          for (int j = 0; j < 2; ++j)
+            if (pc.tok0 + j * kBlk < pc.tok_end) kv_coord(p, pc.b, pc.tok0 + j * kBlk, nc1[j], nc2[j]);
           for (int tok = pc.tok0; tok < pc.tok_end && ok; tok += 2 * kBlk, ++tg) {
             const int n_blk = (pc.tok_end - tok > kBlk) ? 2 : 1;
-            int c1[2], c2[2];
-            for (int j = 0; j < n_blk; ++j) kv_coord(p, pc.b, tok + j * kBlk, c1[j], c2[j]);
-            for (int c = 0; c < kKChunks; ++c, ++rc) {
-              const int slot = rc % kRing;
-              ok = mbar_wait(smem_u32(&bars->ch_empty[slot]), ((rc / kRing) & 1) ^ 1, abort_flag,
-                             p.status, kDevTimeoutProducer);
-              if (!ok) break;
-              const uint32_t full = smem_u32(&bars->ch_full[slot]);
+            const int c1[2] = {nc1[0], nc1[1]}, c2[2] = {nc2[0], nc2[1]};
+            for (int j = 0; j < 2; ++j)
+              if (tok + (2 + j) * kBlk < pc.tok_end)
+                kv_coord(p, pc.b, tok + (2 + j) * kBlk, nc1[j], nc2[j]);
+            for (int c = 0; c < kKChunks; ++c) {
+              const uint32_t full = next_slot(n_blk * kBoxBytes);
+              if (!(ok = full != 0xffffffffu)) break;
               if (c == 0) SV_TRACE(0, tg);
               if (c == kKChunks - 1) SV_TRACE(1, tg);
-              mbar_arrive_expect_tx(full, n_blk * kBoxBytes);
               for (int j = 0; j < n_blk; ++j)
-                tma_load_3d(ring + slot * kChunkBytes + j * kBoxBytes, &kv_map, full, 64 * c,
+                tma_load_3d(ring + rp.slot * kChunkBytes + j * kBoxBytes, &kv_map, full, 64 * c,
                             c1[j], c2[j]);
+              rp.next();
             }
           }
         }
         if (*abort_flag) {  // copies in flight must land before the CTA may exit
           volatile int never = 0;
-          for (uint32_t t = rc > kRing ? rc - kRing : 0; t < rc; ++t)
+          for (uint32_t t = issued > kRing ? issued - kRing : 0; t < issued; ++t)
             mbar_wait(smem_u32(&bars->ch_full[t % kRing]), (t / kRing) & 1, &never, nullptr, 0);
           if (qi > 0)
             mbar_wait(smem_u32(&bars->rope_full[(qi - 1) & 1]), ((qi - 1) >> 1) & 1, &never,
@@ -330,49 +443,60 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       __syncwarp();
     } else if (warp == 1) {
       // -------------------------------------------------------- MMA issuer
-      // The whole warp runs the loop (warp-uniform operands); one elected
-      // lane issues each MMA / commit.
+      // One thread issues every MMA / copy / commit (FA_SV_SINGLE_ISSUE), or
+      // the whole warp runs the loop and an elected lane issues.
       // The instruction descriptor must be a compile-time constant: a runtime
       // one costs about 40 extra cycles per MMA.  Full tiles (N = 128) and
       // the half tile at a piece end (N = 64) get separate loops.
+      if (SV_ISSUER) {
       constexpr uint32_t kIdesc128 = umma_idesc_f16(128, 128, fmt, 0);
       constexpr uint32_t kIdesc64 = umma_idesc_f16(128, 64, fmt, 0);
       const uint64_t ring_desc = smem_desc_sw128(ring, 16, 1024);
       const uint64_t rope_desc = smem_desc_sw128(qrope, 16, 1024);
-      auto wait = [&](uint32_t bar, uint32_t parity) {
-        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma));
+      auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+        // fast path: the phase is usually complete already (one test_wait,
+        // uniform across the warp); otherwise the bounded wait
+        if (mbar_probe(bar, parity)) return true;
+        return SV_VOTE(mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma)) != 0;
       };
-      uint32_t rc = 0, g = 0;
+      RingPos rp;
+      uint32_t g = 0;
       int qi = 0;
       bool ok = true;
 #ifdef FA_TRACE
-      long long wait_acc = 0;
+      long long acc_w = 0, acc_i = 0, acc_c = 0, acc_g = 0, t_mark = clock64();
 #endif
       // QK of one tile into S buffer sd: 8 latent chunks (A = Q from TMEM)
       // and the rope chunk (A = rope Q from shared memory).
       auto qk_tile = [&](auto idesc_tag, uint32_t sd, uint64_t rope_a) -> bool {
         constexpr uint32_t idesc = decltype(idesc_tag)::value;
-        for (int c = 0; c < kKChunks; ++c, ++rc) {
-          const uint32_t slot = rc % kRing;
+#pragma unroll 1
+        for (int c = 0; c < kKChunks; ++c) {
 #ifdef FA_TRACE
-          const long long w0_ = clock64();
+          {
+            const long long now_ = clock64();
+            acc_g += now_ - t_mark;  // loop overhead since the previous commit
+            t_mark = now_;
+          }
 #endif
-          if (!wait(smem_u32(&bars->ch_full[slot]), (rc / kRing) & 1)) return false;
-#ifdef FA_TRACE
-          wait_acc += clock64() - w0_;
-#endif
-          tc_fence_after();
-          const uint64_t kdesc = ring_desc + static_cast<uint64_t>((slot * kChunkBytes) >> 4);
+          if (!wait(smem_u32(&bars->ch_full[rp.slot]), rp.phase)) return false;
+          MMA_TRACE(c, 0);
+          // TMA data signalled by the mbarrier: no tcgen05 fence here (one
+          // after every chunk drains the MMA queue and halves the rate)
+          const uint64_t kdesc = ring_desc + static_cast<uint64_t>((rp.slot * kChunkBytes) >> 4);
           if (c < kQChunks) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              umma_ts_warp(sd, tmem + kColQ + c * 32 + kk * 8, kdesc + 2 * kk, idesc,
+              SV_UMMA_TS(sd, tmem + kColQ + c * 32 + kk * 8, kdesc + 2 * kk, idesc,
                            (c | kk) ? 1u : 0u);
           } else {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) umma_ss_warp(sd, rope_a + 2 * kk, kdesc + 2 * kk, idesc, 1u);
+            for (int kk = 0; kk < 4; ++kk) SV_UMMA_SS(sd, rope_a + 2 * kk, kdesc + 2 * kk, idesc, 1u);
           }
-          tc_commit_warp(smem_u32(&bars->ch_empty[slot]));
+          MMA_TRACE(c, 1);
+          SV_COMMIT(smem_u32(&bars->ch_empty[rp.slot]));
+          MMA_TRACE(c, 2);
+          rp.next();
         }
         return true;
       };
@@ -381,15 +505,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (pc.tok_end <= pc.tok0) continue;
         // latent Q -> TMEM columns [0, 256): tcgen05.cp runs in order with
         // this warp's MMAs, so it starts after the previous piece's last QK
-        for (int c = 0; c < kQChunks && ok; ++c, ++rc) {
-          const uint32_t slot = rc % kRing;
-          ok = wait(smem_u32(&bars->ch_full[slot]), (rc / kRing) & 1);
+        for (int c = 0; c < kQChunks && ok; ++c) {
+          ok = wait(smem_u32(&bars->ch_full[rp.slot]), rp.phase);
           if (!ok) break;
-          tc_fence_after();
-          const uint64_t qdesc = ring_desc + static_cast<uint64_t>((slot * kChunkBytes) >> 4);
+          const uint64_t qdesc = ring_desc + static_cast<uint64_t>((rp.slot * kChunkBytes) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) tmem_cp_128x256b_warp(tmem + kColQ + c * 32 + kk * 8, qdesc + 2 * kk);
-          tc_commit_warp(smem_u32(&bars->ch_empty[slot]));
+          for (int kk = 0; kk < 4; ++kk) SV_TMEM_CP(tmem + kColQ + c * 32 + kk * 8, qdesc + 2 * kk);
+          SV_COMMIT(smem_u32(&bars->ch_empty[rp.slot]));
+          rp.next();
         }
         ok = ok && wait(smem_u32(&bars->rope_full[qi & 1]), (qi >> 1) & 1);
         if (!ok) break;
@@ -400,6 +523,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t sd = tmem + kColS + buf * 128;
           ok = wait(smem_u32(&bars->s_empty[buf]), ((g >> 1) & 1) ^ 1);
           if (!ok) break;
+          tc_fence_after();  // the softmax's tcgen05.ld of this buffer precede the new QK
           SV_TRACE(2, g);
           if (pc.tok_end - tok > kBlk)
             ok = qk_tile(std::integral_constant<uint32_t, kIdesc128>{}, sd, rope_a);
@@ -408,19 +532,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (!ok) break;
           SV_TRACE(3, g);
 #ifdef FA_TRACE
-          if (part == 0 && mb == 0 && g < 128) g_sv_trace[0][0][g][10] = wait_acc;
-          wait_acc = 0;
+          if (part == 0 && mb == 0 && g < 128 && lane == 0) {
+            g_sv_trace[0][0][g][12] = acc_w;
+            g_sv_trace[0][0][g][13] = acc_i;
+            g_sv_trace[0][0][g][14] = acc_c;
+            g_sv_trace[0][0][g][15] = acc_g;
+          }
+          acc_w = acc_i = acc_c = acc_g = 0;
 #endif
-          tc_commit_warp(smem_u32(&bars->s_full[buf]));
+          SV_COMMIT(smem_u32(&bars->s_full[buf]));
         }
         if (!ok) break;
-        tc_commit_warp(smem_u32(&bars->rope_empty[qi & 1]));
+        SV_COMMIT(smem_u32(&bars->rope_empty[qi & 1]));
         ++qi;
       }
       // every issued MMA must finish before TMEM is released
-      tc_commit_warp(smem_u32(&bars->drain));
+      SV_COMMIT(smem_u32(&bars->drain));
       volatile int never = 0;
       mbar_wait(smem_u32(&bars->drain), 0, &never, p.status, kDevTimeoutDrain);
+      }
       __syncwarp();
     } else if (warp >= 4 && warp < 12) {
       // --------------------------------------------------------- softmax
@@ -449,6 +579,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t pfull_remote = map_to_rank(smem_u32(&bars->p_full[0]), 1);
       bool ok = true;
       uint32_t g = 0, gb = 0;
+      uint32_t stg_uses[2] = {0, 0};
       for (int i = 0; i < n_pieces && ok; ++i) {
         const Piece pc = get_piece(p, meta, i);
         const int first_slot = p.num_splits[pc.b];
@@ -528,15 +659,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t pdst = p_remote + pslot * kPSlotBytes;
           const uint32_t pbar = pfull_remote + pslot * 8;
           if (ch < n_blk) {
+            // The block's 16 KB of P is staged in local shared memory (buffer
+            // pb & 1) and sent with one bulk copy: 1024 separate 16-byte
+            // remote stores per block crowd the memory-instruction queues
+            // that the producer's and MMA warp's instructions also use.
+            // The staging buffer was last sent for block pb - 2, whose PV has
+            // finished once p_free of its slot has (its copy had landed).
             ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->p_free[pslot]),
                                                    ((pb / kPSlots) & 1) ^ 1, abort_flag, p.status,
                                                    kDevTimeoutSoftmax));
+            if (ok && pb >= 2)
+              ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->p_free[(pb - 2) % kPSlots]),
+                                                     ((pb - 2) / kPSlots) & 1, abort_flag,
+                                                     p.status, kDevTimeoutSoftmax));
             if (!ok) break;
             if (lane == 0 && q4 == 0) SV_TRACE(7 + ch, g);
+            const uint32_t stg = s_base + kOffStgP + (pb & 1) * kPBytes;
 #pragma unroll
             for (int u = 0; u < 8; ++u)
-              st_async_v4_u32(pdst + t * kRowBytes + ((u ^ (t & 7)) << 4), pk[4 * u],
-                              pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3], pbar);
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                               stg + t * kRowBytes + ((u ^ (t & 7)) << 4)),
+                           "r"(pk[4 * u]), "r"(pk[4 * u + 1]), "r"(pk[4 * u + 2]), "r"(pk[4 * u + 3])
+                           : "memory");
+            fence_proxy_async_smem();  // generic-proxy writes -> the bulk copy's reads
+            mbar_arrive(smem_u32(&bars->stg_ready[ch]));
+            if (t == 0) {
+              if (!mbar_wait(smem_u32(&bars->stg_ready[ch]), stg_uses[ch] & 1, abort_flag,
+                             p.status, kDevTimeoutSoftmax))
+                ok = false;
+              else
+                bulk_copy_to_peer(pdst, stg, kPBytes, pbar);
+            }
+            ++stg_uses[ch];
+            if (!(ok = __all_sync(0xffffffffu, ok))) break;
             if (ch == 0) {
               st_async_u32(pdst + kMetaAlpha + 4 * t, __float_as_uint(rescale ? alpha : 1.f), pbar);
               const bool any = __any_sync(0xffffffffu, rescale);
@@ -578,9 +733,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&v_map);
         uint32_t vs = 0, vbk = 0xffffffffu;
         bool ok = true;
+        // L2 prefetch of whole key blocks kPrefetchTiles tiles ahead of this
+        // producer: the value CTA's copy engine takes the HBM misses, so the
+        // score CTA's loads (and this CTA's own) hit L2.
+        PrefetchCursor pf;
+        pf.seek(p, meta, n_pieces);
+        for (int k = 0; k < kPrefetchTiles; ++k) pf.issue(p, meta, n_pieces, row0, n_rows);
         for (int i = 0; i < n_pieces && ok; ++i) {
           const Piece pc = get_piece(p, meta, i);
           for (int bt = pc.tok0; bt < pc.tok_end && ok; bt += kBlk) {
+            if (kPrefetchTiles > 0 && ((bt - pc.tok0) & (2 * kBlk - 1)) == 0)
+              pf.issue(p, meta, n_pieces, row0, n_rows);
             const int vb = min(kBlk, pc.tok_end - bt);
             const int n_sub = vb > kVRows ? 2 : 1;
             int c1, c2;
@@ -611,12 +774,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       __syncwarp();
     } else if (warp == 1) {
       // ----------------------------------------------------- PV MMA issuer
-      // Whole warp runs the loop; one elected lane issues (see the score CTA).
+      // Issued like the score CTA's MMAs (one thread, or the elected lane).
+      if (SV_ISSUER) {
       constexpr uint32_t idesc = umma_idesc_f16(128, 256, fmt, 1);
       const uint64_t p_desc = smem_desc_sw128(pbase, 16, 1024);
       const uint64_t v_desc = smem_desc_sw128(vbase, kVChunkBytes, 1024);
-      auto wait = [&](uint32_t bar, uint32_t parity) {
-        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma));
+      auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+        // fast path: the phase is usually complete already (one test_wait,
+        // uniform across the warp); otherwise the bounded wait
+        if (mbar_probe(bar, parity)) return true;
+        return SV_VOTE(mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma)) != 0;
       };
       uint32_t vs = 0, gb = 0;
       int pi = 0;
@@ -648,30 +815,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint32_t st = vs % kVStages;
             ok = wait(smem_u32(&bars->v_full[st]), (vs / kVStages) & 1);
             if (!ok) break;
-            tc_fence_after();
             const uint64_t vd = v_desc + static_cast<uint64_t>((st * kVStageBytes) >> 4);
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
               const uint64_t adesc = pa + static_cast<uint64_t>(((2 * j + kk) * 32) >> 4);
 #pragma unroll
               for (int hh = 0; hh < 2; ++hh)
-                umma_ss_warp(tmem + 256 * hh, adesc,
+                SV_UMMA_SS(tmem + 256 * hh, adesc,
                              vd + static_cast<uint64_t>((hh * 4 * kVChunkBytes + kk * 16 * kRowBytes) >> 4),
                              idesc, (first_blk && j == 0 && kk == 0) ? 0u : 1u);
             }
-            tc_commit_warp(smem_u32(&bars->v_empty[st]));
+            SV_COMMIT(smem_u32(&bars->v_empty[st]));
           }
           if (!ok) break;
           SV_TRACE(12, gb);
-          tc_commit_warp(smem_u32(&bars->pv_done[ps]));
-          tc_commit_mc_warp(smem_u32(&bars->p_free[ps]), 0x1);  // the score CTA may refill the slot
+          SV_COMMIT(smem_u32(&bars->pv_done[ps]));
+          SV_COMMIT_MC(smem_u32(&bars->p_free[ps]), 0x1);  // the score CTA may refill the slot
           first_blk = false;
         }
         ++pi;
       }
-      tc_commit_warp(smem_u32(&bars->drain));
+      SV_COMMIT(smem_u32(&bars->drain));
       volatile int never = 0;
       mbar_wait(smem_u32(&bars->drain), 0, &never, p.status, kDevTimeoutDrain);
+      }
       __syncwarp();
     } else if (warp >= 4 && warp < 12) {
       // ---------------------------------- O rescale, tail rows, epilogue
@@ -878,6 +1045,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }  // namespace sv
 
 #ifdef FA_TRACE
+extern "C" int fa_debug_sv_mma_read(void *dst, size_t bytes) {
+  return cudaMemcpyFromSymbol(dst, sv::g_sv_mma,
+                              bytes < sizeof(sv::g_sv_mma) ? bytes : sizeof(sv::g_sv_mma)) ==
+                 cudaSuccess ? 0 : -1;
+}
 extern "C" int fa_debug_sv_epi_read(void *dst, size_t bytes) {
   return cudaMemcpyFromSymbol(dst, sv::g_sv_epi,
                               bytes < sizeof(sv::g_sv_epi) ? bytes : sizeof(sv::g_sv_epi)) ==
@@ -896,6 +1068,12 @@ extern "C" int fa_debug_sv_trace_read(void *dst, size_t bytes) {
 cudaError_t launch_mla_sv(const CUtensorMap &qm, const CUtensorMap &km, const CUtensorMap &vm,
                           const fa_mla_args *a, int m_blocks, cudaStream_t stream) {
   sv::Params p;
+  p.kcache = static_cast<const uint8_t *>(a->kcache);
+  p.kv_sp = a->kv_stride_page;
+  p.kv_st = a->kv_stride_tok;
+  p.q = static_cast<const uint8_t *>(a->q);
+  p.q_sb = a->q_stride_b;
+  p.q_sh = a->q_stride_h;
   p.block_table = a->block_table;
   p.bt_stride = a->bt_stride;
   p.seq_lens = a->seq_lens;
