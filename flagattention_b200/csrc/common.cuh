@@ -129,18 +129,16 @@ __device__ __forceinline__ bool mbar_probe(uint32_t bar, uint32_t parity) {
 
 // Wait for the phase with the given parity.  Returns false (and raises the
 // CTA abort flag / device status) once kWaitLimitCycles have passed, or as soon as
-// another role of the CTA has aborted.
-template <bool kClusterScope = false>
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                          int *status, int code) {
-  long long t0 = 0;
-  for (uint32_t it = 0;; ++it) {
+// another role of the CTA has aborted.  The first test is inline; the bounded
+// polling loop is an out-of-line call, which keeps the many wait sites of a
+// kernel small (instruction-cache pressure).
+template <bool kClusterScope>
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                            int *status, int code) {
+  const long long t0 = clock64();
+  for (uint32_t it = 1;; ++it) {
     if (kClusterScope ? mbar_test_cluster(bar, parity) : mbar_test(bar, parity)) return true;
     if ((it & 63u) == 0) {
-      if (it == 0) {
-        t0 = clock64();
-        continue;
-      }
       if (*abort_flag) return false;
       if (clock64() - t0 > kWaitLimitCycles) {
         *abort_flag = 1;
@@ -149,6 +147,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       }
     }
   }
+}
+template <bool kClusterScope = false>
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                          int *status, int code) {
+  if (kClusterScope ? mbar_test_cluster(bar, parity) : mbar_test(bar, parity)) return true;
+  return mbar_wait_slow<kClusterScope>(bar, parity, abort_flag, status, code);
 }
 
 __device__ __forceinline__ void fence_barrier_init() {

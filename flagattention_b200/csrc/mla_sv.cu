@@ -446,11 +446,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // One thread issues every MMA / copy / commit (FA_SV_SINGLE_ISSUE), or
       // the whole warp runs the loop and an elected lane issues.
       // The instruction descriptor must be a compile-time constant: a runtime
-      // one costs about 40 extra cycles per MMA.  Full tiles (N = 128) and
-      // the half tile at a piece end (N = 64) get separate loops.
+      // one costs about 40 extra cycles per MMA.
       if (SV_ISSUER) {
       constexpr uint32_t kIdesc128 = umma_idesc_f16(128, 128, fmt, 0);
-      constexpr uint32_t kIdesc64 = umma_idesc_f16(128, 64, fmt, 0);
       const uint64_t ring_desc = smem_desc_sw128(ring, 16, 1024);
       const uint64_t rope_desc = smem_desc_sw128(qrope, 16, 1024);
       auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
@@ -525,10 +523,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (!ok) break;
           tc_fence_after();  // the softmax's tcgen05.ld of this buffer precede the new QK
           SV_TRACE(2, g);
-          if (pc.tok_end - tok > kBlk)
-            ok = qk_tile(std::integral_constant<uint32_t, kIdesc128>{}, sd, rope_a);
-          else
-            ok = qk_tile(std::integral_constant<uint32_t, kIdesc64>{}, sd, rope_a);
+          // A half tile at a piece end (only its first 64 key rows loaded)
+          // runs the same N = 128 MMAs: the other 64 rows of the ring slot
+          // hold stale but valid bytes, and their score columns are masked
+          // (select) by the softmax.  One instantiation keeps the loop small.
+          ok = qk_tile(std::integral_constant<uint32_t, kIdesc128>{}, sd, rope_a);
           if (!ok) break;
           SV_TRACE(3, g);
 #ifdef FA_TRACE
