@@ -298,7 +298,7 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs,
                          "unit": "GB/s", "frac": achieved / peak_gbs,
                          "traffic": traffic, "peak_source": peak_kind,
-                         "kernel": "mla_decode_tc_kernel<bf16,64,dense>",
+                         "kernel": "sv::mla_decode_sv_kernel<bf16> (score/value CTA pair)",
                          "algorithmic_bytes_per_launch": bytes_local},
             "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
