@@ -47,13 +47,13 @@ constexpr int kRing = 9;
 constexpr int kVRows = 32;                          // tokens per V stage
 constexpr int kVChunkBytes = kVRows * kRowBytes;    // 4 KB: 32 rows x 64 dims
 constexpr int kVStageBytes = 8 * kVChunkBytes;      // 32 KB: 512 dims
-constexpr int kVStages = 4;
+constexpr int kVStages = 3;
 constexpr int kPBytes = kRows * kRowBytes;          // 16 KB: P of one 64-token block
 constexpr int kMetaAlpha = kPBytes;                 // f32[128] O rescale factors
 constexpr int kMetaFlags = kPBytes + 512;           // int[4] "rows of quadrant q rescale"
 constexpr int kMetaInvL = kPBytes + 1024;           // f32[128] 1 / row sum (last block)
 constexpr int kPSlotBytes = kPBytes + 2048;         // 18 KB
-constexpr int kPSlots = 3;
+constexpr int kPSlots = 4;
 constexpr uint32_t kColQ = 0, kColS = 256, kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;           // log2 units (factor 256)
 // MMA issue: one thread (default) or the whole warp with elect.sync.
@@ -93,8 +93,8 @@ constexpr int kOffRed = kOffRing + kRing * kChunkBytes;     // 2 KB row maxima /
 constexpr int kOffStgP = kOffRed + 2048;                    // 2 x 16 KB P staging
 constexpr int kSmemScore = kOffStgP + 2 * kPBytes;
 // value CTA
-constexpr int kOffV = kOffData;                             // 4 x 32 KB
-constexpr int kOffP = kOffV + kVStages * kVStageBytes;      // 3 x 18 KB
+constexpr int kOffV = kOffData;                             // 3 x 32 KB
+constexpr int kOffP = kOffV + kVStages * kVStageBytes;      // 4 x 18 KB
 constexpr int kStageWarpBytes = 32 * 128;                   // epilogue staging per warp
 constexpr int kOffStage = kOffP + kPSlots * kPSlotBytes;    // 8 x 4 KB
 constexpr int kSmemValue = kOffStage + 8 * kStageWarpBytes;
@@ -196,11 +196,13 @@ __device__ __forceinline__ int seq_len(const Params &p, int b) {
 }
 
 // Piece i of a part (tile_meta row: begin batch, begin block, end batch, end
-// block, split index of the first piece, number of pieces).
-__device__ __forceinline__ Piece get_piece(const Params &p, const int32_t *meta, int i) {
+// block, split index of the first piece, number of pieces).  Out of line:
+// every role walks the pieces, once per piece.
+__device__ __noinline__ Piece get_piece_at(const int32_t *seq_lens, int n_ctx,
+                                           const int32_t *meta, int i) {
   Piece pc;
   pc.b = meta[0] + i;
-  const int len = seq_len(p, pc.b);
+  const int len = seq_lens ? seq_lens[pc.b] : n_ctx;
   const int nblk = len > 0 ? (len + kBlk - 1) / kBlk : 0;
   const int lo = (i == 0) ? meta[1] : 0;
   const int hi = (pc.b == meta[2]) ? meta[3] : nblk;
@@ -208,6 +210,9 @@ __device__ __forceinline__ Piece get_piece(const Params &p, const int32_t *meta,
   pc.tok_end = min(hi * kBlk, max(len, 0));
   pc.split_idx = (i == 0) ? meta[4] : 0;
   return pc;
+}
+__device__ __forceinline__ Piece get_piece(const Params &p, const int32_t *meta, int i) {
+  return get_piece_at(p.seq_lens, p.n_ctx, meta, i);
 }
 
 // TMA coordinates (row in page, page) of token t of sequence b.
@@ -297,6 +302,131 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Cold paths, kept out of line.  The kernel holds every role of both CTAs
+// in one function; code that runs once per piece (or rarely) would otherwise
+// share the instruction cache with the per-tile loops of the warps next to it.
+
+// O[row, 256 ch + 0 .. 256) *= a for the calling warp's 32 rows (O rescale
+// after the running max grew).
+__device__ __noinline__ void rescale_o_half(uint32_t trow_col0, float a) {
+#pragma unroll 1
+  for (int c = 0; c < 8; ++c) {
+    const uint32_t col = trow_col0 + c * 32;
+    float v[32];
+    tmem_ld32(col, v);
+    tmem_wait_ld();
+    uint32_t w0[16], w1[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      w0[j] = __float_as_uint(v[j] * a);
+      w1[j] = __float_as_uint(v[16 + j] * a);
+    }
+    tmem_st16(col, w0);
+    tmem_st16(col + 16, w1);
+  }
+  tmem_wait_st();
+}
+
+// Zero rows [lo, kVRows) of a V stage (all 8 chunks); 256 threads, index tt.
+__device__ __noinline__ void clear_v_rows(uint8_t *stage, int lo, int tt) {
+  const int units = (kVRows - lo) * 64;  // 8 chunks x 8 16-byte units per row
+  for (int u = tt; u < units; u += 256) {
+    const int r = lo + (u >> 6);
+    const int rem = u & 63;
+    *reinterpret_cast<uint4 *>(stage + (rem >> 3) * kVChunkBytes + r * kRowBytes + (rem & 7) * 16) =
+        make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// Epilogue of one piece for the calling warp: rows q4 * 32 .. +31 of the
+// query block, output dims [256 ch, 256 ch + 256): O / l from TMEM (zeros when
+// the piece had no keys) to `obase`.  Each warp stages 32 rows x 128 bytes in
+// shared memory (16-byte units XOR-swizzled by row) and writes them back
+// four whole rows per store instruction.  row_base(r) is the byte offset of
+// flat query row r, or -1 when the row is absent.
+struct OutRows {
+  uint8_t *base;
+  int64_t sb, ss, sh;  // final output strides (elements); split: row stride
+  int b, h_q, row0, n_rows;
+  int esz;             // bytes per output element
+  bool split;          // f32 split workspace row (slot * rows_total + flat) * d_v
+  int64_t split_row0;  // slot * rows_total
+  int d_v;
+};
+
+template <typename T>
+__device__ __noinline__ void write_o_half(uint32_t trow, int ch, int q4, int lane, uint32_t stg_s,
+                                          bool has_tiles, float inv_l, const OutRows o) {
+  int64_t row_off[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int tr = q4 * 32 + 4 * k + (lane >> 3);
+    const int fl = o.row0 + tr;
+    if (tr >= o.n_rows) {
+      row_off[k] = -1;
+    } else if (!o.split) {
+      const int st_ = fl / o.h_q, hh = fl % o.h_q;
+      row_off[k] = (o.b * o.sb + st_ * o.ss + hh * o.sh) * o.esz;
+    } else {
+      row_off[k] = (o.split_row0 + fl) * o.d_v * 4;
+    }
+  }
+  const int cols_it = 128 / o.esz;  // output dims per 128-byte row segment
+#pragma unroll 1
+  for (int c0 = 0; c0 < 256; c0 += cols_it) {
+    const int col = ch * 256 + c0;
+    uint32_t w[32];
+    if (o.esz == 4) {
+      float v[32];
+      if (has_tiles) {
+        tmem_ld32(trow + col, v);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j] * inv_l);
+    } else {
+      float v0[32], v1[32];
+      if (has_tiles) {
+        tmem_ld32(trow + col, v0);
+        tmem_ld32(trow + col + 32, v1);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v0[j] = v1[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        w[j] = Elem<T>::pack2(v0[2 * j] * inv_l, v0[2 * j + 1] * inv_l);
+        w[16 + j] = Elem<T>::pack2(v1[2 * j] * inv_l, v1[2 * j + 1] * inv_l);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                       stg_s + lane * 128 + ((u ^ (lane & 7)) << 4)),
+                   "r"(w[4 * u]), "r"(w[4 * u + 1]), "r"(w[4 * u + 2]), "r"(w[4 * u + 3])
+                   : "memory");
+    __syncwarp();
+    const int j = lane & 7;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int r = 4 * k + (lane >> 3);
+      uint4 val;
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
+                   : "r"(stg_s + r * 128 + ((j ^ (r & 7)) << 4))
+                   : "memory");
+      if (row_off[k] >= 0)
+        *reinterpret_cast<uint4 *>(o.base + row_off[k] + static_cast<int64_t>(col) * o.esz + j * 16) = val;
+    }
+    __syncwarp();
+  }
 }
 
 template <typename T>
@@ -878,23 +1008,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               if (!ok) break;
               if (fl[q4]) {
                 tc_fence_after();
-                const float a = reinterpret_cast<const float *>(slotp + kMetaAlpha)[t];
-#pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
-                  const uint32_t col = ch * 256 + c * 32;
-                  float v[32];
-                  tmem_ld32(trow + col, v);
-                  tmem_wait_ld();
-                  uint32_t w0[16], w1[16];
-#pragma unroll
-                  for (int j = 0; j < 16; ++j) {
-                    w0[j] = __float_as_uint(v[j] * a);
-                    w1[j] = __float_as_uint(v[16 + j] * a);
-                  }
-                  tmem_st16(trow + col, w0);
-                  tmem_st16(trow + col + 16, w1);
-                }
-                tmem_wait_st();
+                rescale_o_half(trow + ch * 256, reinterpret_cast<const float *>(slotp + kMetaAlpha)[t]);
               }
             }
           }
@@ -910,14 +1024,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->v_full[st]), (sv / kVStages) & 1,
                                                       abort_flag, p.status, kDevTimeoutSoftmax));
               if (!ok) break;
-              uint8_t *stage = smem + kOffV + st * kVStageBytes;
-              const int units = (kVRows - lo) * 64;  // 8 chunks x 8 16-byte units per row
-              for (int u = tt; u < units; u += 256) {
-                const int r = lo + (u >> 6);
-                const int rem = u & 63;
-                *reinterpret_cast<uint4 *>(stage + (rem >> 3) * kVChunkBytes + r * kRowBytes +
-                                           (rem & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
-              }
+              clear_v_rows(smem + kOffV + st * kVStageBytes, lo, tt);
             }
             if (!ok) break;
             fence_proxy_async_smem();
@@ -937,87 +1044,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (!ok) break;
           tc_fence_after();
         }
-        // O / l -> out (final) or the f32 split workspace.  Each warp stages
-        // 32 rows x 128 bytes in shared memory (16-byte units XOR-swizzled by
-        // row) and writes them back four whole rows per store instruction.
+        // O / l -> out (final) or the f32 split workspace
         const bool final_out = n_split == 1;
-        const bool f32_out = !final_out || p.out_f32;
-        const int esz = f32_out ? 4 : 2;
-        const int cols_it = 128 / esz;  // output dims per 128-byte row segment
-        uint8_t *stg = smem + kOffStage + (warp - 4) * kStageWarpBytes;
-        const uint32_t stg_s = smem_u32(stg);
-        int64_t row_off[8];  // byte offset of this lane's rows (4 k + lane / 8), -1 if absent
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int tr = q4 * 32 + 4 * k + (lane >> 3);
-          const int fl = row0 + tr;
-          if (tr >= n_rows) {
-            row_off[k] = -1;
-          } else if (final_out) {
-            const int st_ = fl / p.h_q, hh = fl % p.h_q;
-            row_off[k] = (pc.b * p.o_sb + st_ * p.o_ss + hh * p.o_sh) * esz;
-          } else {
-            row_off[k] = (static_cast<int64_t>(slot_o) * rows_total + fl) * p.d_v * 4;
-          }
-        }
-        uint8_t *obase = final_out ? static_cast<uint8_t *>(p.out) : reinterpret_cast<uint8_t *>(p.part_o);
+        OutRows o;
+        o.base = final_out ? static_cast<uint8_t *>(p.out) : reinterpret_cast<uint8_t *>(p.part_o);
+        o.sb = p.o_sb;
+        o.ss = p.o_ss;
+        o.sh = p.o_sh;
+        o.b = pc.b;
+        o.h_q = p.h_q;
+        o.row0 = row0;
+        o.n_rows = n_rows;
+        o.esz = (!final_out || p.out_f32) ? 4 : 2;
+        o.split = !final_out;
+        o.split_row0 = static_cast<int64_t>(slot_o) * rows_total;
+        o.d_v = p.d_v;
         if (tt == 0) SV_TRACE(1, 120 + i);
-#pragma unroll 1
-        for (int c0 = 0; c0 < 256; c0 += cols_it) {
-          const int col = ch * 256 + c0;
-          EPI_TRACE(0);
-          uint32_t w[32];
-          if (f32_out) {
-            float v[32];
-            if (has_tiles) {
-              tmem_ld32(trow + col, v);
-              tmem_wait_ld();
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = 0.f;
-            }
-#pragma unroll
-            for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j] * inv_l);
-          } else {
-            float v0[32], v1[32];
-            if (has_tiles) {
-              tmem_ld32(trow + col, v0);
-              tmem_ld32(trow + col + 32, v1);
-              tmem_wait_ld();
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v0[j] = v1[j] = 0.f;
-            }
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              w[j] = Elem<T>::pack2(v0[2 * j] * inv_l, v0[2 * j + 1] * inv_l);
-              w[16 + j] = Elem<T>::pack2(v1[2 * j] * inv_l, v1[2 * j + 1] * inv_l);
-            }
-          }
-          EPI_TRACE(1);
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                             stg_s + lane * 128 + ((u ^ (lane & 7)) << 4)),
-                         "r"(w[4 * u]), "r"(w[4 * u + 1]), "r"(w[4 * u + 2]), "r"(w[4 * u + 3])
-                         : "memory");
-          __syncwarp();
-          EPI_TRACE(2);
-          const int j = lane & 7;
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int r = 4 * k + (lane >> 3);
-            uint4 val;
-            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
-                         : "r"(stg_s + r * 128 + ((j ^ (r & 7)) << 4))
-                         : "memory");
-            if (row_off[k] >= 0)
-              *reinterpret_cast<uint4 *>(obase + row_off[k] + static_cast<int64_t>(col) * esz + j * 16) = val;
-          }
-          EPI_TRACE(3);
-          __syncwarp();
-        }
+        write_o_half<T>(trow, ch, q4, lane, smem_u32(smem + kOffStage + (warp - 4) * kStageWarpBytes),
+                        has_tiles, inv_l, o);
         if (tt == 0) SV_TRACE(2, 120 + i);
         if (has_tiles) {
           tc_fence_before();
