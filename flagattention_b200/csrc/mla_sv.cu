@@ -748,15 +748,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             for (int c = 0; c < kBlk; ++c)
               if (c >= lim) sc[c] = -INFINITY;
           }
-          float mx[4];
+          // row maximum: three-input max in two chains (elements 0, 1 seed
+          // them, 2..61 in steps of four, then 62, 63)
+          static_assert(kBlk == 64, "max chain layout");
+          float mx0 = sc[0], mx1 = sc[1];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) mx[j] = sc[j];
-#pragma unroll
-          for (int c = 4; c < kBlk; c += 4) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) mx[j] = fmaxf(mx[j], sc[c + j]);
+          for (int c = 2; c < kBlk - 2; c += 4) {
+            mx0 = fmax3(mx0, sc[c], sc[c + 1]);
+            mx1 = fmax3(mx1, sc[c + 2], sc[c + 3]);
           }
-          float mraw = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+          float mraw = fmaxf(fmax3(mx0, sc[kBlk - 2], sc[kBlk - 1]), mx1);
           float *rslot = red + (g & 1u) * 2 * kRows;
           rslot[ch * kRows + t] = mraw;
           if (!(ok = pair_sync())) break;
@@ -772,16 +773,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             m_run = mt;
           }
           const float ms = (m_run == -INFINITY) ? 0.f : m_run;
-          float ps[4] = {0.f, 0.f, 0.f, 0.f};
+          // exponent argument and row sum in packed f32 pairs (one FFMA2 /
+          // FADD2 per two scores), exp2 per score, bf16 pair pack
+          const uint64_t sc2 = f32x2(p.scale_log2, p.scale_log2), nms2 = f32x2(-ms, -ms);
+          uint64_t ps2[2] = {f32x2(0.f, 0.f), f32x2(0.f, 0.f)};
           uint32_t pk[kBlk / 2];
 #pragma unroll
           for (int c = 0; c < kBlk; c += 2) {
-            const float p0 = fast_exp2(fmaf(sc[c], p.scale_log2, -ms));
-            const float p1 = fast_exp2(fmaf(sc[c + 1], p.scale_log2, -ms));
-            ps[(c >> 1) & 3] += p0 + p1;
+            float x0, x1;
+            f32x2_split(ffma2(f32x2(sc[c], sc[c + 1]), sc2, nms2), x0, x1);
+            const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+            const uint64_t pp = f32x2(p0, p1);
+            ps2[(c >> 1) & 1] = fadd2(ps2[(c >> 1) & 1], pp);
             pk[c / 2] = Elem<T>::pack2(p0, p1);
           }
-          l_half = l_half * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+          float s0, s1, s2, s3;
+          f32x2_split(ps2[0], s0, s1);
+          f32x2_split(ps2[1], s2, s3);
+          l_half = l_half * alpha + ((s0 + s1) + (s2 + s3));
           // P of this warp's block -> the value CTA's slot (gb + ch) % kPSlots
           const uint32_t pb = gb + ch;
           const uint32_t pslot = pb % kPSlots;
