@@ -45,6 +45,9 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="budget of the cpu_baseline sample")
+    p.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
+                   help="BASELINE config; 2 is the headline workload, 3-5 are timed on one "
+                        "GPU for the record (MTP causal, sparse top-k, 1M-token context)")
     return p.parse_args()
 
 
@@ -266,6 +269,11 @@ def run_ours(args):
         e2e_step(e2e_evs[i])
     torch.cuda.synchronize()
     e2e_ms = sum(e[0].elapsed_time(e[1]) for e in e2e_evs) / args.steps
+    # the end-to-end path computed the same outputs as the device-resident one
+    call.run()
+    torch.cuda.synchronize()
+    assert torch.allclose(out_h.float(), out.cpu().float(), atol=1e-2, rtol=1e-2), \
+        "end-to-end output differs from the device-resident decode"
     h2d = q.numel() * 2 + seq.numel() * 4 + bt.numel() * 4
     d2h = out.numel() * 2 + lse.numel() * 4
 
@@ -400,9 +408,128 @@ def run_reference(args):
     print(json.dumps(rec), flush=True)
 
 
+# ------------------------------------------------- configs 3-5 (one GPU)
+OTHER = {
+    3: dict(workload="mtp_causal_paged_mla_decode_b128_sq2_h128_ctx4k-32k-log_bf16",
+            B=128, s_q=2, causal=True, topk=0),
+    4: dict(workload="sparse_top2048_mla_decode_b64_h128_ctx32k-128k_bf16",
+            B=64, s_q=1, causal=False, topk=2048),
+    5: dict(workload="long_context_mla_decode_b2_h128_ctx1m_bf16",
+            B=2, s_q=1, causal=False, topk=0),
+}
+
+
+def other_lens(cfg):
+    rs = np.random.RandomState(SEED + cfg)
+    if cfg == 3:
+        return np.exp(rs.uniform(np.log(4096), np.log(32768), size=128)).astype(np.int32)
+    if cfg == 4:
+        return rs.randint(32768, 131073, size=64).astype(np.int32)
+    return np.array([1 << 20, 1 << 20], np.int32)
+
+
+def run_other(args):
+    """Decode + combine step of BASELINE config 3, 4 or 5 on one GPU: seeded
+    N(0,1) bf16 inputs made on the device, L2 flushed before each step,
+    CUDA events around the two kernels.  Bytes: every cache row the step
+    reads once (for top-k the gathered rows and the indices) + Q + O + LSE."""
+    import torch
+
+    import flagattention_b200 as fa
+    from flagattention_b200 import _torch as fat
+    from flagattention_b200.mla import MlaCall
+
+    spec = OTHER[args.config]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lens = other_lens(args.config)
+    B, s_q, topk = spec["B"], spec["s_q"], spec["topk"]
+    g = torch.Generator(device=dev).manual_seed(SEED + args.config)
+    pages_per = (lens + PAGE - 1) // PAGE
+    npages = int(pages_per.sum())
+    kcache = torch.empty((npages, PAGE, 1, D_QK), dtype=torch.bfloat16, device=dev)
+    for lo in range(0, npages, 8192):
+        hi = min(npages, lo + 8192)
+        kcache[lo:hi] = torch.randn((hi - lo, PAGE, 1, D_QK), generator=g, device=dev)
+    q = torch.randn((B, s_q, H_Q, D_QK), generator=g, device=dev, dtype=torch.bfloat16)
+    perm = np.random.RandomState(SEED + 100 + args.config).permutation(npages).astype(np.int32)
+    bt_np = np.zeros((B, int(pages_per.max())), np.int32)
+    off = 0
+    for i, k in enumerate(pages_per):
+        bt_np[i, :k] = perm[off:off + k]
+        off += k
+    bt = torch.from_numpy(bt_np).to(dev)
+    seq = torch.from_numpy(lens).to(dev)
+    idx = None
+    if topk:
+        rs = np.random.RandomState(SEED + 200)
+        idx_np = np.full((B, s_q, topk), -1, np.int32)
+        for b, n in enumerate(lens):
+            k = min(int(n), topk)
+            pos = np.sort(rs.choice(int(n), size=k, replace=False))
+            idx_np[b, 0, :k] = bt_np[b][pos // PAGE] * PAGE + pos % PAGE
+        idx = torch.from_numpy(idx_np).to(dev)
+    meta, splits = fa.get_mla_metadata(seq, s_q * H_Q, 1, num_heads_q=H_Q if topk else None,
+                                       topk=topk or None)
+    out = torch.empty((B, s_q, H_Q, D_V), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((B, H_Q, s_q), dtype=torch.float32, device=dev)
+    call = MlaCall(q, kcache, kcache.stride(0), kcache.stride(1), npages, PAGE, bt, seq, 0, meta,
+                   splits, out, lse, D_QK ** -0.5, causal=spec["causal"], indices=idx)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev):
+        flush.fill_(1)
+        ev[0].record(stream)
+        call.partial()
+        ev[1].record(stream)
+        call.combine()
+        ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        step([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    for i in range(args.steps):
+        step(evs[i])
+    torch.cuda.synchronize()
+    assert fat.read_status(dev) == 0, "device wait timeout in the timed region"
+    dec_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
+    step_ms = dec_ms + sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+    rows = int(np.minimum(lens, topk).sum()) if topk else int(lens.astype(np.int64).sum())
+    qo = B * s_q * H_Q * (D_QK * 2 + D_V * 2 + 4)
+    nbytes = rows * D_QK * 2 + qo + (B * s_q * topk * 4 if topk else 0)
+    flops = rows * 2 * s_q * H_Q * (D_QK + D_V)
+    peak_gbs, peak_tf, peak_kind = measured_peaks()
+    tokens = B * s_q
+    line = {"metric": METRIC, "value": tokens / (step_ms * 1e-3), "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16)",
+            "config": {"workload": spec["workload"], "baseline_config": args.config,
+                       "batch": B, "seq_q": s_q, "heads_q": H_Q, "topk": topk,
+                       "causal": spec["causal"], "page_size": PAGE,
+                       "l2": "flushed before every step (256 MB write, outside the events)"},
+            "ms_decode_kernel": dec_ms, "ms_combine_kernel": step_ms - dec_ms,
+            "roofline": {"bound": "hbm", "achieved": nbytes / (dec_ms * 1e-3) / 1e9,
+                         "peak": peak_gbs, "unit": "GB/s",
+                         "frac": nbytes / (dec_ms * 1e-3) / 1e9 / peak_gbs,
+                         "peak_source": peak_kind, "algorithmic_bytes_per_launch": nbytes},
+            "tensor_tflops_decode": flops / (dec_ms * 1e-3) / 1e12,
+            "tensor_frac_decode": flops / (dec_ms * 1e-3) / 1e12 / peak_tf,
+            "gpu_launches": 2 * args.steps}
+    print(json.dumps(line))
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.config != 2:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference arm is timed on the headline config only"}))
+        else:
+            run_other(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
