@@ -26,7 +26,7 @@ size_t generic_smem_bytes(int, int);
 cudaError_t launch_mla_tc(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                           const fa_mla_args *, int, int64_t, cudaStream_t);
 cudaError_t launch_mla_sv(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
-                          const fa_mla_args *, int, cudaStream_t);
+                          const CUtensorMap &, const fa_mla_args *, int, cudaStream_t);
 }  // namespace fa
 
 namespace {
@@ -94,6 +94,28 @@ int encode_map(CUtensorMap *map, const void *base, int dtype, uint64_t d, uint64
                 static_cast<int>(r), (unsigned long long)d, (unsigned long long)rows,
                 (unsigned long long)groups, (unsigned long long)strides[0],
                 (unsigned long long)strides[1]);
+  return FA_OK;
+}
+
+// 2-D map over every row of a paged latent pool ({576, rows}, one row per
+// box, 128-byte swizzle) for tile::gather4 loads of index-listed rows.
+int encode_gather_map(CUtensorMap *map, const void *base, int dtype, uint64_t rows,
+                      uint64_t row_stride_elems) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {576, rows};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {64, 1};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(map, dtype == FA_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   2, const_cast<void *>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FA_ERR_INVALID_ARGUMENT, "gather map rejected (code %d): rows %llu stride %llu B",
+                static_cast<int>(r), (unsigned long long)rows,
+                (unsigned long long)strides[0]);
   return FA_OK;
 }
 
@@ -358,10 +380,15 @@ int fa_mla_decode_partial(const fa_mla_args *a, void *stream) {
   const bool paged = a->block_table != nullptr;
   const uint64_t kv_rows = (sparse || paged) ? a->page_size : (a->n_ctx > 0 ? a->n_ctx : 1);
   const uint64_t kv_groups = (sparse || paged) ? a->num_pages : a->batch;
-  if (!sparse) {
-    // dense: score / value CTA kernel (query box 64 dims x 128 rows, key
-    // rows in 64-row boxes, value rows in 32-row boxes)
-    CUtensorMap qm, km, vm;
+  // Top-k rows go through the score / value kernel with tile::gather4 loads
+  // when every pool row lies at one stride (pages back to back); other pool
+  // layouts keep the head-dim-split kernel's per-row copies.
+  const bool uniform_rows =
+      sparse && a->kv_stride_page == static_cast<int64_t>(a->page_size) * a->kv_stride_tok;
+  if (!sparse || uniform_rows) {
+    // score / value CTA kernel (query box 64 dims x 128 rows, key rows in
+    // 64-row boxes, value rows in 32-row boxes; top-k: one-row gathers)
+    CUtensorMap qm, km, vm, gm;
     st = encode_map(&qm, a->q, a->dtype, 576, static_cast<uint64_t>(a->s_q) * a->h_q, a->batch,
                     a->q_stride_h, a->q_stride_b, 128, 64);
     if (st != FA_OK) return st;
@@ -371,7 +398,14 @@ int fa_mla_decode_partial(const fa_mla_args *a, void *stream) {
     st = encode_map(&vm, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
                     a->kv_stride_page, 32, 64);
     if (st != FA_OK) return st;
-    cudaError_t e = fa::launch_mla_sv(qm, km, vm, a, m_blocks, static_cast<cudaStream_t>(stream));
+    if (sparse) {
+      st = encode_gather_map(&gm, a->kcache, a->dtype,
+                             static_cast<uint64_t>(a->num_pages) * a->page_size, a->kv_stride_tok);
+      if (st != FA_OK) return st;
+    } else {
+      gm = qm;  // not read by the dense instance
+    }
+    cudaError_t e = fa::launch_mla_sv(qm, km, vm, gm, a, m_blocks, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? FA_OK : cuda_fail(e, "MLA decode launch");
   }
   CUtensorMap qrm, km, krm;

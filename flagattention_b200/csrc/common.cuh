@@ -254,6 +254,17 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+// Four rows r0..r3 of a 2-D tensor map whose box is {inner, 1 row}, columns
+// [c0, c0 + inner), stored at dst + i * (inner bytes) in the map's swizzle.
+// c0 times the element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, uint32_t bar,
+                                            int c0, int r0, int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
 // Bring [src, src + bytes) into L2 without touching shared memory (16-byte
 // aligned address, size a multiple of 16).
 __device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {

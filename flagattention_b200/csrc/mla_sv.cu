@@ -36,6 +36,7 @@ namespace fa {
 namespace sv {
 
 constexpr int kRows = 128;
+constexpr int kGatherWarps = 7;                    // sparse: warps 0, 2, 3, 12-15 gather rows
 constexpr int kBlk = FA_MLA_BLOCK_N;                 // 64 tokens: scheduler block, one page box
 constexpr int kThreads = 512;
 constexpr int kRowBytes = 128;                      // 64 dims x 2 bytes (one 128-byte swizzle row)
@@ -125,6 +126,9 @@ struct Bars {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
+  // sparse: per tile (g % 4), one byte per 4-row group with the invalid-index
+  // bits of its key rows (row 4 group + j: bit j)
+  alignas(16) uint8_t inval[4][32];
 };
 static_assert(sizeof(Bars) <= kOffData, "barrier block");
 
@@ -185,14 +189,22 @@ struct Params {
   int32_t causal, paged, out_f32;
   float scale_log2;
   int32_t *status;
+  // top-k sparse decode: indices[b][s][topk] are global pool rows
+  // (page * page_size + offset); an index outside [0, total_rows) is masked
+  const int32_t *indices;
+  int64_t idx_sb, idx_ss;
+  int32_t topk;  // 0: dense
+  int64_t total_rows;
 };
 
 struct Piece {
   int b, tok0, tok_end, split_idx;
 };
 
+// Length of sequence b's key list: its context (dense) or topk (sparse, the
+// positions of its index list).
 __device__ __forceinline__ int seq_len(const Params &p, int b) {
-  return p.seq_lens ? p.seq_lens[b] : p.n_ctx;
+  return p.topk ? p.topk : (p.seq_lens ? p.seq_lens[b] : p.n_ctx);
 }
 
 // Piece i of a part (tile_meta row: begin batch, begin block, end batch, end
@@ -212,7 +224,35 @@ __device__ __noinline__ Piece get_piece_at(const int32_t *seq_lens, int n_ctx,
   return pc;
 }
 __device__ __forceinline__ Piece get_piece(const Params &p, const int32_t *meta, int i) {
-  return get_piece_at(p.seq_lens, p.n_ctx, meta, i);
+  return p.topk ? get_piece_at(nullptr, p.topk, meta, i) : get_piece_at(p.seq_lens, p.n_ctx, meta, i);
+}
+
+// Sparse: pool rows of index-list positions pos .. pos + 3 (-1 past `end`).
+__device__ __forceinline__ void load_rows4(const int32_t *idx, int pos, int end, int (&r)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) r[j] = (pos + j < end) ? __ldg(idx + pos + j) : -1;
+}
+
+// Sparse: this lane's invalid-row bits (row j invalid: bit j), with every
+// invalid row replaced by the first valid row of the warp's rows (real cache
+// bytes: the softmax masks the column, the value product then adds 0 times a
+// finite row).  Pool row 0 stands in when none of the warp's rows is valid.
+__device__ __forceinline__ uint32_t fix_rows4(int (&r)[4], int64_t total_rows) {
+  uint32_t bad = 0;
+  int first = -1;
+#pragma unroll
+  for (int j = 3; j >= 0; --j) {
+    if (r[j] >= 0 && r[j] < total_rows)
+      first = r[j];
+    else
+      bad |= 1u << j;
+  }
+  const unsigned has = __ballot_sync(0xffffffffu, first >= 0);
+  const int sub = has ? __shfl_sync(0xffffffffu, first, __ffs(has) - 1) : 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if ((bad >> j) & 1u) r[j] = sub;
+  return bad;
 }
 
 // TMA coordinates (row in page, page) of token t of sequence b.
@@ -429,11 +469,12 @@ __device__ __noinline__ void write_o_half(uint32_t trow, int ch, int q4, int lan
   }
 }
 
-template <typename T>
+template <typename T, bool kSparse>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mla_decode_sv_kernel(const __grid_constant__ CUtensorMap q_map,
                          const __grid_constant__ CUtensorMap kv_map,
-                         const __grid_constant__ CUtensorMap v_map, const Params p) {
+                         const __grid_constant__ CUtensorMap v_map,
+                         const __grid_constant__ CUtensorMap g_map, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
@@ -452,8 +493,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int32_t *meta = p.tile_meta + static_cast<int64_t>(part) * FA_MLA_META_INTS;
   const int n_pieces = meta[5];
   const int rows_total = p.s_q * p.h_q;
-  const int row0 = mb * kRows;
-  const int n_rows = min(kRows, rows_total - row0);
+  // dense: 128 consecutive (s, h) rows; sparse: the h_q rows of query token
+  // mb (each token has its own index list)
+  const int row0 = kSparse ? mb * p.h_q : mb * kRows;
+  const int n_rows = kSparse ? p.h_q : min(kRows, rows_total - row0);
   constexpr int fmt = std::is_same<T, __half>::value ? 0 : 1;
 
   if (threadIdx.x == 0) {
@@ -502,8 +545,103 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ================================================================ score CTA
     const uint32_t ring = s_base + kOffRing;
     const uint32_t qrope = s_base + kOffQRope;
-    if (warp == 0) {
+    if (warp == 0 || (kSparse && (warp == 2 || warp == 3 || warp >= 12))) {
       // ---------------------------------------------------------- producer
+      if constexpr (kSparse) {
+        // Top-k rows: seven gather warps (0, 2, 3, 12-15), warp k owning row
+        // groups k, k + 7, ... (rows 4 group .. + 3 of a tile, one
+        // tile::gather4 per chunk: the TMA unit serialises the gathers of one
+        // warp, so spreading them over warps multiplies the row rate).  Every
+        // gather warp waits for each ring slot to be free; warp 0 also arms
+        // the slots, loads the query and gates each tile on the release of
+        // its S buffer.
+        const int gw = warp == 0 ? 0 : (warp <= 3 ? warp - 1 : warp - 9);
+        const int rg = gw + kGatherWarps * lane;  // this lane's row group (< 32)
+        const bool has_rg = rg < 32;
+        if (warp == 0 && lane == 0) {
+          tma_prefetch_desc(&q_map);
+          tma_prefetch_desc(&g_map);
+        }
+        RingPos rp;
+        uint32_t issued = 0, tg = 0;
+        int qi = 0;
+        bool ok = true;
+        auto take_slot = [&](uint32_t bytes) -> uint32_t {  // wait until free; warp 0 arms
+          uint32_t full = 0xffffffffu;
+          if (lane == 0 && mbar_wait(smem_u32(&bars->ch_empty[rp.slot]), rp.phase ^ 1, abort_flag,
+                                     p.status, kDevTimeoutProducer)) {
+            full = smem_u32(&bars->ch_full[rp.slot]);
+            if (warp == 0) mbar_arrive_expect_tx(full, bytes);
+          }
+          full = __shfl_sync(0xffffffffu, full, 0);
+          if (full != 0xffffffffu) ++issued;
+          return full;
+        };
+        for (int i = 0; i < n_pieces && ok; ++i) {
+          const Piece pc = get_piece(p, meta, i);
+          if (pc.tok_end <= pc.tok0) continue;
+          for (int c = 0; c < kQChunks; ++c) {  // latent Q: warp 0's slots
+            if (warp == 0) {
+              const uint32_t full = take_slot(kChunkBytes);
+              if (!(ok = full != 0xffffffffu)) break;
+              if (lane == 0)
+                tma_load_3d(ring + rp.slot * kChunkBytes, &q_map, full, 64 * c, row0, pc.b);
+            }
+            rp.next();
+          }
+          if (!ok) break;
+          if (warp == 0) {
+            bool okr = true;
+            if (lane == 0) {
+              okr = mbar_wait(smem_u32(&bars->rope_empty[qi & 1]), ((qi >> 1) & 1) ^ 1, abort_flag,
+                              p.status, kDevTimeoutProducer);
+              if (okr) {
+                mbar_arrive_expect_tx(smem_u32(&bars->rope_full[qi & 1]), kChunkBytes);
+                tma_load_3d(qrope + (qi & 1) * kChunkBytes, &q_map,
+                            smem_u32(&bars->rope_full[qi & 1]), 512, row0, pc.b);
+              }
+            }
+            if (!(ok = __shfl_sync(0xffffffffu, okr ? 1 : 0, 0) != 0)) break;
+          }
+          ++qi;
+          const int32_t *idx = p.indices + static_cast<int64_t>(pc.b) * p.idx_sb +
+                               static_cast<int64_t>(mb) * p.idx_ss;
+          int nr[4] = {-1, -1, -1, -1};  // the next tile's rows, loaded one tile ahead
+          if (has_rg) load_rows4(idx, pc.tok0 + 4 * rg, pc.tok_end, nr);
+          for (int tok = pc.tok0; tok < pc.tok_end && ok; tok += 2 * kBlk, ++tg) {
+            const int n_blk = (pc.tok_end - tok > kBlk) ? 2 : 1;
+            int r[4] = {nr[0], nr[1], nr[2], nr[3]};
+            if (has_rg && tok + 2 * kBlk < pc.tok_end)
+              load_rows4(idx, tok + 2 * kBlk + 4 * rg, pc.tok_end, nr);
+            const uint32_t bad = fix_rows4(r, p.total_rows);
+            if (has_rg) bars->inval[tg & 3u][rg] = static_cast<uint8_t>(bad);
+            if (warp == 0) {  // S buffer release before the tile's first chunk is armed
+              bool okw = true;
+              if (lane == 0)
+                okw = mbar_wait(smem_u32(&bars->s_empty[tg & 1u]), ((tg >> 1) & 1u) ^ 1u, abort_flag,
+                                p.status, kDevTimeoutProducer);
+              if (!(ok = __shfl_sync(0xffffffffu, okw ? 1 : 0, 0) != 0)) break;
+            }
+            __syncwarp();
+            for (int c = 0; c < kKChunks; ++c) {
+              const uint32_t full = take_slot(n_blk * kBoxBytes);
+              if (!(ok = full != 0xffffffffu)) break;
+              if (has_rg && rg < n_blk * 16)
+                tma_gather4(ring + rp.slot * kChunkBytes + rg * 4 * kRowBytes, &g_map, full,
+                            64 * c, r[0], r[1], r[2], r[3]);
+              rp.next();
+            }
+          }
+        }
+        if (*abort_flag && warp == 0 && lane == 0) {  // copies in flight land before exit
+          volatile int never = 0;
+          for (uint32_t t = issued > kRing ? issued - kRing : 0; t < issued; ++t)
+            mbar_wait(smem_u32(&bars->ch_full[t % kRing]), (t / kRing) & 1, &never, nullptr, 0);
+          if (qi > 0)
+            mbar_wait(smem_u32(&bars->rope_full[(qi - 1) & 1]), ((qi - 1) >> 1) & 1, &never,
+                      nullptr, 0);
+        }
+      } else {
       if (lane == 0) {
         tma_prefetch_desc(&q_map);
         tma_prefetch_desc(&kv_map);
@@ -575,6 +713,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_wait(smem_u32(&bars->rope_full[(qi - 1) & 1]), ((qi - 1) >> 1) & 1, &never,
                       nullptr, 0);
         }
+      }
       }
       __syncwarp();
     } else if (warp == 1) {
@@ -749,6 +888,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               sc[32 + j] = v1[j];
             }
           }
+          // sparse: this block's invalid-row bits (row groups 16 ch .. 16 ch +
+          // 15), read before the S buffer is released (the tile whose rows
+          // reuse the slot cannot start gathering before that release)
+          uint4 bad4 = make_uint4(0u, 0u, 0u, 0u);
+          if constexpr (kSparse) bad4 = *reinterpret_cast<const uint4 *>(&bars->inval[g & 3u][16 * ch]);
           tc_fence_before();
           mbar_arrive(smem_u32(&bars->s_empty[buf]));
           // mask columns past the sequence / causal end (select: NaN-safe)
@@ -757,6 +901,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int c = 0; c < kBlk; ++c)
               if (c >= lim) sc[c] = -INFINITY;
+          }
+          if constexpr (kSparse) {
+            // column c = block row 4 k + j: bit j of byte k (word k / 4)
+            if (bad4.x | bad4.y | bad4.z | bad4.w) {
+              const uint32_t bw[4] = {bad4.x, bad4.y, bad4.z, bad4.w};
+#pragma unroll
+              for (int c = 0; c < kBlk; ++c)
+                if ((bw[c >> 4] >> (8 * ((c >> 2) & 3) + (c & 3))) & 1u) sc[c] = -INFINITY;
+            }
           }
           // row maximum: three-input max in two chains (elements 0, 1 seed
           // them, 2..61 in steps of four, then 62, 63)
@@ -875,8 +1028,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ================================================================ value CTA
     const uint32_t vbase = s_base + kOffV;
     const uint32_t pbase = s_base + kOffP;
-    if (warp == 0) {
+    if (warp == 0 || (kSparse && (warp == 2 || warp == 3 || warp >= 12))) {
       // ------------------------------------------------------- V producer
+      if constexpr (kSparse) {
+        // Top-k rows: the seven gather warps (0, 2, 3, 12-15) split the 64
+        // (value chunk, 4-row group) gathers of every 32-row stage, pair
+        // q = warp index + 7 lane: chunk q / 8, rows 4 (q % 8) .. + 3.  Each
+        // gather warp waits for the stage to be free; warp 0 arms it.
+        const int gw = warp == 0 ? 0 : (warp <= 3 ? warp - 1 : warp - 9);
+        const int q = gw + kGatherWarps * lane;
+        const bool has_q = q < 64;
+        const int d = q >> 3, rg = q & 7;
+        if (warp == 0 && lane == 0) tma_prefetch_desc(&g_map);
+        uint32_t vs = 0;
+        bool ok = true;
+        for (int i = 0; i < n_pieces && ok; ++i) {
+          const Piece pc = get_piece(p, meta, i);
+          const int32_t *idx = p.indices + static_cast<int64_t>(pc.b) * p.idx_sb +
+                               static_cast<int64_t>(mb) * p.idx_ss;
+          // stages start at tok0, tok0 + 32, ... (< tok_end); their rows are
+          // loaded two stages ahead
+          int n1[4] = {-1, -1, -1, -1}, n2[4] = {-1, -1, -1, -1};
+          if (has_q) {
+            load_rows4(idx, pc.tok0 + 4 * rg, pc.tok_end, n1);
+            load_rows4(idx, pc.tok0 + kVRows + 4 * rg, pc.tok_end, n2);
+          }
+          for (int bt = pc.tok0; bt < pc.tok_end && ok; bt += kBlk) {
+            const int vb = min(kBlk, pc.tok_end - bt);
+            const int n_sub = vb > kVRows ? 2 : 1;
+            for (int j = 0; j < n_sub; ++j, ++vs) {
+              int r[4] = {n1[0], n1[1], n1[2], n1[3]};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) n1[k] = n2[k];
+              const int ahead = bt + kVRows * (j + 2);
+              if (has_q && ahead < pc.tok_end) load_rows4(idx, ahead + 4 * rg, pc.tok_end, n2);
+              fix_rows4(r, p.total_rows);
+              const int st = vs % kVStages;
+              const uint32_t full = smem_u32(&bars->v_full[st]);
+              bool okw = true;
+              if (lane == 0) {
+                okw = mbar_wait(smem_u32(&bars->v_empty[st]), ((vs / kVStages) & 1) ^ 1, abort_flag,
+                                p.status, kDevTimeoutProducer);
+                if (okw && warp == 0) mbar_arrive_expect_tx(full, kVStageBytes);
+              }
+              if (!(ok = __shfl_sync(0xffffffffu, okw ? 1 : 0, 0) != 0)) break;
+              if (has_q)
+                tma_gather4(vbase + st * kVStageBytes + d * kVChunkBytes + rg * 4 * kRowBytes,
+                            &g_map, full, 64 * d, r[0], r[1], r[2], r[3]);
+            }
+          }
+        }
+        if (*abort_flag && warp == 0 && lane == 0) {
+          volatile int never = 0;
+          for (uint32_t t = vs > kVStages ? vs - kVStages : 0; t < vs; ++t)
+            mbar_wait(smem_u32(&bars->v_full[t % kVStages]), (t / kVStages) & 1, &never, nullptr,
+                      0);
+        }
+      } else {
       if (lane == 0) {
         tma_prefetch_desc(&v_map);
         uint32_t vs = 0, vbk = 0xffffffffu;
@@ -918,6 +1126,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_wait(smem_u32(&bars->v_full[t % kVStages]), (t / kVStages) & 1, &never, nullptr,
                       0);
         }
+      }
       }
       __syncwarp();
     } else if (warp == 1) {
@@ -1127,8 +1336,25 @@ extern "C" int fa_debug_sv_trace_read(void *dst, size_t bytes) {
 // q_map: query (box 64 dims x 128 rows), kv_map: key rows (box 64 x 64),
 // v_map: value rows (box 64 x 32); all 128-byte swizzle over the same layouts
 // as the reference's caches ([pages, page, 1, 576]).
+namespace {
+template <typename T, bool kSparse>
+cudaError_t launch_sv_t(const CUtensorMap &qm, const CUtensorMap &km, const CUtensorMap &vm,
+                        const CUtensorMap &gm, const sv::Params &p, dim3 grid,
+                        cudaStream_t stream) {
+  auto kern = sv::mla_decode_sv_kernel<T, kSparse>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       sv::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, sv::kThreads, sv::kSmemBytes, stream>>>(qm, km, vm, gm, p);
+  return cudaGetLastError();
+}
+}  // namespace
+
+// gm: 2-D gather map over every pool row ({576, num_pages * page_size},
+// box {64, 1}); read only by the top-k instance (indices != nullptr).
 cudaError_t launch_mla_sv(const CUtensorMap &qm, const CUtensorMap &km, const CUtensorMap &vm,
-                          const fa_mla_args *a, int m_blocks, cudaStream_t stream) {
+                          const CUtensorMap &gm, const fa_mla_args *a, int m_blocks,
+                          cudaStream_t stream) {
   sv::Params p;
   p.kcache = static_cast<const uint8_t *>(a->kcache);
   p.kv_sp = a->kv_stride_page;
@@ -1159,20 +1385,18 @@ cudaError_t launch_mla_sv(const CUtensorMap &qm, const CUtensorMap &km, const CU
   p.out_f32 = a->out_dtype == FA_DTYPE_F32;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.status = a->status;
+  const bool sparse = a->indices != nullptr;
+  p.indices = a->indices;
+  p.idx_sb = a->idx_stride_b;
+  p.idx_ss = a->idx_stride_s;
+  p.topk = sparse ? a->topk : 0;
+  p.total_rows = static_cast<int64_t>(a->num_pages) * a->page_size;
   const dim3 grid(2 * a->num_sm_parts, m_blocks);
-  cudaError_t e;
-  if (a->dtype == FA_DTYPE_F16) {
-    auto kern = sv::mla_decode_sv_kernel<__half>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sv::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    kern<<<grid, sv::kThreads, sv::kSmemBytes, stream>>>(qm, km, vm, p);
-  } else {
-    auto kern = sv::mla_decode_sv_kernel<__nv_bfloat16>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sv::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    kern<<<grid, sv::kThreads, sv::kSmemBytes, stream>>>(qm, km, vm, p);
-  }
-  return cudaGetLastError();
+  if (a->dtype == FA_DTYPE_F16)
+    return sparse ? launch_sv_t<__half, true>(qm, km, vm, gm, p, grid, stream)
+                  : launch_sv_t<__half, false>(qm, km, vm, gm, p, grid, stream);
+  return sparse ? launch_sv_t<__nv_bfloat16, true>(qm, km, vm, gm, p, grid, stream)
+                : launch_sv_t<__nv_bfloat16, false>(qm, km, vm, gm, p, grid, stream);
 }
 
 }  // namespace fa
