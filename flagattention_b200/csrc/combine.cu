@@ -23,54 +23,71 @@ __device__ __forceinline__ void store4(T *dst, float4 v) {
 
 // Merge `n` partial rows located at part_o[slot(s) * slot_stride + row_off]
 // (and part_lse[slot(s) * lse_stride + row]).  Returns the merged lse.
+// Partials go in groups of four: a group's LSEs and value rows are all loaded
+// before any is used, and the groups are folded with a running maximum, so a
+// warp waits for one memory round trip per group (for the usual 2-3 splits,
+// one in all) instead of one for the LSEs and then one per partial.
 template <typename T>
 __device__ __forceinline__ float merge_row(const float *__restrict__ part_o,
                                            const float *__restrict__ part_lse, int first_slot,
                                            int n, int64_t o_slot_stride, int64_t lse_slot_stride,
                                            int64_t o_row_off, int64_t lse_row, int d_v, T *out,
                                            int lane) {
-  float m = -INFINITY;
-  for (int s = lane; s < n; s += 32)
-    m = fmaxf(m, part_lse[(first_slot + s) * lse_slot_stride + lse_row]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  const float msafe = (m == -INFINITY) ? 0.f : m;
-  float z = 0.f;
-  for (int s = lane; s < n; s += 32)
-    z += __expf(part_lse[(first_slot + s) * lse_slot_stride + lse_row] - msafe);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-  const float lse = (z > 0.f) ? msafe + __logf(z) : -INFINITY;
-  // Each lane owns up to 4 float4 columns (d = 4 lane + 128 k).  All of a
-  // partial's loads are issued before they are used, and two partials are
-  // in flight at a time, so the warp keeps ~8 loads outstanding per lane.
+  constexpr int kGroup = 4;
+  float m = -INFINITY, z = 0.f;  // running maximum and sum of exp(lse_s - m)
+  // Each lane owns up to 4 float4 columns (d = 4 lane + 128 k).
   float4 acc[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 2
-  for (int s = 0; s < n; ++s) {
-    const float ls = part_lse[(first_slot + s) * lse_slot_stride + lse_row];
-    const float w = (lse == -INFINITY || ls == -INFINITY) ? 0.f : __expf(ls - lse);
-    const float *src = part_o + (first_slot + s) * o_slot_stride + o_row_off;
-    float4 v[4];
+  for (int s0 = 0; s0 < n; s0 += kGroup) {
+    float ls[kGroup];
+    float4 v[kGroup][4];
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+      const bool live = s0 + g < n;
+      ls[g] = live ? __ldg(part_lse + (first_slot + s0 + g) * lse_slot_stride + lse_row) : -INFINITY;
+      const float *src = part_o + (first_slot + s0 + g) * o_slot_stride + o_row_off;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int d = lane * 4 + k * 128;
+        v[g][k] = (live && d < d_v) ? __ldg(reinterpret_cast<const float4 *>(src + d))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float mg = m;
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) mg = fmaxf(mg, ls[g]);
+    if (mg == -INFINITY) continue;  // nothing but empty partials so far
+    const float keep = (m == -INFINITY) ? 0.f : __expf(m - mg);
+    z *= keep;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int d = lane * 4 + k * 128;
-      v[k] = d < d_v ? __ldg(reinterpret_cast<const float4 *>(src + d))
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
+      acc[k].x *= keep;
+      acc[k].y *= keep;
+      acc[k].z *= keep;
+      acc[k].w *= keep;
     }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      acc[k].x += w * v[k].x;
-      acc[k].y += w * v[k].y;
-      acc[k].z += w * v[k].z;
-      acc[k].w += w * v[k].w;
+    for (int g = 0; g < kGroup; ++g) {
+      const float w = (ls[g] == -INFINITY) ? 0.f : __expf(ls[g] - mg);
+      z += w;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        acc[k].x += w * v[g][k].x;
+        acc[k].y += w * v[g][k].y;
+        acc[k].z += w * v[g][k].z;
+        acc[k].w += w * v[g][k].w;
+      }
     }
+    m = mg;
   }
+  const float lse = (z > 0.f) ? m + __logf(z) : -INFINITY;
+  const float inv = (z > 0.f) ? 1.f / z : 0.f;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int d = lane * 4 + k * 128;
-    if (d < d_v) store4<T>(out + d, acc[k]);
+    const float4 o = make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
+    if (d < d_v) store4<T>(out + d, o);
   }
   return lse;
 }
