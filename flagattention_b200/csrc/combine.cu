@@ -23,17 +23,19 @@ __device__ __forceinline__ void store4(T *dst, float4 v) {
 
 // Merge `n` partial rows located at part_o[slot(s) * slot_stride + row_off]
 // (and part_lse[slot(s) * lse_stride + row]).  Returns the merged lse.
-// Partials go in groups of four: a group's LSEs and value rows are all loaded
+// Partials go in groups of two: a group's LSEs and value rows are all loaded
 // before any is used, and the groups are folded with a running maximum, so a
-// warp waits for one memory round trip per group (for the usual 2-3 splits,
-// one in all) instead of one for the LSEs and then one per partial.
+// warp waits for one memory round trip per group instead of one for the LSEs
+// and then one per partial.  Two, not more: the merge is latency-bound on
+// partials that come from DRAM, and a 64-register budget (eight 4-warp blocks
+// per SM) hides more latency than more loads in flight per warp.
 template <typename T>
 __device__ __forceinline__ float merge_row(const float *__restrict__ part_o,
                                            const float *__restrict__ part_lse, int first_slot,
                                            int n, int64_t o_slot_stride, int64_t lse_slot_stride,
                                            int64_t o_row_off, int64_t lse_row, int d_v, T *out,
                                            int lane) {
-  constexpr int kGroup = 4;
+  constexpr int kGroup = 2;
   float m = -INFINITY, z = 0.f;  // running maximum and sum of exp(lse_s - m)
   // Each lane owns up to 4 float4 columns (d = 4 lane + 128 k).
   float4 acc[4];
@@ -95,7 +97,7 @@ __device__ __forceinline__ float merge_row(const float *__restrict__ part_o,
 // Generic: rows decomposed as (b, h, m) with h < H, m < M; every row has
 // num_parts partials laid out [part][rows][d_v]; lse out f32 [rows].
 template <typename T>
-__global__ void lse_combine_kernel(const float *__restrict__ part_o,
+__global__ void __launch_bounds__(128, 8) lse_combine_kernel(const float *__restrict__ part_o,
                                    const float *__restrict__ part_lse, int num_parts, int64_t rows,
                                    int H, int M, int d_v, T *__restrict__ out, int64_t o_sb,
                                    int64_t o_sh, int64_t o_sm, float *__restrict__ lse) {
@@ -114,7 +116,7 @@ __global__ void lse_combine_kernel(const float *__restrict__ part_o,
 // MLA: sequence b owns slots num_splits[b] .. num_splits[b+1]-1 of
 // part_o [slot][s_q*h_q][d_v]; single-piece sequences were written directly.
 template <typename T>
-__global__ void mla_combine_kernel(const float *__restrict__ part_o,
+__global__ void __launch_bounds__(128, 8) mla_combine_kernel(const float *__restrict__ part_o,
                                    const float *__restrict__ part_lse,
                                    const int32_t *__restrict__ num_splits, int s_q, int h_q,
                                    int d_v, T *__restrict__ out, int64_t o_sb, int64_t o_ss,
