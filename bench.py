@@ -48,6 +48,8 @@ def parse():
     p.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
                    help="BASELINE config; 2 is the headline workload, 3-5 are timed on one "
                         "GPU for the record (MTP causal, sparse top-k, 1M-token context)")
+    p.add_argument("--batch", type=int, default=0,
+                   help="configs 3-5: first N sequences only (smaller cases for profiling)")
     return p.parse_args()
 
 
@@ -443,7 +445,9 @@ def run_other(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     lens = other_lens(args.config)
-    B, s_q, topk = spec["B"], spec["s_q"], spec["topk"]
+    if args.batch:
+        lens = lens[:args.batch]
+    B, s_q, topk = len(lens), spec["s_q"], spec["topk"]
     g = torch.Generator(device=dev).manual_seed(SEED + args.config)
     pages_per = (lens + PAGE - 1) // PAGE
     npages = int(pages_per.sum())
