@@ -12,7 +12,7 @@ import torch
 import flagattention_b200 as fa
 import oracle
 from flagattention_b200 import _torch as fat
-from mla_cases import D_QK, D_V, assert_close, build_dense, build_sparse, to_dev
+from mla_cases import D_QK, D_V, PAGE, assert_close, build_dense, build_sparse, to_dev
 from inputs import digest, mla_inputs
 
 pytestmark = pytest.mark.gpu
@@ -136,6 +136,25 @@ def test_sparse_padding_and_out_of_range(parts):
     d["idx_np"][1, 0, 9] = 10 ** 9                   # out of range: masked too
     d["idx"] = to_dev(d["idx_np"])
     out, lse, _, _ = _decode(d, indices=d["idx"], topk=256, parts=parts)
+    want_o, want_l = oracle.mla_decode_sparse(d["q_np"], d["kc_np"], d["idx_np"], D_V, SCALE)
+    assert_close("out", out, want_o)
+    assert_close("lse", lse, want_l)
+
+
+def test_sparse_padded_pool_row_copy_route():
+    """Top-k over a pool whose pages are not back to back (64-row pages
+    allocated 65 rows apart, the spare rows NaN): no single row map covers it,
+    so the per-row copy kernel runs, against the same oracle."""
+    d = build_sparse(17, [300, 5000], topk=512, s_q=1, heads=128)
+    kc = d["kc"]
+    padded = torch.full((kc.shape[0], PAGE + 1, 1, D_QK), float("nan"), dtype=kc.dtype,
+                        device="cuda")
+    padded[:, :PAGE] = kc
+    d["kc"] = padded[:, :PAGE]
+    assert d["kc"].stride(0) != PAGE * d["kc"].stride(1)
+    d["idx_np"][1, 0, 3] = -1                        # a masked entry on this route too
+    d["idx"] = to_dev(d["idx_np"])
+    out, lse, _, _ = _decode(d, indices=d["idx"], topk=512)
     want_o, want_l = oracle.mla_decode_sparse(d["q_np"], d["kc_np"], d["idx_np"], D_V, SCALE)
     assert_close("out", out, want_o)
     assert_close("lse", lse, want_l)
