@@ -1,4 +1,5 @@
-// mla_sv.cu -- dense MLA decode on tcgen05 with a score CTA and a value CTA.
+// mla_sv.cu -- MLA decode (dense paged and top-k) on tcgen05 with a score CTA
+// and a value CTA.
 //
 // Problem: 128 query rows (query tokens x heads) share one latent key head of
 // 576 dims; values are the first 512 dims of the same rows.  The reference
@@ -10,23 +11,26 @@
 //   rank 0, the score CTA: latent Q (512 dims) in TMEM as the A operand, two
 //     128-column score buffers, S = Q K^T for 128-token tiles (N = 128), the
 //     online softmax, and P sent as bf16/f16 into the value CTA's shared
-//     memory with st.async (16 KB per 64 tokens, one direction);
+//     memory as one bulk DSMEM copy per 64 tokens (one direction);
 //   rank 1, the value CTA: O in all 512 TMEM columns, O += P V with P and V
 //     from shared memory.
 // Both CTAs read the key rows they need with their own TMA: the value CTA's
-// 512 dims of a row are an L2 hit after the score CTA's 576 (or the other way
-// round), so HBM sees each row about once.  Nothing travels back from the
-// value CTA except "slot free" arrivals (tcgen05.commit multicast).
+// 512 dims of a row are an L2 hit after the score CTA's 576, so HBM sees each
+// row about once.  Nothing travels back from the value CTA except "slot free"
+// arrivals (tcgen05.commit multicast).
 //
 // Score CTA (512 threads): warp 0 TMA producer (latent Q chunks and key
-// chunks through one 11-slot ring of 16 KB = 128 rows x 64 dims, rope Q in
-// two 16 KB buffers), warp 1 MMA issuer (also copies the latent Q chunks from
-// the ring into TMEM with tcgen05.cp), warps 4-11 softmax (two warps per 32
-// query rows, one per 64-token block of the tile).
+// chunks through one 9-slot ring of 16 KB = 128 rows x 64 dims, rope Q in two
+// 16 KB buffers; it also gates each tile on its S buffer's release), warp 1
+// MMA issuer (also copies the latent Q chunks from the ring into TMEM with
+// tcgen05.cp), warps 4-11 softmax (two warps per 32 query rows, one per
+// 64-token block of the tile).
 // Value CTA (512 threads): warp 0 TMA producer (V in 32-token stages of
 // 8 x 4 KB), warp 1 MMA issuer, warps 4-11 O rescaling, tail clearing and the
 // epilogue (two warps per 32 rows, one per 256 output dims; stores staged
 // through shared memory so that each store instruction writes whole rows).
+// Top-k instance (kSparse): rows come from index lists with tile::gather4,
+// issued by seven warps per CTA (0, 2, 3, 12-15); see the producer comments.
 // Every mbarrier wait is bounded (common.cuh); a timeout sets the device
 // status word and the kernel unwinds instead of hanging.
 #include "common.cuh"

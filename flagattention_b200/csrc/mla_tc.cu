@@ -1,4 +1,9 @@
-// mla_tc.cu -- tensor-core (tcgen05 / TMEM / TMA) MLA decode for sm_100a.
+// mla_tc.cu -- tensor-core (tcgen05 / TMEM / TMA) MLA decode for sm_100a,
+// head-dim-split design.  Launched only for top-k decode over a latent pool
+// whose pages are not back to back (page stride != page_size x token
+// stride), where one TMA row map cannot address every row and key rows are
+// copied row by row with cp.async instead.  Dense decode and top-k over
+// ordinary pools run on the score / value kernel (mla_sv.cu).
 //
 // Problem: 128 query rows (query tokens x heads) share one latent key head of
 // 576 dims; values are the first 512 dims of the same rows.  Per 64-token
@@ -893,14 +898,12 @@ cudaError_t launch_mla_tc(const CUtensorMap &qrm, const CUtensorMap &km, const C
   p.out_f32 = a->out_dtype == FA_DTYPE_F32;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.status = a->status;
-  const bool sparse = a->indices != nullptr;
-  const bool f16 = a->dtype == FA_DTYPE_F16;
-  if (f16) {
-    if (sparse) return launch_mla_t<__half, true>(qrm, km, krm, p, a->num_sm_parts, m_blocks, stream);
-    return launch_mla_t<__half, false>(qrm, km, krm, p, a->num_sm_parts, m_blocks, stream);
-  }
-  if (sparse) return launch_mla_t<__nv_bfloat16, true>(qrm, km, krm, p, a->num_sm_parts, m_blocks, stream);
-  return launch_mla_t<__nv_bfloat16, false>(qrm, km, krm, p, a->num_sm_parts, m_blocks, stream);
+  // Only the top-k instance is launched (dense decode and top-k over
+  // back-to-back pools run on the score / value kernel, mla_sv.cu).
+  if (a->indices == nullptr) return cudaErrorInvalidValue;
+  if (a->dtype == FA_DTYPE_F16)
+    return launch_mla_t<__half, true>(qrm, km, krm, p, a->num_sm_parts, m_blocks, stream);
+  return launch_mla_t<__nv_bfloat16, true>(qrm, km, krm, p, a->num_sm_parts, m_blocks, stream);
 }
 
 #ifdef FA_TRACE
