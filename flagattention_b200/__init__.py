@@ -12,7 +12,7 @@ Public operators (no CPU path: every call runs CUDA kernels of the in-tree
 """
 
 from flagattention_b200._lib import CudaError, InvalidArgument, Unsupported  # noqa: F401
-from flagattention_b200.mla import flash_mla_with_kvcache, get_mla_metadata  # noqa: F401
+from flagattention_b200.mla import append_kv_rows, flash_mla_with_kvcache, get_mla_metadata  # noqa: F401
 from flagattention_b200.paged import paged_attention  # noqa: F401
 from flagattention_b200.split_kv import flash_attention, flash_attention_split_kv  # noqa: F401
 

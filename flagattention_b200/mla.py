@@ -185,3 +185,37 @@ def flash_mla_with_kvcache(q, k_cache, block_table, cache_seqlens, head_dim_v,
                k_cache.shape[1], block_table, cache_seqlens, 0, tile_scheduler_metadata,
                num_splits, out, lse, softmax_scale, causal, indices)
     return out, lse
+
+
+def append_kv_rows(kv_rows, k_cache, slot_mapping):
+    """Write new tokens' latent rows into the paged cache, in place.
+
+    kv_rows: [n, 576] (or [n, 1, 576]) in k_cache's dtype, unit inner stride;
+    k_cache: [num_blocks, page_size, 1, 576]; slot_mapping: int64 [n] of pool
+    rows (block * page_size + offset in block).  A negative slot skips its
+    row (padding).  Slots must be distinct.  The step before a decode whose
+    cache_seqlens count the appended tokens.  No function in the reference
+    (its caches are written by the caller, in the layout of paged.py:22-23).
+    """
+    require_cuda(kv_rows, k_cache, slot_mapping)
+    if kv_rows.dim() == 3:
+        kv_rows = kv_rows.reshape(kv_rows.shape[0], kv_rows.shape[-1])
+    if kv_rows.dim() != 2 or kv_rows.shape[-1] != D_QK:
+        raise _lib.InvalidArgument("kv_rows must be [n, 576]")
+    if k_cache.dim() != 4 or k_cache.shape[2] != 1 or k_cache.shape[-1] != D_QK:
+        raise _lib.InvalidArgument("k_cache must be [num_blocks, page_size, 1, 576]")
+    if kv_rows.dtype != k_cache.dtype:
+        raise _lib.InvalidArgument("kv_rows and k_cache dtypes differ")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.dim() != 1 or \
+            slot_mapping.shape[0] != kv_rows.shape[0]:
+        raise _lib.InvalidArgument("slot_mapping must be int64 [n]")
+    if kv_rows.stride(-1) != 1:
+        kv_rows = kv_rows.contiguous()
+    slot_mapping = slot_mapping.contiguous()
+    _lib.check(_lib.lib().fa_mla_append_rows(ptr(kv_rows), kv_rows.stride(0), ptr(slot_mapping),
+                                             kv_rows.shape[0], ptr(k_cache), k_cache.stride(0),
+                                             k_cache.stride(1), k_cache.shape[0],
+                                             k_cache.shape[1], dtype_code(k_cache),
+                                             stream_of(k_cache)),
+               "fa_mla_append_rows")
+    return k_cache

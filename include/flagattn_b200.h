@@ -27,6 +27,9 @@
  *   fa_mla_combine            paged.py:366-449 / split_kv.py:198-228, over the
  *                             per-sequence variable split counts of the
  *                             metadata
+ *   fa_mla_append_rows        no reference function: writes new tokens'
+ *                             latent rows into the paged pool read by the
+ *                             decode (the cache layout of paged.py:22-23)
  */
 #ifndef FLAGATTN_B200_H_
 #define FLAGATTN_B200_H_
@@ -194,6 +197,17 @@ int fa_mla_decode(const fa_mla_args *args, void *stream);
 int fa_mla_decode_partial(const fa_mla_args *args, void *stream);
 /* Combine only (the decode kernel's split partials -> out / lse). */
 int fa_mla_combine(const fa_mla_args *args, void *stream);
+
+/* Write n latent rows (576 dims, bf16 / f16 as dtype; row r at
+ * rows + r * rows_stride elements, unit inner stride) into the pool row
+ * slots[r] = page * page_size + offset of kcache (layout as in fa_mla_args).
+ * A negative slot, or one at or past num_pages * page_size, skips its row.
+ * Slots must be distinct (two rows aimed at one slot race).  rows / kcache
+ * 16-byte aligned, slots (int64) 8-byte aligned, strides multiples of 8
+ * elements.  Asynchronous on stream; n == 0 launches nothing. */
+int fa_mla_append_rows(const void *rows, int64_t rows_stride, const int64_t *slots, int64_t n,
+                       void *kcache, int64_t kv_stride_page, int64_t kv_stride_tok,
+                       int32_t num_pages, int32_t page_size, int32_t dtype, void *stream);
 
 /* No counterpart in the reference.  fa_mla_decode for callers that cannot
  * allocate device memory: serving engines that reserve nearly all of it for

@@ -19,6 +19,7 @@ against those fixtures.
 from oracle.attention import (  # noqa: F401
     flash_attention,
     lse_combine,
+    mla_append_rows,
     mla_decode_dense,
     mla_decode_sparse,
     paged_attention,

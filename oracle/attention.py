@@ -204,3 +204,20 @@ def paged_v2_reduce(tmp_out, m_i, l_i):
     l_tot = np.sum(l_scaled, axis=0)
     r = l_scaled / l_tot[None]
     return np.sum(tmp_out * r[..., None], axis=0).astype(np.float32)
+
+
+def mla_append_rows(cache, rows, slots):
+    """Paged write of new latent rows (no reference function: the pool layout
+    of ``paged.py:22-23``, ``[pages, page_size, heads, dim]``).
+
+    Row r of ``rows`` goes to ``cache[slots[r] // page_size, slots[r] %
+    page_size, 0]``; a negative slot or one past the pool skips the row.
+    Returns a new array (the input is not modified).
+    """
+    out = np.array(cache, copy=True)
+    page = out.shape[1]
+    total = out.shape[0] * page
+    for r, s in enumerate(np.asarray(slots, np.int64)):
+        if 0 <= s < total:
+            out[s // page, s % page, 0] = rows[r]
+    return out

@@ -83,3 +83,30 @@ def test_invalid_arguments_are_rejected_on_host():
         _lib.FA_ERR_UNSUPPORTED
     with pytest.raises(_lib.InvalidArgument):
         _lib.check(_lib.FA_ERR_INVALID_ARGUMENT, "x")
+
+
+def test_append_rows_rejected_on_host():
+    """fa_mla_append_rows checks its arguments before any CUDA call (the
+    pointers below are never dereferenced)."""
+    lib = _lib.lib()
+    fake = ctypes.c_void_p(1 << 20)
+    page_stride, tok_stride = 64 * 576, 576
+    args = lambda rows, rs, n, dtype: (rows, rs, fake, n, fake, page_stride, tok_stride, 4, 64,  # noqa: E731
+                                       dtype, None)
+    assert lib.fa_mla_append_rows(*args(fake, 576, -1, 0)) == _lib.FA_ERR_INVALID_ARGUMENT
+    assert lib.fa_mla_append_rows(*args(fake, 576, 4, 2)) == _lib.FA_ERR_UNSUPPORTED  # f32
+    assert lib.fa_mla_append_rows(*args(fake, 570, 4, 0)) == _lib.FA_ERR_INVALID_ARGUMENT
+    assert lib.fa_mla_append_rows(*args(ctypes.c_void_p((1 << 20) + 8), 576, 4, 0)) == \
+        _lib.FA_ERR_INVALID_ARGUMENT                                           # misaligned rows
+    assert lib.fa_mla_append_rows(None, 576, None, 0, None, page_stride, tok_stride, 4, 64, 0,
+                                  None) == _lib.FA_OK                           # nothing to write
+
+
+def test_append_oracle_skips_negative_and_out_of_pool_slots():
+    import numpy as np
+    import oracle
+    cache = np.zeros((2, 4, 1, 3), np.float32)
+    rows = np.arange(12, dtype=np.float32).reshape(4, 3)
+    out = oracle.mla_append_rows(cache, rows, [5, -1, 8, 0])
+    assert np.array_equal(out[1, 1, 0], rows[0]) and np.array_equal(out[0, 0, 0], rows[3])
+    assert np.count_nonzero(out) == 6 - 1 and not np.any(cache)   # row 0 holds a 0; input untouched
