@@ -95,6 +95,7 @@ SIGNATURES = [
     ("fa_mla_decode_static_workspace", _i32, [ctypes.POINTER(MlaArgs), _vp]),
     ("fa_mla_append_rows", _i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i32, _i32, _i32,
                                   _vp]),
+    ("fa_selftest_wait_timeout", _i32, [_vp, _vp]),
 ]
 
 _lib = None

@@ -22,6 +22,7 @@ enum DeviceStatus : int {
   kDevTimeoutExchange = 4,
   kDevTimeoutDrain = 5,
   kDevBadSmemAlign = 6,
+  kDevTimeoutSelfTest = 7,  // fa_selftest_wait_timeout: the expected outcome
 };
 
 // Every wait on an mbarrier gives up after this many SM clock cycles (about

@@ -209,6 +209,15 @@ int fa_mla_append_rows(const void *rows, int64_t rows_stride, const int64_t *slo
                        void *kcache, int64_t kv_stride_page, int64_t kv_stride_tok,
                        int32_t num_pages, int32_t page_size, int32_t dtype, void *stream);
 
+/* No counterpart in the reference (the reference's Triton kernels have no
+ * waits that can time out).  Self-test of the bounded wait inside every
+ * kernel here: one warp waits on a barrier that nothing completes; after the
+ * limit (about 2 s) the wait gives up and writes FA_DEVICE_TIMEOUT_SELFTEST
+ * into *status (a device int32 the caller zeroed), and the kernel returns.
+ * The CUDA context stays usable. */
+#define FA_DEVICE_TIMEOUT_SELFTEST 7
+int fa_selftest_wait_timeout(int32_t *status, void *stream);
+
 /* No counterpart in the reference.  fa_mla_decode for callers that cannot
  * allocate device memory: serving engines that reserve nearly all of it for
  * their KV-cache pool up front, and plugin / FFI hosts that pass device
