@@ -1,9 +1,9 @@
 #!/usr/bin/env python
 """MLA decode benchmark on B200 (one JSON line on rank 0).
 
-Workload: DeepSeek-V3-shaped dense paged MLA decode --
-64 sequences per GPU, seq_q 1, 128 query heads, one 576-dim latent head
-(values = first 512 dims), page 64, bf16 N(0,1), context lengths
+Headline workload: DeepSeek-V3-shaped dense paged MLA
+decode -- 64 sequences per GPU, seq_q 1, 128 query heads, one 576-dim latent
+head (values = first 512 dims), page 64, bf16 N(0,1), context lengths
 U[1024, 8192], block table a random permutation of a pooled page cache,
 softmax scale 576^-0.5.  A step is one decode of the batch (decode kernel +
 split combine; the tile metadata is computed once per batch, as it is shared
@@ -11,14 +11,22 @@ by every layer of a model step).  With --gpus N (torchrun) the global batch
 of 64*N sequences is sharded by sequence across the ranks (greedy by KV bytes,
 no collective on the data path): weak scaling.
 
-``--impl reference`` times the reference algorithm's CPU implementation (the
-numpy restatement of flag_attn.testing in oracle/) on the host cores instead.
+The same line carries ``long_context``: BASELINE config 5 (2 sequences of
+1,048,576 tokens) with the KV pages split evenly over the N ranks, each rank
+decoding its pages into a packed f32 partial, one NCCL all-gather, and the
+on-device combine -- strong scaling, with the all-gather and combine times
+broken out.
+
+Inputs of sequence i (query and its KV rows) come from a CPU generator seeded
+with i, so both arms decode the same values.  ``--impl reference`` times the
+reference algorithm's CPU implementation (the numpy restatement of
+flag_attn.testing in oracle/) on all host cores, on the first sequences of the
+same global batch.
 """
 
 import argparse
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -58,6 +66,26 @@ def global_lens(world):
     return rs.randint(CTX_LO, CTX_HI + 1, size=B_PER_GPU * world).astype(np.int32)
 
 
+def sequence_inputs(i, n):
+    """Query [S_Q, H_Q, 576] and KV rows [pages*64, 576] (bf16) of global
+    sequence i with context n, from a CPU generator seeded with i: the same
+    values in both arms, at every GPU count."""
+    import torch
+    g = torch.Generator().manual_seed(SEED * 1000 + int(i))
+    q = torch.randn((S_Q, H_Q, D_QK), generator=g).to(torch.bfloat16)
+    kv = torch.randn((-(-int(n) // PAGE) * PAGE, D_QK), generator=g).to(torch.bfloat16)
+    return q, kv
+
+
+def config_dict(world):
+    return {"workload": WORKLOAD, "batch_per_gpu": B_PER_GPU, "global_batch": B_PER_GPU * world,
+            "seq_q": S_Q, "heads_q": H_Q, "d_qk": D_QK, "d_v": D_V, "page_size": PAGE,
+            "ctx": [CTX_LO, CTX_HI], "parallelism": f"seq-shard{world}",
+            "inputs": "sequence i from a CPU torch generator seeded with i (bf16 N(0,1))",
+            "l2": "flushed before every step (256 MB write, outside the events)",
+            "metadata": "computed once per batch (outside the step)"}
+
+
 def algorithmic_bytes(lens):
     n = len(lens)
     return int(np.sum(lens.astype(np.int64)) * D_QK * 2 + n * S_Q * H_Q * (D_QK * 2 + D_V * 2 + 4))
@@ -74,16 +102,6 @@ def measured_peaks():
         return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     except Exception:  # noqa: BLE001
         return 6650.0, 1590.0, "fallback"
-
-
-def profiled_traffic():
-    """dram read+write bytes per decode launch from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "mla_decode_config2.md")
-    try:
-        m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(path).read())
-        return int(m.group(1)) if m else None
-    except OSError:
-        return None
 
 
 # ----------------------------------------------------------------- clocks
@@ -166,6 +184,30 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- our arm
+def build_batch(lens, gidx, dev):
+    """Paged pool (pages in a random permutation) holding the sequences
+    gidx (global indices, context lens), queries, block table."""
+    import torch
+    B = len(lens)
+    npg = (lens + PAGE - 1) // PAGE
+    npages = int(npg.sum())
+    kcache = torch.empty((npages, PAGE, 1, D_QK), dtype=torch.bfloat16, device=dev)
+    q = torch.empty((B, S_Q, H_Q, D_QK), dtype=torch.bfloat16, device=dev)
+    perm = np.random.RandomState(SEED + 1 + int(gidx[0]) if B else SEED).permutation(npages)
+    bt_np = np.zeros((B, int(npg.max())), np.int32)
+    off = 0
+    for j, (gi, n) in enumerate(zip(gidx, lens)):
+        k = int(npg[j])
+        pages = perm[off:off + k]
+        off += k
+        bt_np[j, :k] = pages
+        qs, kv = sequence_inputs(gi, n)
+        q[j] = qs.to(dev)
+        kcache[torch.from_numpy(pages.astype(np.int64)).to(dev)] = \
+            kv.view(k, PAGE, 1, D_QK).to(dev)
+    return q, kcache, torch.from_numpy(bt_np).to(dev), npages
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -188,18 +230,7 @@ def run_ours(args):
     mine = partition_sequences(lens_all, world)[rank]
     lens = lens_all[mine]
     B = len(lens)
-    g = torch.Generator(device=dev).manual_seed(SEED + 17 * rank)
-    npages = int(np.sum((lens + PAGE - 1) // PAGE))
-    kcache = torch.randn((npages, PAGE, 1, D_QK), generator=g, device=dev, dtype=torch.bfloat16)
-    q = torch.randn((B, S_Q, H_Q, D_QK), generator=g, device=dev, dtype=torch.bfloat16)
-    perm = torch.randperm(npages, generator=g, device=dev).to(torch.int32)
-    width = int(((lens.max() + PAGE - 1) // PAGE))
-    bt = torch.zeros((B, width), dtype=torch.int32, device=dev)
-    off = 0
-    for i, n in enumerate(lens):
-        k = int((n + PAGE - 1) // PAGE)
-        bt[i, :k] = perm[off:off + k]
-        off += k
+    q, kcache, bt, npages = build_batch(lens, mine, dev)
     seq = torch.from_numpy(lens).to(dev)
     meta, splits = fa.get_mla_metadata(seq, S_Q * H_Q, 1)
     out = torch.empty((B, S_Q, H_Q, D_V), dtype=torch.bfloat16, device=dev)
@@ -274,7 +305,7 @@ def run_ours(args):
     # the end-to-end path computed the same outputs as the device-resident one
     call.run()
     torch.cuda.synchronize()
-    assert torch.allclose(out_h.float(), out.cpu().float(), atol=1e-2, rtol=1e-2), \
+    assert torch.equal(out_h, out.cpu()) and torch.equal(lse_h, lse.cpu()), \
         "end-to-end output differs from the device-resident decode"
     h2d = q.numel() * 2 + seq.numel() * 4 + bt.numel() * 4
     d2h = out.numel() * 2 + lse.numel() * 4
@@ -283,31 +314,28 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms, dec_ms, e2e_ms = t.tolist()
+
+    long_ctx = run_long_context(args, world, rank, dev, flush)
+
     tokens = len(lens_all) * S_Q
     bytes_local = algorithmic_bytes(lens)
     flops_local = algorithmic_flops(lens)
     if rank == 0:
         peak_gbs, peak_tf, peak_kind = measured_peaks()
         achieved = bytes_local / (dec_ms * 1e-3) / 1e9
-        traffic = profiled_traffic()
         rec = {
             "metric": METRIC, "value": tokens / (step_ms * 1e-3), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16)",
-            "config": {"workload": WORKLOAD, "batch_per_gpu": B_PER_GPU,
-                       "global_batch": len(lens_all), "seq_q": S_Q, "heads_q": H_Q,
-                       "d_qk": D_QK, "d_v": D_V, "page_size": PAGE,
-                       "ctx": [CTX_LO, CTX_HI], "parallelism": f"seq-shard{world}",
-                       "l2": "flushed before every step (256 MB write, outside the events)",
-                       "metadata": "computed once per batch (outside the step)"},
+            "config": config_dict(world),
             "hbm_gbs_step": bytes_local / (step_ms * 1e-3) / 1e9,
             "hbm_frac_step": bytes_local / (step_ms * 1e-3) / 1e9 / peak_gbs,
             "tensor_tflops_decode": flops_local / (dec_ms * 1e-3) / 1e12,
             "ms_decode_kernel": dec_ms, "ms_combine_kernel": step_ms - dec_ms,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs,
                          "unit": "GB/s", "frac": achieved / peak_gbs,
-                         "traffic": traffic, "peak_source": peak_kind,
+                         "traffic": None, "peak_source": peak_kind,
                          "kernel": "sv::mla_decode_sv_kernel<bf16> (score/value CTA pair)",
                          "algorithmic_bytes_per_launch": bytes_local},
             "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tok/s",
@@ -316,24 +344,124 @@ def run_ours(args):
                     "path": "get_mla_metadata + flash_mla_with_kvcache, pinned host buffers"},
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
+            "long_context": long_ctx,
         }
         if world == 1:
-            rec["cpu_baseline"] = cpu_baseline(q, kcache, bt, lens, args.cpu_seconds)
+            rec["cpu_baseline"] = cpu_baseline(lens_all, args.cpu_seconds)
         print(json.dumps(rec), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
 
-# ------------------------------------------------------------ CPU timing
-def _host_sequence(q, kcache, bt, lens, i):
-    """Sequence i as float32 numpy (its pages gathered, block table remapped)."""
+# ------------------------------------------- config 5: KV pages over N ranks
+LC_TOKENS, LC_BATCH = 1 << 20, 2
+LC_WORKLOAD = "long_context_mla_decode_b2_h128_ctx1m_bf16_kv_page_sharded"
+
+
+def run_long_context(args, world, rank, dev, flush):
+    """BASELINE config 5 with the KV pages of both 1M-token sequences split
+    evenly over the ranks (strong scaling).  A step: decode of this rank's
+    pages (+ the combine of its own split pieces) into a packed f32 partial,
+    one NCCL all-gather of the partials, the log-sum-exp merge on the GPU.
+    At N = 1 the step is the plain decode to bf16.  Every phase is timed with
+    CUDA events on the launching stream; the figures are the max over ranks."""
     import torch
-    n = int(lens[i])
-    k = (n + PAGE - 1) // PAGE
-    pages = bt[i, :k].long()
-    kc = kcache[pages].float().cpu().numpy()
-    return q[i:i + 1].float().cpu().numpy(), kc, np.arange(k, dtype=np.int32)[None], lens[i:i + 1]
+    import torch.distributed as dist
+
+    import flagattention_b200 as fa
+    from flagattention_b200 import _torch as fat
+    from flagattention_b200 import shard
+    from flagattention_b200.mla import MlaCall
+
+    pages_per_seq = LC_TOKENS // PAGE
+    lo, hi = shard.page_range(pages_per_seq, world, rank)
+    local_pages = hi - lo
+    local_len = min(LC_TOKENS, hi * PAGE) - lo * PAGE
+    g = torch.Generator(device=dev).manual_seed(SEED + 5000 + rank)
+    pool = torch.empty((LC_BATCH * local_pages, PAGE, 1, D_QK), dtype=torch.bfloat16, device=dev)
+    for a in range(0, pool.shape[0], 8192):
+        b = min(pool.shape[0], a + 8192)
+        pool[a:b] = torch.randn((b - a, PAGE, 1, D_QK), generator=g, device=dev)
+    bt = torch.randperm(pool.shape[0], generator=g, device=dev).to(torch.int32)
+    bt = bt.view(LC_BATCH, local_pages).contiguous()
+    seq = torch.full((LC_BATCH,), local_len, dtype=torch.int32, device=dev)
+    gq = torch.Generator(device=dev).manual_seed(SEED + 5999)          # same q on every rank
+    q = torch.randn((LC_BATCH, 1, H_Q, D_QK), generator=gq, device=dev).to(torch.bfloat16)
+    rows = LC_BATCH * H_Q
+    if world == 1:
+        meta, splits = fa.get_mla_metadata(seq, H_Q, 1)
+        out = torch.empty((LC_BATCH, 1, H_Q, D_V), dtype=torch.bfloat16, device=dev)
+        lse = torch.empty((LC_BATCH, H_Q, 1), dtype=torch.float32, device=dev)
+        call = MlaCall(q, pool, pool.stride(0), pool.stride(1), pool.shape[0], PAGE, bt, seq, 0,
+                       meta, splits, out, lse, D_QK ** -0.5)
+    else:
+        part = shard.PartialDecode(q, pool, bt, seq, D_QK ** -0.5)
+        call = part.call
+        gathered = torch.empty((world, part.packed.numel()), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev):
+        flush.fill_(1)
+        ev[0].record(stream)
+        call.run()
+        ev[1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered.view(-1), part.packed)
+            ev[2].record(stream)
+            shard.merge_partials(gathered, rows, D_V, torch.bfloat16)
+        else:
+            ev[2].record(stream)
+        ev[3].record(stream)
+
+    for _ in range(args.warmup):
+        step([torch.cuda.Event(enable_timing=True) for _ in range(4)])
+    torch.cuda.synchronize()
+    assert fat.read_status(dev) == 0, "device wait timeout during warm-up (long context)"
+    steps = max(3, min(args.steps, 100))
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        step(evs[i])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    assert fat.read_status(dev) == 0, "device wait timeout in the timed region (long context)"
+    mean = lambda k0, k1: sum(e[k0].elapsed_time(e[k1]) for e in evs) / steps  # noqa: E731
+    t = torch.tensor([mean(0, 3), mean(0, 1), mean(1, 2), mean(2, 3)], dtype=torch.float64,
+                     device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, dec_ms, gather_ms, merge_ms = t.tolist()
+    peak_gbs, _, peak_kind = measured_peaks()
+    kv_bytes = LC_BATCH * local_len * D_QK * 2 + rows * (D_QK * 2 + D_V * 4 + 4)
+    return {"workload": LC_WORKLOAD, "baseline_config": 5, "n_gpus": world,
+            "scaling": "strong", "steps": steps,
+            "tokens_per_s": LC_BATCH / (step_ms * 1e-3), "ms_per_step": step_ms,
+            "ms_decode": dec_ms, "us_allgather": gather_ms * 1e3, "us_merge": merge_ms * 1e3,
+            "gpu_launches_per_step": 2 + (1 if world > 1 else 0),
+            "nccl_collectives_per_step": 1 if world > 1 else 0,
+            "allgather_bytes_per_rank": rows * (D_V + 1) * 4 if world > 1 else 0,
+            "tokens_per_rank": LC_BATCH * local_len,
+            "hbm_frac_decode": kv_bytes / (dec_ms * 1e-3) / 1e9 / peak_gbs,
+            "peak_source": peak_kind}
+
+
+# ------------------------------------------------------------ CPU timing
+def reference_samples(lens_all, n_seq):
+    """The first n_seq sequences of the global batch as float32 numpy, each
+    in a pool of exactly its pages (the same bf16 values the GPU arm decodes,
+    upcast as the reference's fp32 path does)."""
+    samples = []
+    for i in range(min(n_seq, len(lens_all))):
+        n = int(lens_all[i])
+        qs, kv = sequence_inputs(i, n)
+        k = (n + PAGE - 1) // PAGE
+        samples.append((qs.float().numpy()[None], kv.float().numpy().reshape(k, PAGE, 1, D_QK),
+                        np.arange(k, dtype=np.int32)[None], lens_all[i:i + 1]))
+    return samples
 
 
 def time_oracle(samples, budget_s):
@@ -349,62 +477,53 @@ def time_oracle(samples, budget_s):
             return done * S_Q / el, done, el
 
 
-def _threads():
-    try:
-        from threadpoolctl import threadpool_info
-        n = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
-        return int(n)
-    except Exception:  # noqa: BLE001
-        return os.cpu_count() or 1
+def all_host_threads():
+    """Let BLAS use every host core, whatever the launcher set
+    (torchrun exports OMP_NUM_THREADS=1); returns the thread count."""
+    n = os.cpu_count() or 1
+    from threadpoolctl import threadpool_limits
+    threadpool_limits(limits=n)
+    return n
 
 
-def cpu_baseline(q, kcache, bt, lens, budget):
-    samples = [_host_sequence(q, kcache, bt, lens, i) for i in range(min(8, len(lens)))]
+def cpu_baseline(lens_all, budget):
+    cores = all_host_threads()
+    samples = reference_samples(lens_all, 8)
     tps, done, el = time_oracle(samples, budget)
-    return {"value": tps, "unit": "tok/s", "cores": _threads(), "kind": "port",
-            "sample": f"{done} sequence decodes of the config-2 workload (first 8 sequences, "
-                      f"ctx {int(lens[:8].min())}-{int(lens[:8].max())}, 128 heads) through the "
-                      f"numpy oracle in {el:.1f}s, float32, all BLAS threads"}
+    return {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{done} sequence decodes of the config-2 workload (global sequences 0-7, "
+                      f"ctx {int(lens_all[:8].min())}-{int(lens_all[:8].max())}, 128 heads) "
+                      f"through the numpy oracle in {el:.1f}s, float32, {cores} BLAS threads"}
 
 
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    lens = global_lens(1)
-    rs = np.random.RandomState(SEED)
+    cores = all_host_threads()
+    lens_all = global_lens(world)
     n_seq = 8
-    samples = []
-    for i in range(n_seq):
-        n = int(lens[i])
-        k = (n + PAGE - 1) // PAGE
-        kc = rs.standard_normal((k, PAGE, 1, D_QK)).astype(np.float32)
-        qs = rs.standard_normal((1, S_Q, H_Q, D_QK)).astype(np.float32)
-        samples.append((qs, kc, np.arange(k, dtype=np.int32)[None], lens[i:i + 1]))
+    samples = reference_samples(lens_all, n_seq)
     per_step = max(0.5, min(2.0, 150.0 / max(1, args.steps + args.warmup)))
     for _ in range(args.warmup):
         time_oracle(samples, per_step)
-    vals = []
     t0 = time.perf_counter()
     total_done = 0
     for _ in range(args.steps):
-        v, d, _ = time_oracle(samples, per_step)
-        vals.append(v)
+        _, d, _ = time_oracle(samples, per_step)
         total_done += d
     el = time.perf_counter() - t0
     value = total_done * S_Q / el
-    cores = _threads()
     rec = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-           "data": "synthetic (seeded N(0,1))", "impl": "reference",
-           "config": {"workload": WORKLOAD, "batch_per_gpu": B_PER_GPU, "seq_q": S_Q,
-                      "heads_q": H_Q, "d_qk": D_QK, "d_v": D_V, "page_size": PAGE,
-                      "ctx": [CTX_LO, CTX_HI], "parallelism": "host cpu"},
+           "data": "synthetic (seeded N(0,1) bf16)", "impl": "reference",
+           "config": config_dict(world),
            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
-                            "sample": f"each step decodes config-2 sequences (the first {n_seq},"
-                                      f" round-robin) for ~{per_step:.1f}s through the numpy "
-                                      "restatement of flag_attn.testing"},
+                            "sample": f"each step decodes global sequences 0-{n_seq - 1} of the "
+                                      f"config-2 batch (round-robin, ~{per_step:.1f}s) through "
+                                      "the numpy restatement of flag_attn.testing, float32 "
+                                      "upcast of the same bf16 inputs the GPU arm decodes"},
            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(rec), flush=True)

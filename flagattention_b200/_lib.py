@@ -8,8 +8,8 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-# FA_LIB_PATH selects another build of the same library (e.g. a debug build
-# with kernel tracing); by default the in-tree build is loaded.
+# FA_LIB_PATH selects another build of the same library; by default the
+# in-tree build is loaded.
 LIB_PATH = os.environ.get("FA_LIB_PATH") or os.path.join(_HERE, "libflagattn_b200.so")
 
 FA_OK = 0
@@ -84,6 +84,8 @@ SIGNATURES = [
     ("fa_paged_attention", _i32, [ctypes.POINTER(DecodeArgs), _vp]),
     ("fa_split_kv_attention", _i32, [ctypes.POINTER(DecodeArgs), _vp]),
     ("fa_lse_combine", _i32, [_vp, _vp, _i32, _i64, _i32, _vp, _i32, _vp, _vp]),
+    ("fa_lse_combine_strided", _i32, [_vp, _i64, _vp, _i64, _i32, _i64, _i32, _vp, _i32, _vp,
+                                      _vp]),
     ("fa_mla_num_sm_parts", _i32, [_i32, _i32, _i32, _i32, ctypes.POINTER(_i32)]),
     ("fa_mla_workspace_size", _i32, [_i32, _i32, _i32, _i32, _i32,
                                      ctypes.POINTER(ctypes.c_size_t),

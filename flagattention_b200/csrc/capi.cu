@@ -17,14 +17,12 @@
 
 namespace fa {
 void launch_mla_metadata(const int32_t *, int, int, int, int32_t *, int32_t *, cudaStream_t);
-void launch_lse_combine(const float *, const float *, int, int64_t, int, int, int, void *, int,
-                        int64_t, int64_t, int64_t, float *, cudaStream_t);
+void launch_lse_combine(const float *, const float *, int, int64_t, int64_t, int64_t, int, int,
+                        int, void *, int, int64_t, int64_t, int64_t, float *, cudaStream_t);
 void launch_mla_combine(const float *, const float *, const int32_t *, int, int, int, int, void *,
                         int, int64_t, int64_t, int64_t, float *, cudaStream_t);
 cudaError_t launch_generic_decode(const fa_decode_args *, cudaStream_t);
 size_t generic_smem_bytes(int, int);
-cudaError_t launch_mla_tc(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
-                          const fa_mla_args *, int, int64_t, cudaStream_t);
 cudaError_t launch_mla_sv(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                           const CUtensorMap &, const fa_mla_args *, int, cudaStream_t);
 }  // namespace fa
@@ -157,9 +155,9 @@ int run_decode(const fa_decode_args *a, void *stream) {
   if (e != cudaSuccess) return cuda_fail(e, "generic decode launch");
   if (a->num_splits > 1) {
     const int64_t rows = static_cast<int64_t>(a->batch) * a->num_q_heads * a->m_q;
-    fa::launch_lse_combine(a->part_o, a->part_lse, a->num_splits, rows, a->num_q_heads, a->m_q,
-                           a->d_v, a->o, a->dtype, a->o_stride_b, a->o_stride_h, a->o_stride_m,
-                           a->lse, s);
+    fa::launch_lse_combine(a->part_o, a->part_lse, a->num_splits, rows * a->d_v, rows, rows,
+                           a->num_q_heads, a->m_q, a->d_v, a->o, a->dtype, a->o_stride_b,
+                           a->o_stride_h, a->o_stride_m, a->lse, s);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "combine launch");
   }
@@ -317,12 +315,24 @@ int fa_split_kv_attention(const fa_decode_args *a, void *stream) {
 
 int fa_lse_combine(const float *part_o, const float *part_lse, int num_parts, int64_t rows,
                    int d_v, void *o, int dtype, float *lse, void *stream) {
+  return fa_lse_combine_strided(part_o, rows * d_v, part_lse, rows, num_parts, rows, d_v, o, dtype,
+                                lse, stream);
+}
+
+int fa_lse_combine_strided(const float *part_o, int64_t o_part_stride, const float *part_lse,
+                           int64_t lse_part_stride, int num_parts, int64_t rows, int d_v, void *o,
+                           int dtype, float *lse, void *stream) {
   if (!part_o || !part_lse || !o || num_parts < 1 || rows < 0 || d_v <= 0 || d_v % 4)
     return fail(FA_ERR_INVALID_ARGUMENT, "bad combine arguments");
   if (d_v > 512) return fail(FA_ERR_UNSUPPORTED, "combine supports d_v <= 512 (got %d)", d_v);
+  if (o_part_stride < rows * d_v || lse_part_stride < 0 || o_part_stride % 4)
+    return fail(FA_ERR_INVALID_ARGUMENT, "combine part strides must cover a part (and keep "
+                                         "16-byte alignment)");
   if (!aligned16(part_o)) return fail(FA_ERR_INVALID_ARGUMENT, "part_o must be 16-byte aligned");
-  fa::launch_lse_combine(part_o, part_lse, num_parts, rows, 1, 1, d_v, o, dtype, d_v, 0, 0, lse,
-                         static_cast<cudaStream_t>(stream));
+  if (dtype != FA_DTYPE_BF16 && dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_F32)
+    return fail(FA_ERR_INVALID_ARGUMENT, "dtype %d", dtype);
+  fa::launch_lse_combine(part_o, part_lse, num_parts, o_part_stride, lse_part_stride, rows, 1, 1,
+                         d_v, o, dtype, d_v, 0, 0, lse, static_cast<cudaStream_t>(stream));
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? FA_OK : cuda_fail(e, "combine launch");
 }
@@ -340,12 +350,18 @@ int fa_mla_num_sm_parts(int device, int s_q, int h_q, int sparse, int *num_sm_pa
 
 int fa_mla_workspace_size(int batch, int s_q, int h_q, int d_v, int num_sm_parts,
                           size_t *part_o_bytes, size_t *part_lse_bytes) {
-  if (!part_o_bytes || !part_lse_bytes || batch < 0 || num_sm_parts < 1)
+  if (!part_o_bytes || !part_lse_bytes || batch < 0 || num_sm_parts < 1 || s_q <= 0 ||
+      h_q <= 0 || d_v <= 0)
     return fail(FA_ERR_INVALID_ARGUMENT, "bad arguments");
   const size_t slots = static_cast<size_t>(batch) + num_sm_parts;
-  const size_t rows = static_cast<size_t>(s_q) * h_q;
-  *part_o_bytes = slots * rows * d_v * sizeof(float);
-  *part_lse_bytes = slots * rows * sizeof(float);
+  size_t rows = 0, cells = 0, o_bytes = 0, lse_bytes = 0;
+  if (__builtin_mul_overflow(static_cast<size_t>(s_q), static_cast<size_t>(h_q), &rows) ||
+      __builtin_mul_overflow(slots, rows, &cells) ||
+      __builtin_mul_overflow(cells, static_cast<size_t>(d_v) * sizeof(float), &o_bytes) ||
+      __builtin_mul_overflow(cells, sizeof(float), &lse_bytes))
+    return fail(FA_ERR_INVALID_ARGUMENT, "workspace size overflows size_t");
+  *part_o_bytes = o_bytes;
+  *part_lse_bytes = lse_bytes;
   return FA_OK;
 }
 
@@ -380,47 +396,35 @@ int fa_mla_decode_partial(const fa_mla_args *a, void *stream) {
   const bool paged = a->block_table != nullptr;
   const uint64_t kv_rows = (sparse || paged) ? a->page_size : (a->n_ctx > 0 ? a->n_ctx : 1);
   const uint64_t kv_groups = (sparse || paged) ? a->num_pages : a->batch;
-  // Top-k rows go through the score / value kernel with tile::gather4 loads
-  // when every pool row lies at one stride (pages back to back); other pool
-  // layouts keep the head-dim-split kernel's per-row copies.
-  const bool uniform_rows =
-      sparse && a->kv_stride_page == static_cast<int64_t>(a->page_size) * a->kv_stride_tok;
-  if (!sparse || uniform_rows) {
-    // score / value CTA kernel (query box 64 dims x 128 rows, key rows in
-    // 64-row boxes, value rows in 32-row boxes; top-k: one-row gathers)
-    CUtensorMap qm, km, vm, gm;
-    st = encode_map(&qm, a->q, a->dtype, 576, static_cast<uint64_t>(a->s_q) * a->h_q, a->batch,
-                    a->q_stride_h, a->q_stride_b, 128, 64);
-    if (st != FA_OK) return st;
-    st = encode_map(&km, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
-                    a->kv_stride_page, bn, 64);
-    if (st != FA_OK) return st;
-    st = encode_map(&vm, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
-                    a->kv_stride_page, 32, 64);
-    if (st != FA_OK) return st;
-    if (sparse) {
-      st = encode_gather_map(&gm, a->kcache, a->dtype,
-                             static_cast<uint64_t>(a->num_pages) * a->page_size, a->kv_stride_tok);
-      if (st != FA_OK) return st;
-    } else {
-      gm = qm;  // not read by the dense instance
-    }
-    cudaError_t e = fa::launch_mla_sv(qm, km, vm, gm, a, m_blocks, static_cast<cudaStream_t>(stream));
-    return e == cudaSuccess ? FA_OK : cuda_fail(e, "MLA decode launch");
-  }
-  CUtensorMap qrm, km, krm;
-  st = encode_map(&qrm, a->q, a->dtype, 576, static_cast<uint64_t>(a->s_q) * a->h_q, a->batch,
-                  a->q_stride_h, a->q_stride_b, 128, 32);
+  // One score / value CTA kernel for dense and top-k decode: query box 64
+  // dims x 128 rows, key rows in 64-row boxes, value rows in 32-row boxes.
+  // Top-k rows come from a gather map: when every pool row lies at one stride
+  // (pages back to back) a 2-D map over all rows read by tile::gather4,
+  // otherwise the 3-D page map with one-row boxes.
+  CUtensorMap qm, km, vm, gm;
+  st = encode_map(&qm, a->q, a->dtype, 576, static_cast<uint64_t>(a->s_q) * a->h_q, a->batch,
+                  a->q_stride_h, a->q_stride_b, 128, 64);
   if (st != FA_OK) return st;
   st = encode_map(&km, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
                   a->kv_stride_page, bn, 64);
   if (st != FA_OK) return st;
-  st = encode_map(&krm, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
-                  a->kv_stride_page, bn, 32);
+  st = encode_map(&vm, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
+                  a->kv_stride_page, 32, 64);
   if (st != FA_OK) return st;
-  const int64_t total_rows = static_cast<int64_t>(a->num_pages) * a->page_size;
-  cudaError_t e = fa::launch_mla_tc(qrm, km, krm, a, m_blocks, total_rows,
-                                    static_cast<cudaStream_t>(stream));
+  if (sparse) {
+    const bool uniform_rows =
+        a->kv_stride_page == static_cast<int64_t>(a->page_size) * a->kv_stride_tok;
+    st = uniform_rows
+             ? encode_gather_map(&gm, a->kcache, a->dtype,
+                                 static_cast<uint64_t>(a->num_pages) * a->page_size,
+                                 a->kv_stride_tok)
+             : encode_map(&gm, a->kcache, a->dtype, 576, a->page_size, a->num_pages,
+                          a->kv_stride_tok, a->kv_stride_page, 1, 64);
+    if (st != FA_OK) return st;
+  } else {
+    gm = qm;  // not read by the dense instance
+  }
+  cudaError_t e = fa::launch_mla_sv(qm, km, vm, gm, a, m_blocks, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FA_OK : cuda_fail(e, "MLA decode launch");
 }
 

@@ -98,7 +98,8 @@ __device__ __forceinline__ float merge_row(const float *__restrict__ part_o,
 // num_parts partials laid out [part][rows][d_v]; lse out f32 [rows].
 template <typename T>
 __global__ void __launch_bounds__(128, 8) lse_combine_kernel(const float *__restrict__ part_o,
-                                   const float *__restrict__ part_lse, int num_parts, int64_t rows,
+                                   const float *__restrict__ part_lse, int num_parts,
+                                   int64_t o_part_stride, int64_t lse_part_stride, int64_t rows,
                                    int H, int M, int d_v, T *__restrict__ out, int64_t o_sb,
                                    int64_t o_sh, int64_t o_sm, float *__restrict__ lse) {
   const int lane = threadIdx.x & 31;
@@ -108,8 +109,8 @@ __global__ void __launch_bounds__(128, 8) lse_combine_kernel(const float *__rest
   const int h = static_cast<int>((row / M) % H);
   const int m = static_cast<int>(row % M);
   T *o = out + b * o_sb + h * o_sh + m * o_sm;
-  const float l = merge_row<T>(part_o, part_lse, 0, num_parts, rows * d_v, rows, row * d_v, row,
-                               d_v, o, lane);
+  const float l = merge_row<T>(part_o, part_lse, 0, num_parts, o_part_stride, lse_part_stride,
+                               row * d_v, row, d_v, o, lane);
   if (lse != nullptr && lane == 0) lse[row] = l;
 }
 
@@ -137,28 +138,34 @@ __global__ void __launch_bounds__(128, 8) mla_combine_kernel(const float *__rest
 }
 
 template <typename T>
-void launch_lse_combine_t(const float *part_o, const float *part_lse, int num_parts, int64_t rows,
-                          int H, int M, int d_v, void *out, int64_t o_sb, int64_t o_sh,
-                          int64_t o_sm, float *lse, cudaStream_t stream) {
+void launch_lse_combine_t(const float *part_o, const float *part_lse, int num_parts,
+                          int64_t o_part_stride, int64_t lse_part_stride, int64_t rows, int H,
+                          int M, int d_v, void *out, int64_t o_sb, int64_t o_sh, int64_t o_sm,
+                          float *lse, cudaStream_t stream) {
   const int warps = 4;
   const int64_t grid = (rows + warps - 1) / warps;
   if (grid == 0) return;
   lse_combine_kernel<T><<<static_cast<unsigned>(grid), warps * 32, 0, stream>>>(
-      part_o, part_lse, num_parts, rows, H, M, d_v, static_cast<T *>(out), o_sb, o_sh, o_sm, lse);
+      part_o, part_lse, num_parts, o_part_stride, lse_part_stride, rows, H, M, d_v,
+      static_cast<T *>(out), o_sb, o_sh, o_sm, lse);
 }
 
-void launch_lse_combine(const float *part_o, const float *part_lse, int num_parts, int64_t rows,
-                        int H, int M, int d_v, void *out, int dtype, int64_t o_sb, int64_t o_sh,
-                        int64_t o_sm, float *lse, cudaStream_t stream) {
+// Partial p of row r: O at part_o + p * o_part_stride + r * d_v, LSE at
+// part_lse + p * lse_part_stride + r.
+void launch_lse_combine(const float *part_o, const float *part_lse, int num_parts,
+                        int64_t o_part_stride, int64_t lse_part_stride, int64_t rows, int H, int M,
+                        int d_v, void *out, int dtype, int64_t o_sb, int64_t o_sh, int64_t o_sm,
+                        float *lse, cudaStream_t stream) {
   if (dtype == FA_DTYPE_BF16)
-    launch_lse_combine_t<__nv_bfloat16>(part_o, part_lse, num_parts, rows, H, M, d_v, out, o_sb,
-                                        o_sh, o_sm, lse, stream);
+    launch_lse_combine_t<__nv_bfloat16>(part_o, part_lse, num_parts, o_part_stride,
+                                        lse_part_stride, rows, H, M, d_v, out, o_sb, o_sh, o_sm,
+                                        lse, stream);
   else if (dtype == FA_DTYPE_F16)
-    launch_lse_combine_t<__half>(part_o, part_lse, num_parts, rows, H, M, d_v, out, o_sb, o_sh,
-                                 o_sm, lse, stream);
+    launch_lse_combine_t<__half>(part_o, part_lse, num_parts, o_part_stride, lse_part_stride,
+                                 rows, H, M, d_v, out, o_sb, o_sh, o_sm, lse, stream);
   else
-    launch_lse_combine_t<float>(part_o, part_lse, num_parts, rows, H, M, d_v, out, o_sb, o_sh,
-                                o_sm, lse, stream);
+    launch_lse_combine_t<float>(part_o, part_lse, num_parts, o_part_stride, lse_part_stride, rows,
+                                H, M, d_v, out, o_sb, o_sh, o_sm, lse, stream);
 }
 
 void launch_mla_combine(const float *part_o, const float *part_lse, const int32_t *num_splits,

@@ -7,8 +7,8 @@
 // sequence.  One CTA owns 16 query rows of one kv head (all rows read the same
 // key/value rows, so each key tile is staged once in shared memory for the
 // group) and one split of the keys; tiles of 16 keys go through an online
-// softmax in f32.  The tensor-core MLA kernel (mla_tc.cu) is the fast path for
-// the 576/512 latent shape; this kernel serves every other shape.
+// softmax in f32.  The tensor-core MLA kernel (mla_sv.cu) serves the 576/512
+// latent shape; this kernel serves every other shape.
 #include "common.cuh"
 #include "flagattn_b200.h"
 

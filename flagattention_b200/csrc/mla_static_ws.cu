@@ -17,9 +17,10 @@
 //     without ordering) race -- serialise them on one stream;
 //   * nothing in it has to start at zero: every partial the combine reads is
 //     written by the same call's decode kernel first.
-// The first call on a device looks up the array's device address
-// (cudaGetSymbolAddress with that device current); make that first call
-// before capturing work into a stream.  No cudaMalloc / cudaFree or
+// The first call in a CUDA context (per device, and again after
+// cudaDeviceReset) looks up the array's device address (cudaGetSymbolAddress
+// with that device current); make that first call before capturing work into
+// a stream.  No cudaMalloc / cudaFree or
 // allocating library routine is ever called here.
 #include <mutex>
 
@@ -35,16 +36,41 @@ int record_error(int status, const char *msg);
 namespace {
 
 constexpr size_t kMaxBytes = FA_MLA_STATIC_WORKSPACE_BYTES;
-constexpr int kMaxDevices = 64;
+constexpr int kMaxContexts = 256;
 
 // The workspace itself.  In host code this name is only a stand-in for the
 // symbol, never a device address: it is resolved per device below.
 static __device__ __align__(256) unsigned char g_mla_workspace[kMaxBytes];
 
+// Resolved addresses, keyed by the CUDA context they were looked up in (its
+// process-unique id): a context created after cudaDeviceReset loads the
+// module again, possibly at another address, and gets its own entry.
+struct Resolved {
+  unsigned long long ctx_id;
+  void *addr;
+};
 std::mutex g_lock;
-void *g_addr[kMaxDevices] = {};
+Resolved g_addr[kMaxContexts] = {};
+int g_count = 0;
 
 size_t round_up_256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Driver entry points looked up through the runtime, so the library does
+// not link against libcuda (it loads where no driver is installed, e.g. for
+// the host-only functions).
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long *);
+template <typename Fn>
+Fn driver_fn(const char *name) {
+  void *ptr = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return reinterpret_cast<Fn>(ptr);
+}
 
 }  // namespace
 
@@ -65,22 +91,43 @@ extern "C" int fa_mla_decode_static_workspace(const fa_mla_args *args, void *str
     return fa::record_error(FA_ERR_INVALID_ARGUMENT, msg);
   }
 
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return fa::record_error(FA_ERR_NO_DEVICE, "no current CUDA device");
+  // The context the kernels will run in: the calling thread's current one
+  // (a runtime call makes the current device's primary context current when
+  // the thread has none yet).
+  static const CtxGetCurrentFn ctx_get_current = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+  static const CtxGetIdFn ctx_get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
+  if (!ctx_get_current || !ctx_get_id)
+    return fa::record_error(FA_ERR_NO_DEVICE, "CUDA driver entry points unavailable");
+  CUcontext ctx = nullptr;
+  if (ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+    void *probe = nullptr;
+    if (cudaGetSymbolAddress(&probe, g_mla_workspace) != cudaSuccess) {
+      cudaGetLastError();
+      return fa::record_error(FA_ERR_NO_DEVICE, "no usable CUDA device");
+    }
+    if (ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+      return fa::record_error(FA_ERR_NO_DEVICE, "no current CUDA context");
+  }
+  unsigned long long ctx_id = 0;
+  if (ctx_get_id(ctx, &ctx_id) != CUDA_SUCCESS)
+    return fa::record_error(FA_ERR_CUDA, "cuCtxGetId failed");
   void *base = nullptr;
   {
     std::lock_guard<std::mutex> guard(g_lock);
-    if (g_addr[dev] == nullptr) {
+    for (int i = 0; i < g_count; ++i)
+      if (g_addr[i].ctx_id == ctx_id) base = g_addr[i].addr;
+    if (base == nullptr) {
       void *p = nullptr;
       const cudaError_t e = cudaGetSymbolAddress(&p, g_mla_workspace);
       if (e != cudaSuccess || p == nullptr) {
         cudaGetLastError();
         return fa::record_error(FA_ERR_CUDA, "cudaGetSymbolAddress of the static workspace failed");
       }
-      g_addr[dev] = p;
+      if (g_count == kMaxContexts)
+        return fa::record_error(FA_ERR_CUDA, "static workspace: too many CUDA contexts");
+      g_addr[g_count++] = Resolved{ctx_id, p};
+      base = p;
     }
-    base = g_addr[dev];
   }
   fa_mla_args a = *args;
   a.part_o = static_cast<float *>(base);

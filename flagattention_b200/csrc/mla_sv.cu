@@ -61,34 +61,6 @@ constexpr int kPSlotBytes = kPBytes + 2048;         // 18 KB
 constexpr int kPSlots = 4;
 constexpr uint32_t kColQ = 0, kColS = 256, kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;           // log2 units (factor 256)
-// MMA issue: one thread (default) or the whole warp with elect.sync.
-#ifndef FA_SV_SINGLE_ISSUE
-#define FA_SV_SINGLE_ISSUE 0
-#endif
-#if FA_SV_SINGLE_ISSUE
-#define SV_UMMA_TS umma_ts
-#define SV_UMMA_SS umma_ss
-#define SV_COMMIT tc_commit
-#define SV_COMMIT_MC tc_commit_mc
-#define SV_TMEM_CP tmem_cp_128x256b
-#define SV_ISSUER (lane == 0)
-#define SV_VOTE(x) (x)
-#else
-#define SV_UMMA_TS umma_ts_warp
-#define SV_UMMA_SS umma_ss_warp
-#define SV_COMMIT tc_commit_warp
-#define SV_COMMIT_MC tc_commit_mc_warp
-#define SV_TMEM_CP tmem_cp_128x256b_warp
-#define SV_ISSUER true
-#define SV_VOTE(x) __all_sync(0xffffffffu, (x))
-#endif
-
-#ifndef FA_SV_PREFETCH_TILES
-#define FA_SV_PREFETCH_TILES 0
-#endif
-// Distance, in 128-token tiles, of the value CTA's L2 prefetch of key rows.
-constexpr int kPrefetchTiles = FA_SV_PREFETCH_TILES;
-
 constexpr int kOffBar = 0;
 constexpr int kOffData = 1024;
 // score CTA
@@ -136,47 +108,9 @@ struct Bars {
 };
 static_assert(sizeof(Bars) <= kOffData, "barrier block");
 
-#ifdef FA_TRACE
-// Debug builds only: SM-clock timestamps of pipeline events of two parts
-// (index: tile for score-CTA events, 64-token block for value-CTA events).
-__device__ long long g_sv_trace[2][2][128][16];
-#define SV_TRACE(ev, idx)                                                             \
-  do {                                                                               \
-    const int tp_ = (part == 0 && mb == 0) ? 0 : ((part == 37 && mb == 0) ? 1 : -1); \
-    if (tp_ >= 0 && (idx) < 128) g_sv_trace[tp_][rank][(idx)][(ev)] = clock64();     \
-  } while (0)
-__device__ long long g_sv_epi[2][8][4];
-__device__ long long g_sv_mma[4][9][4];
-#define MMA_TRACE(c, ev)                                     \
-  do {                                                       \
-    const long long now_ = clock64();                        \
-    if ((ev) == 0) acc_w += now_ - t_mark;                   \
-    if ((ev) == 1) acc_i += now_ - t_mark;                   \
-    if ((ev) == 2) acc_c += now_ - t_mark;                   \
-    t_mark = now_;                                           \
-  } while (0)
-#define EPI_TRACE(ev)                                                                  \
-  do {                                                                                 \
-    if (part == 0 && mb == 0 && tt == 0 && i < 2 && c0 / cols_it < 8)                  \
-      g_sv_epi[i][c0 / cols_it][(ev)] = clock64();                                     \
-  } while (0)
-#else
-#define EPI_TRACE(ev) \
-  do {                \
-  } while (0)
-#define MMA_TRACE(c, ev) \
-  do {                   \
-  } while (0)
-#define SV_TRACE(ev, idx) \
-  do {                    \
-  } while (0)
-#endif
-
 struct Params {
-  const uint8_t *kcache;  // L2 prefetch of whole 64-token blocks (rows of 576 contiguous)
+  const uint8_t *kcache;
   int64_t kv_sp, kv_st;   // page / token strides in elements
-  const uint8_t *q;       // L2 prefetch of a piece's query rows
-  int64_t q_sb, q_sh;
   const int32_t *block_table;
   int64_t bt_stride;
   const int32_t *seq_lens;
@@ -199,6 +133,7 @@ struct Params {
   int64_t idx_sb, idx_ss;
   int32_t topk;  // 0: dense
   int64_t total_rows;
+  int32_t uniform_rows;  // sparse: pool rows at one stride (2-D gather map)
 };
 
 struct Piece {
@@ -237,26 +172,51 @@ __device__ __forceinline__ void load_rows4(const int32_t *idx, int pos, int end,
   for (int j = 0; j < 4; ++j) r[j] = (pos + j < end) ? __ldg(idx + pos + j) : -1;
 }
 
-// Sparse: this lane's invalid-row bits (row j invalid: bit j), with every
-// invalid row replaced by the first valid row of the warp's rows (real cache
-// bytes: the softmax masks the column, the value product then adds 0 times a
-// finite row).  Pool row 0 stands in when none of the warp's rows is valid.
-__device__ __forceinline__ uint32_t fix_rows4(int (&r)[4], int64_t total_rows) {
-  uint32_t bad = 0;
-  int first = -1;
-#pragma unroll
-  for (int j = 3; j >= 0; --j) {
-    if (r[j] >= 0 && r[j] < total_rows)
-      first = r[j];
-    else
-      bad |= 1u << j;
+// Sparse: the first in-range pool row of a query token's index list (-1 when
+// it has none), found by the whole warp 32 positions at a time.
+__device__ __noinline__ int first_valid_row(const int32_t *idx, int topk, int64_t total_rows) {
+  const int lane = threadIdx.x & 31;
+  for (int base = 0; base < topk; base += 32) {
+    const int r = base + lane < topk ? __ldg(idx + base + lane) : -1;
+    const unsigned ok = __ballot_sync(0xffffffffu, r >= 0 && r < total_rows);
+    if (ok) return __shfl_sync(0xffffffffu, r, __ffs(ok) - 1);
   }
-  const unsigned has = __ballot_sync(0xffffffffu, first >= 0);
-  const int sub = has ? __shfl_sync(0xffffffffu, first, __ffs(has) - 1) : 0;
+  return -1;
+}
+
+// Sparse: this lane's invalid-row bits (row j invalid: bit j), with every
+// invalid row replaced by `fallback`, a valid row of the same index list: the
+// softmax masks the column and the value product adds 0 times a row the list
+// attends anyway (finite unless the reference's own result is NaN).  A list
+// with no valid row (fallback -1) reads pool row 0, whatever it holds: every
+// weight is 0 there and the epilogue writes zeros for a row sum of 0.
+__device__ __forceinline__ uint32_t fix_rows4(int (&r)[4], int64_t total_rows, int fallback) {
+  uint32_t bad = 0;
+  const int sub = fallback >= 0 ? fallback : 0;
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
-    if ((bad >> j) & 1u) r[j] = sub;
+  for (int j = 0; j < 4; ++j) {
+    if (r[j] < 0 || r[j] >= total_rows) {
+      bad |= 1u << j;
+      r[j] = sub;
+    }
+  }
   return bad;
+}
+
+// Sparse: fetch 64 dims (from c0) of the four pool rows r[0..3] into four
+// consecutive 128-byte rows at dst.  Pools whose rows all lie at one stride
+// take one tile::gather4 over the 2-D row map; other pools (page stride !=
+// page_size x token stride) take four one-row boxes of the 3-D page map.
+__device__ __forceinline__ void gather_rows4(uint32_t dst, const CUtensorMap *map, uint32_t bar,
+                                             int c0, const int (&r)[4], bool uniform,
+                                             int page_size) {
+  if (uniform) {
+    tma_gather4(dst, map, bar, c0, r[0], r[1], r[2], r[3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      tma_load_3d(dst + j * kRowBytes, map, bar, c0, r[j] % page_size, r[j] / page_size);
+  }
 }
 
 // TMA coordinates (row in page, page) of token t of sequence b.
@@ -277,51 +237,6 @@ struct RingPos {
     if (++slot == kRing) {
       slot = 0;
       phase ^= 1u;
-    }
-  }
-};
-
-// Tiles of a part in order, for the producer's L2 prefetch that runs
-// kPrefetchTiles tiles ahead of its loads.
-struct PrefetchCursor {
-  int i = 0, tok = 0, tok_end = 0, b = 0;
-  bool first = false, valid = false;
-  __device__ __forceinline__ void seek(const Params &p, const int32_t *meta, int n_pieces) {
-    for (; i < n_pieces; ++i) {
-      const Piece pc = get_piece(p, meta, i);
-      if (pc.tok_end > pc.tok0) {
-        tok = pc.tok0;
-        tok_end = pc.tok_end;
-        b = pc.b;
-        first = valid = true;
-        return;
-      }
-    }
-    valid = false;
-  }
-  // Prefetch the cursor's tile (and the piece's query rows on its first
-  // tile), then step to the next tile.
-  __device__ __forceinline__ void issue(const Params &p, const int32_t *meta, int n_pieces,
-                                        int row0, int n_rows) {
-    if (!valid) return;
-    if (first && p.q_sh == 576)
-      bulk_prefetch_l2(p.q + (static_cast<int64_t>(b) * p.q_sb + static_cast<int64_t>(row0) * 576) * 2,
-                       n_rows * 1152);
-    first = false;
-    if (p.paged && p.kv_st == 576) {  // a 64-row block lies inside one page
-      for (int j = 0; j < 2 && tok + j * kBlk < tok_end; ++j) {
-        const int t = tok + j * kBlk;
-        int c1, c2;
-        kv_coord(p, b, t, c1, c2);
-        const int rows = min(kBlk, tok_end - t);
-        bulk_prefetch_l2(p.kcache + (static_cast<int64_t>(c2) * p.kv_sp + static_cast<int64_t>(c1) * 576) * 2,
-                         rows * 1152);
-      }
-    }
-    tok += 2 * kBlk;
-    if (tok >= tok_end) {
-      ++i;
-      seek(p, meta, n_pieces);
     }
   }
 };
@@ -419,6 +334,10 @@ __device__ __noinline__ void write_o_half(uint32_t trow, int ch, int q4, int lan
     }
   }
   const int cols_it = 128 / o.esz;  // output dims per 128-byte row segment
+  // A row whose sum is 0 attended no key (every column masked): its output
+  // is 0, written as such rather than as O * 0 (the masked value rows of a
+  // top-k list with no valid index are arbitrary pool bytes, possibly NaN).
+  const bool zero_row = !has_tiles || inv_l == 0.f;
 #pragma unroll 1
   for (int c0 = 0; c0 < 256; c0 += cols_it) {
     const int col = ch * 256 + c0;
@@ -433,7 +352,7 @@ __device__ __noinline__ void write_o_half(uint32_t trow, int ch, int q4, int lan
         for (int j = 0; j < 32; ++j) v[j] = 0.f;
       }
 #pragma unroll
-      for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j] * inv_l);
+      for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(zero_row ? 0.f : v[j] * inv_l);
     } else {
       float v0[32], v1[32];
       if (has_tiles) {
@@ -446,8 +365,8 @@ __device__ __noinline__ void write_o_half(uint32_t trow, int ch, int q4, int lan
       }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        w[j] = Elem<T>::pack2(v0[2 * j] * inv_l, v0[2 * j + 1] * inv_l);
-        w[16 + j] = Elem<T>::pack2(v1[2 * j] * inv_l, v1[2 * j + 1] * inv_l);
+        w[j] = zero_row ? 0u : Elem<T>::pack2(v0[2 * j] * inv_l, v0[2 * j + 1] * inv_l);
+        w[16 + j] = zero_row ? 0u : Elem<T>::pack2(v1[2 * j] * inv_l, v1[2 * j + 1] * inv_l);
       }
     }
 #pragma unroll
@@ -540,10 +459,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   cluster_sync();  // the peer's barriers exist before any remote access
-  if (threadIdx.x == 0) SV_TRACE(11, 127);
-#ifdef FA_TRACE
-  if (threadIdx.x == 0 && part == 0 && mb == 0) g_sv_trace[0][rank][126][0] = static_cast<long long>(global_ns());
-#endif
 
   if (rank == 0) {
     // ================================================================ score CTA
@@ -610,6 +525,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ++qi;
           const int32_t *idx = p.indices + static_cast<int64_t>(pc.b) * p.idx_sb +
                                static_cast<int64_t>(mb) * p.idx_ss;
+          const int fb = first_valid_row(idx, p.topk, p.total_rows);
           int nr[4] = {-1, -1, -1, -1};  // the next tile's rows, loaded one tile ahead
           if (has_rg) load_rows4(idx, pc.tok0 + 4 * rg, pc.tok_end, nr);
           for (int tok = pc.tok0; tok < pc.tok_end && ok; tok += 2 * kBlk, ++tg) {
@@ -617,7 +533,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             int r[4] = {nr[0], nr[1], nr[2], nr[3]};
             if (has_rg && tok + 2 * kBlk < pc.tok_end)
               load_rows4(idx, tok + 2 * kBlk + 4 * rg, pc.tok_end, nr);
-            const uint32_t bad = fix_rows4(r, p.total_rows);
+            const uint32_t bad = fix_rows4(r, p.total_rows, fb);
             if (has_rg) bars->inval[tg & 3u][rg] = static_cast<uint8_t>(bad);
             if (warp == 0) {  // S buffer release before the tile's first chunk is armed
               bool okw = true;
@@ -631,8 +547,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               const uint32_t full = take_slot(n_blk * kBoxBytes);
               if (!(ok = full != 0xffffffffu)) break;
               if (has_rg && rg < n_blk * 16)
-                tma_gather4(ring + rp.slot * kChunkBytes + rg * 4 * kRowBytes, &g_map, full,
-                            64 * c, r[0], r[1], r[2], r[3]);
+                gather_rows4(ring + rp.slot * kChunkBytes + rg * 4 * kRowBytes, &g_map, full,
+                             64 * c, r, p.uniform_rows, p.page_size);
               rp.next();
             }
           }
@@ -700,8 +616,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             for (int c = 0; c < kKChunks; ++c) {
               const uint32_t full = next_slot(n_blk * kBoxBytes);
               if (!(ok = full != 0xffffffffu)) break;
-              if (c == 0) SV_TRACE(0, tg);
-              if (c == kKChunks - 1) SV_TRACE(1, tg);
               for (int j = 0; j < n_blk; ++j)
                 tma_load_3d(ring + rp.slot * kChunkBytes + j * kBoxBytes, &kv_map, full, 64 * c,
                             c1[j], c2[j]);
@@ -722,11 +636,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       __syncwarp();
     } else if (warp == 1) {
       // -------------------------------------------------------- MMA issuer
-      // One thread issues every MMA / copy / commit (FA_SV_SINGLE_ISSUE), or
-      // the whole warp runs the loop and an elected lane issues.
-      // The instruction descriptor must be a compile-time constant: a runtime
-      // one costs about 40 extra cycles per MMA.
-      if (SV_ISSUER) {
+      // The whole warp runs the loop and an elected lane issues each MMA /
+      // copy / commit.  The instruction descriptor must be a compile-time
+      // constant: a runtime one costs about 40 extra cycles per MMA.
+      {
       constexpr uint32_t kIdesc128 = umma_idesc_f16(128, 128, fmt, 0);
       const uint64_t ring_desc = smem_desc_sw128(ring, 16, 1024);
       const uint64_t rope_desc = smem_desc_sw128(qrope, 16, 1024);
@@ -734,46 +647,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // fast path: the phase is usually complete already (one test_wait,
         // uniform across the warp); otherwise the bounded wait
         if (mbar_probe(bar, parity)) return true;
-        return SV_VOTE(mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma)) != 0;
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma)) != 0;
       };
       RingPos rp;
       uint32_t g = 0;
       int qi = 0;
       bool ok = true;
-#ifdef FA_TRACE
-      long long acc_w = 0, acc_i = 0, acc_c = 0, acc_g = 0, t_mark = clock64();
-#endif
       // QK of one tile into S buffer sd: 8 latent chunks (A = Q from TMEM)
       // and the rope chunk (A = rope Q from shared memory).
       auto qk_tile = [&](auto idesc_tag, uint32_t sd, uint64_t rope_a) -> bool {
         constexpr uint32_t idesc = decltype(idesc_tag)::value;
 #pragma unroll 1
         for (int c = 0; c < kKChunks; ++c) {
-#ifdef FA_TRACE
-          {
-            const long long now_ = clock64();
-            acc_g += now_ - t_mark;  // loop overhead since the previous commit
-            t_mark = now_;
-          }
-#endif
           if (!wait(smem_u32(&bars->ch_full[rp.slot]), rp.phase)) return false;
           if (c == 0) tc_fence_after();  // after the S buffer release (through the producer)
-          MMA_TRACE(c, 0);
           // TMA data signalled by the mbarrier: no tcgen05 fence here (one
           // after every chunk drains the MMA queue and halves the rate)
           const uint64_t kdesc = ring_desc + static_cast<uint64_t>((rp.slot * kChunkBytes) >> 4);
           if (c < kQChunks) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              SV_UMMA_TS(sd, tmem + kColQ + c * 32 + kk * 8, kdesc + 2 * kk, idesc,
+              umma_ts_warp(sd, tmem + kColQ + c * 32 + kk * 8, kdesc + 2 * kk, idesc,
                            (c | kk) ? 1u : 0u);
           } else {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) SV_UMMA_SS(sd, rope_a + 2 * kk, kdesc + 2 * kk, idesc, 1u);
+            for (int kk = 0; kk < 4; ++kk) umma_ss_warp(sd, rope_a + 2 * kk, kdesc + 2 * kk, idesc, 1u);
           }
-          MMA_TRACE(c, 1);
-          SV_COMMIT(smem_u32(&bars->ch_empty[rp.slot]));
-          MMA_TRACE(c, 2);
+          tc_commit_warp(smem_u32(&bars->ch_empty[rp.slot]));
           rp.next();
         }
         return true;
@@ -788,13 +688,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (!ok) break;
           const uint64_t qdesc = ring_desc + static_cast<uint64_t>((rp.slot * kChunkBytes) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) SV_TMEM_CP(tmem + kColQ + c * 32 + kk * 8, qdesc + 2 * kk);
-          SV_COMMIT(smem_u32(&bars->ch_empty[rp.slot]));
+          for (int kk = 0; kk < 4; ++kk) tmem_cp_128x256b_warp(tmem + kColQ + c * 32 + kk * 8, qdesc + 2 * kk);
+          tc_commit_warp(smem_u32(&bars->ch_empty[rp.slot]));
           rp.next();
         }
         ok = ok && wait(smem_u32(&bars->rope_full[qi & 1]), (qi >> 1) & 1);
         if (!ok) break;
-        SV_TRACE(9, qi);
         const uint64_t rope_a = rope_desc + static_cast<uint64_t>(((qi & 1) * kChunkBytes) >> 4);
         for (int tok = pc.tok0; tok < pc.tok_end && ok; tok += 2 * kBlk, ++g) {
           const uint32_t buf = g & 1u;
@@ -805,31 +704,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           // the softmax's reads.  Waiting on s_empty here instead costs about
           // 800 cycles of tensor-pipe time per tile (measured), even when the
           // phase is already complete.
-          SV_TRACE(2, g);
           // A half tile at a piece end (only its first 64 key rows loaded)
           // runs the same N = 128 MMAs: the other 64 rows of the ring slot
           // hold stale but valid bytes, and their score columns are masked
           // (select) by the softmax.  One instantiation keeps the loop small.
           ok = qk_tile(std::integral_constant<uint32_t, kIdesc128>{}, sd, rope_a);
           if (!ok) break;
-          SV_TRACE(3, g);
-#ifdef FA_TRACE
-          if (part == 0 && mb == 0 && g < 128 && lane == 0) {
-            g_sv_trace[0][0][g][12] = acc_w;
-            g_sv_trace[0][0][g][13] = acc_i;
-            g_sv_trace[0][0][g][14] = acc_c;
-            g_sv_trace[0][0][g][15] = acc_g;
-          }
-          acc_w = acc_i = acc_c = acc_g = 0;
-#endif
-          SV_COMMIT(smem_u32(&bars->s_full[buf]));
+          tc_commit_warp(smem_u32(&bars->s_full[buf]));
         }
         if (!ok) break;
-        SV_COMMIT(smem_u32(&bars->rope_empty[qi & 1]));
+        tc_commit_warp(smem_u32(&bars->rope_empty[qi & 1]));
         ++qi;
       }
       // every issued MMA must finish before TMEM is released
-      SV_COMMIT(smem_u32(&bars->drain));
+      tc_commit_warp(smem_u32(&bars->drain));
       volatile int never = 0;
       mbar_wait(smem_u32(&bars->drain), 0, &never, p.status, kDevTimeoutDrain);
       }
@@ -878,7 +766,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->s_full[buf]), (g >> 1) & 1,
                                                   abort_flag, p.status, kDevTimeoutSoftmax));
           if (!ok) break;
-          if (lane == 0 && q4 == 0) SV_TRACE(4 + ch, g);
           tc_fence_after();
           float sc[64];
           {
@@ -928,7 +815,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           float *rslot = red + (g & 1u) * 2 * kRows;
           rslot[ch * kRows + t] = mraw;
           if (!(ok = pair_sync())) break;
-          if (t == 0 && ch == 0) SV_TRACE(6, g);
           mraw = fmaxf(mraw, rslot[(ch ^ 1) * kRows + t]);
           // online softmax with a lazily updated running max (log2 units)
           const float mt = mraw * p.scale_log2;
@@ -978,7 +864,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                                      ((pb - 2) / kPSlots) & 1, abort_flag,
                                                      p.status, kDevTimeoutSoftmax));
             if (!ok) break;
-            if (lane == 0 && q4 == 0) SV_TRACE(7 + ch, g);
             const uint32_t stg = s_base + kOffStgP + (pb & 1) * kPBytes;
 #pragma unroll
             for (int u = 0; u < 8; ++u)
@@ -1052,6 +937,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                static_cast<int64_t>(mb) * p.idx_ss;
           // stages start at tok0, tok0 + 32, ... (< tok_end); their rows are
           // loaded two stages ahead
+          const int fb = first_valid_row(idx, p.topk, p.total_rows);
           int n1[4] = {-1, -1, -1, -1}, n2[4] = {-1, -1, -1, -1};
           if (has_q) {
             load_rows4(idx, pc.tok0 + 4 * rg, pc.tok_end, n1);
@@ -1066,7 +952,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               for (int k = 0; k < 4; ++k) n1[k] = n2[k];
               const int ahead = bt + kVRows * (j + 2);
               if (has_q && ahead < pc.tok_end) load_rows4(idx, ahead + 4 * rg, pc.tok_end, n2);
-              fix_rows4(r, p.total_rows);
+              fix_rows4(r, p.total_rows, fb);
               const int st = vs % kVStages;
               const uint32_t full = smem_u32(&bars->v_full[st]);
               bool okw = true;
@@ -1077,8 +963,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               }
               if (!(ok = __shfl_sync(0xffffffffu, okw ? 1 : 0, 0) != 0)) break;
               if (has_q)
-                tma_gather4(vbase + st * kVStageBytes + d * kVChunkBytes + rg * 4 * kRowBytes,
-                            &g_map, full, 64 * d, r[0], r[1], r[2], r[3]);
+                gather_rows4(vbase + st * kVStageBytes + d * kVChunkBytes + rg * 4 * kRowBytes,
+                             &g_map, full, 64 * d, r, p.uniform_rows, p.page_size);
             }
           }
         }
@@ -1091,30 +977,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       } else {
       if (lane == 0) {
         tma_prefetch_desc(&v_map);
-        uint32_t vs = 0, vbk = 0xffffffffu;
+        uint32_t vs = 0;
         bool ok = true;
-        // L2 prefetch of whole key blocks kPrefetchTiles tiles ahead of this
-        // producer: the value CTA's copy engine takes the HBM misses, so the
-        // score CTA's loads (and this CTA's own) hit L2.
-        PrefetchCursor pf;
-        pf.seek(p, meta, n_pieces);
-        for (int k = 0; k < kPrefetchTiles; ++k) pf.issue(p, meta, n_pieces, row0, n_rows);
         for (int i = 0; i < n_pieces && ok; ++i) {
           const Piece pc = get_piece(p, meta, i);
           for (int bt = pc.tok0; bt < pc.tok_end && ok; bt += kBlk) {
-            if (kPrefetchTiles > 0 && ((bt - pc.tok0) & (2 * kBlk - 1)) == 0)
-              pf.issue(p, meta, n_pieces, row0, n_rows);
             const int vb = min(kBlk, pc.tok_end - bt);
             const int n_sub = vb > kVRows ? 2 : 1;
             int c1, c2;
             kv_coord(p, pc.b, bt, c1, c2);
-            ++vbk;
             for (int j = 0; j < n_sub; ++j, ++vs) {
               const int st = vs % kVStages;
               ok = mbar_wait(smem_u32(&bars->v_empty[st]), ((vs / kVStages) & 1) ^ 1, abort_flag,
                              p.status, kDevTimeoutProducer);
               if (!ok) break;
-              if (j == 0) SV_TRACE(14, vbk);
               const uint32_t full = smem_u32(&bars->v_full[st]);
               mbar_arrive_expect_tx(full, kVStageBytes);
 #pragma unroll
@@ -1135,8 +1011,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       __syncwarp();
     } else if (warp == 1) {
       // ----------------------------------------------------- PV MMA issuer
-      // Issued like the score CTA's MMAs (one thread, or the elected lane).
-      if (SV_ISSUER) {
+      // Issued like the score CTA's MMAs (warp-wide, elected lane).
+      {
       constexpr uint32_t idesc = umma_idesc_f16(128, 256, fmt, 1);
       const uint64_t p_desc = smem_desc_sw128(pbase, 16, 1024);
       const uint64_t v_desc = smem_desc_sw128(vbase, kVChunkBytes, 1024);
@@ -1144,7 +1020,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // fast path: the phase is usually complete already (one test_wait,
         // uniform across the warp); otherwise the bounded wait
         if (mbar_probe(bar, parity)) return true;
-        return SV_VOTE(mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma)) != 0;
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma)) != 0;
       };
       uint32_t vs = 0, gb = 0;
       int pi = 0;
@@ -1164,9 +1040,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_arrive_expect_tx(smem_u32(&bars->p_full[ps]),
                                   kPBytes + (tile_first ? 512 + 16 : 0) + (piece_last ? 512 : 0));
           ok = wait(smem_u32(&bars->p_full[ps]), ph);
-          SV_TRACE(10, gb);
           ok = ok && wait(smem_u32(&bars->m_read[ps]), ph);
-          SV_TRACE(11, gb);
           if (ok && first_blk) ok = wait(smem_u32(&bars->o_empty), (pi & 1) ^ 1);
           if (!ok) break;
           fence_proxy_async_smem();  // st.async / cleared rows -> tensor-core reads
@@ -1182,21 +1056,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               const uint64_t adesc = pa + static_cast<uint64_t>(((2 * j + kk) * 32) >> 4);
 #pragma unroll
               for (int hh = 0; hh < 2; ++hh)
-                SV_UMMA_SS(tmem + 256 * hh, adesc,
+                umma_ss_warp(tmem + 256 * hh, adesc,
                              vd + static_cast<uint64_t>((hh * 4 * kVChunkBytes + kk * 16 * kRowBytes) >> 4),
                              idesc, (first_blk && j == 0 && kk == 0) ? 0u : 1u);
             }
-            SV_COMMIT(smem_u32(&bars->v_empty[st]));
+            tc_commit_warp(smem_u32(&bars->v_empty[st]));
           }
           if (!ok) break;
-          SV_TRACE(12, gb);
-          SV_COMMIT(smem_u32(&bars->pv_done[ps]));
-          SV_COMMIT_MC(smem_u32(&bars->p_free[ps]), 0x1);  // the score CTA may refill the slot
+          tc_commit_warp(smem_u32(&bars->pv_done[ps]));
+          tc_commit_mc_warp(smem_u32(&bars->p_free[ps]), 0x1);  // the score CTA may refill the slot
           first_blk = false;
         }
         ++pi;
       }
-      SV_COMMIT(smem_u32(&bars->drain));
+      tc_commit_warp(smem_u32(&bars->drain));
       volatile int never = 0;
       mbar_wait(smem_u32(&bars->drain), 0, &never, p.status, kDevTimeoutDrain);
       }
@@ -1227,7 +1100,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->p_full[ps]), ph, abort_flag,
                                                   p.status, kDevTimeoutSoftmax));
           if (!ok) break;
-          if (tt == 0) SV_TRACE(13, gb);
           const uint8_t *slotp = smem + kOffP + ps * kPSlotBytes;
           if (tile_first && bt != pc.tok0) {
             const int *fl = reinterpret_cast<const int *>(slotp + kMetaFlags);
@@ -1262,12 +1134,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             fence_proxy_async_smem();
           }
           tc_fence_before();
-          if (tt == 0) SV_TRACE(15, gb);
           mbar_arrive(smem_u32(&bars->m_read[ps]));
           vs += n_sub;
         }
         if (!ok) break;
-        if (tt == 0) SV_TRACE(0, 120 + i);
         if (has_tiles) {
           const uint32_t lg = gb - 1;
           ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done[lg % kPSlots]),
@@ -1291,10 +1161,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         o.split = !final_out;
         o.split_row0 = static_cast<int64_t>(slot_o) * rows_total;
         o.d_v = p.d_v;
-        if (tt == 0) SV_TRACE(1, 120 + i);
         write_o_half<T>(trow, ch, q4, lane, smem_u32(smem + kOffStage + (warp - 4) * kStageWarpBytes),
                         has_tiles, inv_l, o);
-        if (tt == 0) SV_TRACE(2, 120 + i);
         if (has_tiles) {
           tc_fence_before();
           mbar_arrive(smem_u32(&bars->o_empty));
@@ -1306,10 +1174,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // -------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) SV_TRACE(12, 127);
-#ifdef FA_TRACE
-  if (threadIdx.x == 0 && part == 0 && mb == 0) g_sv_trace[0][rank][126][1] = static_cast<long long>(global_ns());
-#endif
   cluster_sync();  // the peer no longer touches this CTA's shared memory
   if (warp == 1) {
     tc_fence_after();
@@ -1319,23 +1183,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 }  // namespace sv
 
-#ifdef FA_TRACE
-extern "C" int fa_debug_sv_mma_read(void *dst, size_t bytes) {
-  return cudaMemcpyFromSymbol(dst, sv::g_sv_mma,
-                              bytes < sizeof(sv::g_sv_mma) ? bytes : sizeof(sv::g_sv_mma)) ==
-                 cudaSuccess ? 0 : -1;
-}
-extern "C" int fa_debug_sv_epi_read(void *dst, size_t bytes) {
-  return cudaMemcpyFromSymbol(dst, sv::g_sv_epi,
-                              bytes < sizeof(sv::g_sv_epi) ? bytes : sizeof(sv::g_sv_epi)) ==
-                 cudaSuccess ? 0 : -1;
-}
-extern "C" int fa_debug_sv_trace_read(void *dst, size_t bytes) {
-  return cudaMemcpyFromSymbol(dst, sv::g_sv_trace,
-                              bytes < sizeof(sv::g_sv_trace) ? bytes : sizeof(sv::g_sv_trace)) ==
-                 cudaSuccess ? 0 : -1;
-}
-#endif
 
 // q_map: query (box 64 dims x 128 rows), kv_map: key rows (box 64 x 64),
 // v_map: value rows (box 64 x 32); all 128-byte swizzle over the same layouts
@@ -1363,9 +1210,6 @@ cudaError_t launch_mla_sv(const CUtensorMap &qm, const CUtensorMap &km, const CU
   p.kcache = static_cast<const uint8_t *>(a->kcache);
   p.kv_sp = a->kv_stride_page;
   p.kv_st = a->kv_stride_tok;
-  p.q = static_cast<const uint8_t *>(a->q);
-  p.q_sb = a->q_stride_b;
-  p.q_sh = a->q_stride_h;
   p.block_table = a->block_table;
   p.bt_stride = a->bt_stride;
   p.seq_lens = a->seq_lens;
@@ -1395,6 +1239,7 @@ cudaError_t launch_mla_sv(const CUtensorMap &qm, const CUtensorMap &km, const CU
   p.idx_ss = a->idx_stride_s;
   p.topk = sparse ? a->topk : 0;
   p.total_rows = static_cast<int64_t>(a->num_pages) * a->page_size;
+  p.uniform_rows = a->kv_stride_page == static_cast<int64_t>(a->page_size) * a->kv_stride_tok;
   const dim3 grid(2 * a->num_sm_parts, m_blocks);
   if (a->dtype == FA_DTYPE_F16)
     return sparse ? launch_sv_t<__half, true>(qm, km, vm, gm, p, grid, stream)

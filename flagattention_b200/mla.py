@@ -206,6 +206,8 @@ def append_kv_rows(kv_rows, k_cache, slot_mapping):
         raise _lib.InvalidArgument("k_cache must be [num_blocks, page_size, 1, 576]")
     if kv_rows.dtype != k_cache.dtype:
         raise _lib.InvalidArgument("kv_rows and k_cache dtypes differ")
+    if k_cache.stride(-1) != 1:
+        raise _lib.InvalidArgument("k_cache must have a unit inner stride (576 contiguous dims)")
     if slot_mapping.dtype != torch.int64 or slot_mapping.dim() != 1 or \
             slot_mapping.shape[0] != kv_rows.shape[0]:
         raise _lib.InvalidArgument("slot_mapping must be int64 [n]")

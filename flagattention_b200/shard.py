@@ -8,9 +8,10 @@ is what makes both modes exact:
   nothing on the data path: no collective.
 * **Long-context decode** -- ``page_range`` gives each rank an even,
   contiguous range of one sequence's KV pages.  Every rank decodes its range to
-  an f32 partial (O, LSE); ``exchange_partials`` all-gathers them (NCCL over
-  NVLink on GPUs, any backend in tests) and ``merge_partials`` runs the
-  log-sum-exp combine kernel on every rank.
+  an f32 partial (O, LSE) packed in one buffer; ``exchange_partials``
+  all-gathers the buffers in one collective (NCCL over NVLink on GPUs, any
+  backend in tests) and ``merge_partials`` runs the log-sum-exp combine
+  kernel over them on every rank.
 """
 
 import ctypes
@@ -83,54 +84,87 @@ def new_group_with_timeout(backend, seconds, **kw):
     dist.init_process_group(backend, timeout=datetime.timedelta(seconds=seconds), **kw)
 
 
-def exchange_partials(part_o, part_lse, group=None):
-    """All-gather each rank's partial (O, LSE) -> ([world, ...], [world, ...])."""
+def packed_partial(batch, h_q, d_v=512, device=None):
+    """One rank's partial result of a KV-page-sharded decode, in the layout
+    that travels between GPUs: f32 [batch*h_q*d_v + batch*h_q], the O rows
+    (b, h) first, then their LSEs in the same row order."""
+    return torch.empty(batch * h_q * (d_v + 1), dtype=torch.float32, device=device)
+
+
+def unpack_partial(packed, batch, h_q, d_v=512):
+    """Views (O [batch, 1, h_q, d_v], LSE [batch, h_q, 1]) of a packed partial."""
+    rows = batch * h_q
+    return (packed[:rows * d_v].view(batch, 1, h_q, d_v),
+            packed[rows * d_v:rows * (d_v + 1)].view(batch, h_q, 1))
+
+
+def exchange_partials(packed, group=None):
+    """All-gather every rank's packed partial with ONE collective (NCCL over
+    NVLink on GPUs, any backend in tests): returns f32 [world, packed.numel()],
+    rank r's partial in row r."""
     world = dist.get_world_size(group)
-    os_ = [torch.empty_like(part_o) for _ in range(world)]
-    ls_ = [torch.empty_like(part_lse) for _ in range(world)]
-    dist.all_gather(os_, part_o.contiguous(), group=group)
-    dist.all_gather(ls_, part_lse.contiguous(), group=group)
-    return torch.stack(os_), torch.stack(ls_)
+    gathered = torch.empty(world * packed.numel(), dtype=packed.dtype, device=packed.device)
+    dist.all_gather_into_tensor(gathered, packed.contiguous(), group=group)
+    return gathered.view(world, packed.numel())
 
 
-def merge_partials(all_o, all_lse, out_dtype=torch.bfloat16):
-    """Log-sum-exp merge of gathered partials on the GPU (fa_lse_combine).
+def merge_partials(gathered, rows, d_v=512, out_dtype=torch.bfloat16):
+    """Log-sum-exp merge of gathered packed partials on the GPU
+    (fa_lse_combine_strided, the algebra of split_kv.py:198-228).
 
-    all_o: f32 [P, rows..., d_v]; all_lse: f32 [P, rows...].  Returns
-    (out [rows..., d_v] of out_dtype, lse f32 [rows...]).
+    gathered: f32 [P, rows*(d_v+1)] (``exchange_partials``).  Returns
+    (out [rows, d_v] of out_dtype, lse f32 [rows]).
     """
-    P = all_o.shape[0]
-    d_v = all_o.shape[-1]
-    rows = all_lse[0].numel()
-    all_o = all_o.contiguous()
-    all_lse = all_lse.contiguous()
-    out = torch.empty(all_o.shape[1:], dtype=out_dtype, device=all_o.device)
-    lse = torch.empty(all_lse.shape[1:], dtype=torch.float32, device=all_o.device)
-    _lib.check(_lib.lib().fa_lse_combine(ctypes.c_void_p(all_o.data_ptr()),
-                                         ctypes.c_void_p(all_lse.data_ptr()), P, rows, d_v,
-                                         ctypes.c_void_p(out.data_ptr()), dtype_code(out),
-                                         ctypes.c_void_p(lse.data_ptr()), stream_of(out)),
-               "fa_lse_combine")
+    P, n = gathered.shape
+    if n != rows * (d_v + 1):
+        raise _lib.InvalidArgument(f"packed partials of {n} floats, expected rows*(d_v+1)")
+    gathered = gathered.contiguous()
+    out = torch.empty((rows, d_v), dtype=out_dtype, device=gathered.device)
+    lse = torch.empty((rows,), dtype=torch.float32, device=gathered.device)
+    base = gathered.data_ptr()
+    _lib.check(_lib.lib().fa_lse_combine_strided(ctypes.c_void_p(base), n,
+                                                 ctypes.c_void_p(base + rows * d_v * 4), n, P,
+                                                 rows, d_v, ctypes.c_void_p(out.data_ptr()),
+                                                 dtype_code(out), ctypes.c_void_p(lse.data_ptr()),
+                                                 stream_of(out)),
+               "fa_lse_combine_strided")
     return out, lse
 
 
-def decode_partial(q, kcache, block_table, seq_lens, softmax_scale=None):
-    """One rank's share of a KV-page-sharded decode: f32 partial (O, LSE).
+class PartialDecode:
+    """One rank's share of a KV-page-sharded decode, bound once: the decode
+    writes its f32 partial (O, LSE) straight into the packed buffer that the
+    all-gather sends, so no copy sits between the kernel and the collective.
 
-    q [B, 1, h_q, 576] (replicated); kcache / block_table / seq_lens describe
-    the tokens this rank holds (``shard_pages``).  Returns (part_o f32
-    [B, 1, h_q, 512], part_lse f32 [B, 1, h_q]); a rank holding no token of a
-    sequence gives O = 0 and LSE = -inf there, which the merge ignores.
+    q [B, 1, h_q, 576] (replicated on every rank); kcache / block_table /
+    seq_lens describe the tokens this rank holds (``shard_pages``).  A rank
+    holding no token of a sequence gives O = 0 and LSE = -inf there, which
+    the merge ignores.
     """
-    from flagattention_b200.mla import flash_mla_with_kvcache, get_mla_metadata
-    B, s_q, h_q, _ = q.shape
-    if s_q != 1:
-        raise _lib.Unsupported("KV-page sharding is implemented for s_q == 1 (non-causal)")
-    meta, splits = get_mla_metadata(seq_lens, s_q * h_q, 1)
-    part_o = torch.empty((B, s_q, h_q, 512), dtype=torch.float32, device=q.device)
-    _, lse = flash_mla_with_kvcache(q, kcache, block_table, seq_lens, 512, meta, splits,
-                                    softmax_scale=softmax_scale, out=part_o)
-    return part_o, lse.transpose(1, 2).contiguous()     # lse rows ordered like part_o
+
+    def __init__(self, q, kcache, block_table, seq_lens, softmax_scale=None, num_sm_parts=None):
+        from flagattention_b200.mla import MlaCall, get_mla_metadata
+        B, s_q, h_q, _ = q.shape
+        if s_q != 1:
+            raise _lib.Unsupported("KV-page sharding is implemented for s_q == 1 (non-causal)")
+        self.batch, self.h_q = B, h_q
+        meta, splits = get_mla_metadata(seq_lens, s_q * h_q, 1,
+                                        num_sm_parts_override=num_sm_parts)
+        self.packed = packed_partial(B, h_q, 512, q.device)
+        o, lse = unpack_partial(self.packed, B, h_q)
+        scale = 576 ** -0.5 if softmax_scale is None else softmax_scale
+        self.call = MlaCall(q, kcache, kcache.stride(0), kcache.stride(1), kcache.shape[0],
+                            kcache.shape[1], block_table, seq_lens, 0, meta, splits, o, lse, scale)
+
+    def run(self):
+        """Decode into ``self.packed`` (asynchronous on the current stream)."""
+        self.call.run()
+        return self.packed
+
+
+def decode_partial(q, kcache, block_table, seq_lens, softmax_scale=None):
+    """One rank's packed f32 partial (see ``PartialDecode``)."""
+    return PartialDecode(q, kcache, block_table, seq_lens, softmax_scale).run()
 
 
 def long_context_decode(q, kcache, block_table, seq_lens, softmax_scale=None, group=None):
@@ -138,10 +172,13 @@ def long_context_decode(q, kcache, block_table, seq_lens, softmax_scale=None, gr
 
     Each rank passes its own shard: ``kcache`` / ``block_table`` / ``seq_lens``
     describe the tokens it holds (``shard_pages``).  q [B, 1, h_q, 576] is
-    replicated.  Returns (out [B, 1, h_q, 512] of q's dtype, lse f32
-    [B, h_q, 1]) identical on every rank.
+    replicated.  Each rank decodes its pages into a packed partial, one
+    all-gather exchanges the partials, and every rank merges them on its GPU.
+    Returns (out [B, 1, h_q, 512] of q's dtype, lse f32 [B, h_q, 1]),
+    identical on every rank.
     """
-    part_o, part_lse = decode_partial(q, kcache, block_table, seq_lens, softmax_scale)
-    all_o, all_l = exchange_partials(part_o, part_lse, group)
-    out, lse_m = merge_partials(all_o, all_l, q.dtype)
-    return out, lse_m.transpose(1, 2).contiguous()
+    B, _, h_q, _ = q.shape
+    packed = decode_partial(q, kcache, block_table, seq_lens, softmax_scale)
+    gathered = exchange_partials(packed, group)
+    out, lse = merge_partials(gathered, B * h_q, 512, q.dtype)
+    return out.view(B, 1, h_q, 512), lse.view(B, h_q, 1)

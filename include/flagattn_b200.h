@@ -16,7 +16,9 @@
  *   fa_split_kv_attention     split_kv.py:279-344 and flash.py:72-143 (the
  *                             split-KV flash-decoding path that returns LSE)
  *   fa_split_kv_num_splits    split_kv.py:247-276 (num_splits_herustic)
- *   fa_lse_combine            split_kv.py:176-241 (_fwd_combine_kv_splits)
+ *   fa_lse_combine            split_kv.py:176-241 (_fwd_combine_kv_splits);
+ *                             fa_lse_combine_strided is the same merge over
+ *                             partials gathered from several GPUs
  *   fa_mla_get_metadata       no reference function: the FlashMLA-style
  *                             metadata call (get_mla_metadata) that the MLA
  *                             decode path needs; format defined in this file
@@ -136,6 +138,17 @@ int fa_split_kv_attention(const fa_decode_args *args, void *stream);
 int fa_lse_combine(const float *part_o, const float *part_lse, int num_parts,
                    int64_t rows, int d_v, void *o, int dtype, float *lse,
                    void *stream);
+/* fa_lse_combine with the partials at any distance from one another (in
+ * f32 elements): partial p of row r has its O at part_o + p*o_part_stride +
+ * r*d_v and its LSE at part_lse + p*lse_part_stride + r.  One buffer per
+ * part holding [O rows | LSE rows] (o_part_stride == lse_part_stride ==
+ * rows*(d_v+1), part_lse = part_o + rows*d_v) is what an all-gather of each
+ * GPU's packed partial delivers (split_kv.py:198-228 merged across GPUs).
+ * o_part_stride must be a multiple of 4 and at least rows*d_v. */
+int fa_lse_combine_strided(const float *part_o, int64_t o_part_stride,
+                           const float *part_lse, int64_t lse_part_stride,
+                           int num_parts, int64_t rows, int d_v, void *o,
+                           int dtype, float *lse, void *stream);
 
 /* ---- MLA decode (tensor-core path) --------------------------------------
  * q      [batch][s_q][h_q][d_qk]   (q_stride_* in elements, last dim dense)
@@ -200,7 +213,8 @@ int fa_mla_combine(const fa_mla_args *args, void *stream);
 
 /* Write n latent rows (576 dims, bf16 / f16 as dtype; row r at
  * rows + r * rows_stride elements, unit inner stride) into the pool row
- * slots[r] = page * page_size + offset of kcache (layout as in fa_mla_args).
+ * slots[r] = page * page_size + offset of kcache (layout as in fa_mla_args;
+ * each pool row's 576 dims contiguous: unit inner stride).
  * A negative slot, or one at or past num_pages * page_size, skips its row.
  * Slots must be distinct (two rows aimed at one slot race).  rows / kcache
  * 16-byte aligned, slots (int64) 8-byte aligned, strides multiples of 8
@@ -227,8 +241,9 @@ int fa_selftest_wait_timeout(int32_t *status, void *stream);
  * exit).  Calls needing more ((batch + num_sm_parts) * s_q * h_q * (d_v + 1)
  * * 4 bytes, rounded) return FA_ERR_INVALID_ARGUMENT with the sizes in
  * fa_last_error().  All calls on a device share the array: calls that
- * overlap on the GPU race.  The first call on a device resolves the array's
- * address; make it before capturing work into a stream. */
+ * overlap on the GPU race.  The first call in a CUDA context (once per
+ * device, and again after cudaDeviceReset) resolves the array's address;
+ * make it before capturing work into a stream. */
 #define FA_MLA_STATIC_WORKSPACE_BYTES (48u << 20)
 int fa_mla_decode_static_workspace(const fa_mla_args *args, void *stream);
 

@@ -27,7 +27,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 from inputs import digest, mla_inputs, paged_pool, round_bf16, sparse_indices  # noqa: E402
 
-sys.path.insert(0, os.environ.get("FLAG_ATTN_SRC", "/root/reference/src"))
+if not os.environ.get("FLAG_ATTN_SRC"):
+    sys.exit("set FLAG_ATTN_SRC to the reference's src/ directory (the one holding flag_attn/)")
+sys.path.insert(0, os.environ["FLAG_ATTN_SRC"])
 import flag_attn  # noqa: E402
 import flag_attn.paged  # noqa: E402
 from flag_attn.split_kv import num_splits_herustic  # noqa: E402

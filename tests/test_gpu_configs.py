@@ -132,18 +132,17 @@ def test_config4_sparse_full_size_sampled():
 
 def _sharded_on_one_gpu(q, kc, bt, lens, world):
     """KV-page sharding with the ranks run one after another on this GPU:
-    decode_partial per rank, partials stacked in rank order (what the
-    all-gather delivers), merged by the combine kernel in f32."""
-    parts_o, parts_l = [], []
+    each rank's decode into its packed partial, the partials stacked in rank
+    order (what the all-gather delivers), merged by the combine kernel in f32."""
+    packed = []
     for rank in range(world):
         lbt, llen = shard.shard_pages(bt, lens, PAGE, world, rank)
-        po, pl = shard.decode_partial(q, kc, torch.from_numpy(lbt).cuda(),
-                                      torch.from_numpy(llen).cuda(), SCALE)
-        parts_o.append(po)
-        parts_l.append(pl)
-    out, lse = shard.merge_partials(torch.stack(parts_o), torch.stack(parts_l), torch.float32)
+        packed.append(shard.decode_partial(q, kc, torch.from_numpy(lbt).cuda(),
+                                           torch.from_numpy(llen).cuda(), SCALE))
+    B, h_q = q.shape[0], q.shape[2]
+    out, lse = shard.merge_partials(torch.stack(packed), B * h_q, D_V, torch.float32)
     torch.cuda.synchronize()
-    return out, lse.transpose(1, 2)
+    return out.view(B, 1, h_q, D_V), lse.view(B, h_q, 1)
 
 
 @pytest.mark.parametrize("world", [2, 3, 8])
@@ -214,15 +213,24 @@ def _nccl_worker(rank, world, port, outdir):
         raise
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
-                    reason="needs 2 GPUs")
-def test_long_context_nccl_two_gpus(tmp_path):
-    """Real 2-rank KV-page sharding: NCCL all-gather of partials + combine."""
+def _gpus():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_long_context_nccl(tmp_path, world):
+    """Real multi-rank KV-page sharding, one process per GPU: each rank
+    decodes its page range into a packed partial, one NCCL all-gather
+    exchanges them, every rank merges; all ranks agree bit for bit and match
+    the oracle's unsharded decode."""
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, str(tmp_path)))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -233,13 +241,14 @@ def test_long_context_nccl_two_gpus(tmp_path):
         p.join(10)
     errs = [f.read_text() for f in tmp_path.glob("*.err")]
     assert not hung and all(p.exitcode == 0 for p in procs), errs
-    z0, z1 = np.load(tmp_path / "rank0.npz"), np.load(tmp_path / "rank1.npz")
-    assert np.array_equal(z0["out"], z1["out"]) and np.array_equal(z0["lse"], z1["lse"])
+    z = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
+    for r in range(1, world):
+        assert np.array_equal(z[0]["out"], z[r]["out"]) and np.array_equal(z[0]["lse"], z[r]["lse"])
     lens = np.array([65536, 1000], np.int32)
     bt, npages = paged_pool(lens, PAGE, 71)
     g = torch.Generator().manual_seed(70)
     torch.randn((2, 1, 128, D_QK), generator=g)
     kc = torch.randn((npages, PAGE, 1, D_QK), generator=g).to(torch.bfloat16).float().numpy()
-    want_o, want_l = oracle.mla_decode_dense(z0["q"], kc, bt, lens, D_V, SCALE)
-    assert_close("out", z0["out"], want_o)
-    assert_close("lse", z0["lse"], want_l)
+    want_o, want_l = oracle.mla_decode_dense(z[0]["q"], kc, bt, lens, D_V, SCALE)
+    assert_close("out", z[0]["out"], want_o)
+    assert_close("lse", z[0]["lse"], want_l)

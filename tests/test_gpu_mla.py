@@ -144,7 +144,7 @@ def test_sparse_padding_and_out_of_range(parts):
 def test_sparse_padded_pool_row_copy_route():
     """Top-k over a pool whose pages are not back to back (64-row pages
     allocated 65 rows apart, the spare rows NaN): no single row map covers it,
-    so the per-row copy kernel runs, against the same oracle."""
+    so rows come in one-row boxes of the page map, against the same oracle."""
     d = build_sparse(17, [300, 5000], topk=512, s_q=1, heads=128)
     kc = d["kc"]
     padded = torch.full((kc.shape[0], PAGE + 1, 1, D_QK), float("nan"), dtype=kc.dtype,
@@ -156,6 +156,39 @@ def test_sparse_padded_pool_row_copy_route():
     d["idx"] = to_dev(d["idx_np"])
     out, lse, _, _ = _decode(d, indices=d["idx"], topk=512)
     want_o, want_l = oracle.mla_decode_sparse(d["q_np"], d["kc_np"], d["idx_np"], D_V, SCALE)
+    assert_close("out", out, want_o)
+    assert_close("lse", lse, want_l)
+
+
+@pytest.mark.parametrize("padded_pool", [False, True])
+def test_sparse_unreferenced_rows_nan(padded_pool):
+    """Every pool row no index list refers to is NaN, pool row 0 included (a
+    NaN page is put in front of the pool and the indices moved past it);
+    lists longer than their sequence end in -1 padding, one query's list is
+    all -1 (out 0, lse -inf) and one holds a single valid row.  A masked
+    column must contribute exactly nothing, whatever its row holds."""
+    lens = [40, 3000, 500, 1]
+    d = build_sparse(18, lens, topk=256, s_q=2, heads=128)
+    idx = d["idx_np"].copy()
+    idx[idx >= 0] += PAGE
+    idx[2, 1, :] = -1                                 # no valid entry at all
+    idx[3, 0, 1:] = -1                                # one valid entry
+    kc_np = np.concatenate([np.full((1, PAGE, 1, D_QK), np.nan, np.float32), d["kc_np"]])
+    n_pages = kc_np.shape[0]
+    stride = PAGE + 1 if padded_pool else PAGE
+    pool = torch.full((n_pages, stride, 1, D_QK), float("nan"), dtype=torch.bfloat16,
+                      device="cuda")
+    pool[:, :PAGE] = to_dev(kc_np, torch.bfloat16)
+    used = torch.zeros(n_pages * PAGE, dtype=torch.bool, device="cuda")
+    used[to_dev(np.unique(idx[idx >= 0]).astype(np.int64))] = True
+    rows = pool[:, :PAGE]
+    rows[~used.view(n_pages, PAGE)] = float("nan")
+    assert not bool(used[0]) and torch.isnan(rows[0, 0]).all()
+    d["kc"] = rows
+    d["idx"] = to_dev(idx)
+    out, lse, _, _ = _decode(d, indices=d["idx"], topk=256)
+    want_o, want_l = oracle.mla_decode_sparse(d["q_np"], kc_np, idx, D_V, SCALE)
+    assert np.isneginf(want_l[2, :, 1]).all() and (want_o[2, 1] == 0).all()
     assert_close("out", out, want_o)
     assert_close("lse", lse, want_l)
 

@@ -2,7 +2,7 @@
 
 Covers ``flagattention_b200.shard``: the sequence partition used by batched
 decode, the KV-page split used by long-context decode, the all-gather of
-partial (O, LSE) between ranks, and a rank that fails before the exchange
+packed partials (O, LSE) between ranks, and a rank that fails before the exchange
 (its peer must get an error within the group timeout, not hang).  The
 per-rank decode here is the CPU oracle, so the merged result can be checked
 against the oracle's unsharded decode.
@@ -80,8 +80,16 @@ def _exchange_worker(rank, world, port, lens, outdir):
         q, kc, bt = mla_inputs(33, len(lens), 1, 8, lens)
         lbt, llen = shard.shard_pages(bt, lens, PAGE, world, rank)
         part_o, part_lse = _oracle_partial(q, kc, lbt, llen)
-        all_o, all_l = shard.exchange_partials(part_o, part_lse)
-        assert all_o.shape == (world,) + tuple(part_o.shape)
+        B, _, H, _ = part_o.shape
+        packed = shard.packed_partial(B, H)
+        o_view, l_view = shard.unpack_partial(packed, B, H)
+        o_view.copy_(part_o)
+        l_view.copy_(part_lse.transpose(1, 2))
+        gathered = shard.exchange_partials(packed)
+        assert gathered.shape == (world, packed.numel())
+        all_o = gathered[:, :B * H * D_V].reshape((world,) + tuple(part_o.shape))
+        all_l = gathered[:, B * H * D_V:].reshape((world,) + tuple(part_lse.shape))
+        assert torch.equal(all_o[rank], part_o) and torch.equal(all_l[rank], part_lse)
         out, lse = oracle.lse_combine(all_o.numpy(), all_l.numpy())
         np.savez(os.path.join(outdir, f"rank{rank}.npz"), out=out, lse=lse)
         torch.distributed.destroy_process_group()
@@ -126,10 +134,9 @@ def _failing_worker(rank, world, port, outdir):
     shard.new_group_with_timeout("gloo", 5, rank=rank, world_size=world)
     if rank == 1:
         raise RuntimeError("injected failure on rank 1 before the exchange")
-    part_o = torch.zeros((1, 1, 4, D_V))
-    part_l = torch.zeros((1, 1, 4))
+    packed = torch.zeros(shard.packed_partial(1, 4).numel())
     try:
-        shard.exchange_partials(part_o, part_l)
+        shard.exchange_partials(packed)
     except Exception as e:                               # the expected path
         with open(os.path.join(outdir, "rank0.caught"), "w") as f:
             f.write(type(e).__name__ + ": " + str(e)[:200])
