@@ -92,6 +92,7 @@ struct Bars {
   uint64_t s_full[2], s_empty[2];
   uint64_t pair[4];
   uint64_t stg_ready[2];     // the 128 rows of a P block are staged (one per block half)
+  uint64_t stg_free[2];      // P staging buffer j's last copy has landed in the value CTA
   uint64_t p_free[kPSlots];  // arrived by the value CTA's PV commit
   // value CTA
   uint64_t v_full[kVStages], v_empty[kVStages];
@@ -434,7 +435,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&bars->ch_empty[i]), 1);
     }
     for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&bars->pair[i]), 64);
-    for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bars->stg_ready[i]), 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&bars->stg_ready[i]), 128);
+      mbar_init(smem_u32(&bars->stg_free[i]), 1);
+    }
     for (int i = 0; i < kPSlots; ++i) {
       mbar_init(smem_u32(&bars->p_free[i]), 1);
       mbar_init(smem_u32(&bars->p_full[i]), 1);
@@ -854,15 +858,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // pb & 1) and sent with one bulk copy: 1024 separate 16-byte
             // remote stores per block crowd the memory-instruction queues
             // that the producer's and MMA warp's instructions also use.
-            // The staging buffer was last sent for block pb - 2, whose PV has
-            // finished once p_free of its slot has (its copy had landed).
+            // The staging buffer (pb & 1) was last sent for block pb - 2: it
+            // may be rewritten once that copy has landed in the value CTA,
+            // which the value CTA's MMA warp relays (stg_free) as soon as it
+            // sees the block's P arrive -- not once the block's PV is done,
+            // which would tie every softmax step to the value CTA's tensor
+            // pipe two blocks back.
             ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->p_free[pslot]),
                                                    ((pb / kPSlots) & 1) ^ 1, abort_flag, p.status,
                                                    kDevTimeoutSoftmax));
             if (ok && pb >= 2)
-              ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->p_free[(pb - 2) % kPSlots]),
-                                                     ((pb - 2) / kPSlots) & 1, abort_flag,
-                                                     p.status, kDevTimeoutSoftmax));
+              ok = __all_sync(0xffffffffu,
+                              mbar_wait<true>(smem_u32(&bars->stg_free[pb & 1]),
+                                              ((pb - 2) >> 1) & 1, abort_flag, p.status,
+                                              kDevTimeoutSoftmax));
             if (!ok) break;
             const uint32_t stg = s_base + kOffStgP + (pb & 1) * kPBytes;
 #pragma unroll
@@ -1022,6 +1031,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (mbar_probe(bar, parity)) return true;
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma)) != 0;
       };
+      const uint32_t stg_free_remote = map_to_rank(smem_u32(&bars->stg_free[0]), 0);
       uint32_t vs = 0, gb = 0;
       int pi = 0;
       bool ok = true;
@@ -1040,6 +1050,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_arrive_expect_tx(smem_u32(&bars->p_full[ps]),
                                   kPBytes + (tile_first ? 512 + 16 : 0) + (piece_last ? 512 : 0));
           ok = wait(smem_u32(&bars->p_full[ps]), ph);
+          // the block's P has landed: the score CTA may restage its buffer
+          if (ok && lane == 0) mbar_arrive_remote(stg_free_remote + (gb & 1) * 8);
           ok = ok && wait(smem_u32(&bars->m_read[ps]), ph);
           if (ok && first_blk) ok = wait(smem_u32(&bars->o_empty), (pi & 1) ^ 1);
           if (!ok) break;
