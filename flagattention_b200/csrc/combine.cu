@@ -1,98 +1,11 @@
-// combine.cu -- log-sum-exp merge of split partial results.
-//
-// Same algebra as the reference's _fwd_combine_kv_splits (split_kv.py:198-228):
-//   lse = m + log(sum_s exp(lse_s - m)),  o = sum_s exp(lse_s - lse) * o_s
-// with f32 partials.  One warp per output row (d_v <= 512); lanes stride over
-// the value dims with 16-byte loads.
+// combine.cu -- log-sum-exp merge of split partial results (merge.cuh: the
+// reference's _fwd_combine_kv_splits algebra, split_kv.py:198-228), one warp
+// per output row.
 #include "common.cuh"
 #include "flagattn_b200.h"
+#include "merge.cuh"
 
 namespace fa {
-
-template <typename T>
-__device__ __forceinline__ void store4(T *dst, float4 v) {
-  if constexpr (sizeof(T) == 4) {
-    *reinterpret_cast<float4 *>(dst) = v;
-  } else {
-    uint2 w;
-    w.x = Elem<T>::pack2(v.x, v.y);
-    w.y = Elem<T>::pack2(v.z, v.w);
-    *reinterpret_cast<uint2 *>(dst) = w;
-  }
-}
-
-// Merge `n` partial rows located at part_o[slot(s) * slot_stride + row_off]
-// (and part_lse[slot(s) * lse_stride + row]).  Returns the merged lse.
-// Partials go in groups of two: a group's LSEs and value rows are all loaded
-// before any is used, and the groups are folded with a running maximum, so a
-// warp waits for one memory round trip per group instead of one for the LSEs
-// and then one per partial.  Two, not more: the merge is latency-bound on
-// partials that come from DRAM, and a 64-register budget (eight 4-warp blocks
-// per SM) hides more latency than more loads in flight per warp.
-template <typename T>
-__device__ __forceinline__ float merge_row(const float *__restrict__ part_o,
-                                           const float *__restrict__ part_lse, int first_slot,
-                                           int n, int64_t o_slot_stride, int64_t lse_slot_stride,
-                                           int64_t o_row_off, int64_t lse_row, int d_v, T *out,
-                                           int lane) {
-  constexpr int kGroup = 2;
-  float m = -INFINITY, z = 0.f;  // running maximum and sum of exp(lse_s - m)
-  // Each lane owns up to 4 float4 columns (d = 4 lane + 128 k).
-  float4 acc[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s0 = 0; s0 < n; s0 += kGroup) {
-    float ls[kGroup];
-    float4 v[kGroup][4];
-#pragma unroll
-    for (int g = 0; g < kGroup; ++g) {
-      const bool live = s0 + g < n;
-      ls[g] = live ? __ldg(part_lse + (first_slot + s0 + g) * lse_slot_stride + lse_row) : -INFINITY;
-      const float *src = part_o + (first_slot + s0 + g) * o_slot_stride + o_row_off;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int d = lane * 4 + k * 128;
-        v[g][k] = (live && d < d_v) ? __ldg(reinterpret_cast<const float4 *>(src + d))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
-    float mg = m;
-#pragma unroll
-    for (int g = 0; g < kGroup; ++g) mg = fmaxf(mg, ls[g]);
-    if (mg == -INFINITY) continue;  // nothing but empty partials so far
-    const float keep = (m == -INFINITY) ? 0.f : __expf(m - mg);
-    z *= keep;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      acc[k].x *= keep;
-      acc[k].y *= keep;
-      acc[k].z *= keep;
-      acc[k].w *= keep;
-    }
-#pragma unroll
-    for (int g = 0; g < kGroup; ++g) {
-      const float w = (ls[g] == -INFINITY) ? 0.f : __expf(ls[g] - mg);
-      z += w;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        acc[k].x += w * v[g][k].x;
-        acc[k].y += w * v[g][k].y;
-        acc[k].z += w * v[g][k].z;
-        acc[k].w += w * v[g][k].w;
-      }
-    }
-    m = mg;
-  }
-  const float lse = (z > 0.f) ? m + __logf(z) : -INFINITY;
-  const float inv = (z > 0.f) ? 1.f / z : 0.f;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int d = lane * 4 + k * 128;
-    const float4 o = make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
-    if (d < d_v) store4<T>(out + d, o);
-  }
-  return lse;
-}
 
 // Generic: rows decomposed as (b, h, m) with h < H, m < M; every row has
 // num_parts partials laid out [part][rows][d_v]; lse out f32 [rows].
@@ -115,25 +28,44 @@ __global__ void __launch_bounds__(128, 8) lse_combine_kernel(const float *__rest
 }
 
 // MLA: sequence b owns slots num_splits[b] .. num_splits[b+1]-1 of
-// part_o [slot][s_q*h_q][d_v]; single-piece sequences were written directly.
+// part_o [slot][s_q*h_q][d_v].  Sequences with fewer than min_parts pieces
+// are skipped: single pieces were written straight to the output, and when
+// the decode merges short splits itself (split counters given) those too.
+// Two rows per 256-thread block, four warps per row: warp j folds partials
+// j, j + 4, ... (a long split, e.g. one 1M-token sequence over 37 parts,
+// keeps four times the loads in flight), then the row's four states are
+// folded in warp order through shared memory.
+// Launched as a programmatic dependent of the decode kernel: blocks with
+// nothing to merge exit while the decode still runs; the others wait for the
+// decode grid to complete (griddepcontrol.wait) before reading partials.
 template <typename T>
-__global__ void __launch_bounds__(128, 8) mla_combine_kernel(const float *__restrict__ part_o,
+__global__ void __launch_bounds__(256) mla_combine_kernel(const float *__restrict__ part_o,
                                    const float *__restrict__ part_lse,
                                    const int32_t *__restrict__ num_splits, int s_q, int h_q,
-                                   int d_v, T *__restrict__ out, int64_t o_sb, int64_t o_ss,
-                                   int64_t o_sh, float *__restrict__ lse) {
-  const int lane = threadIdx.x & 31;
+                                   int d_v, int min_parts, T *__restrict__ out, int64_t o_sb,
+                                   int64_t o_ss, int64_t o_sh, float *__restrict__ lse) {
+  __shared__ MergeState states[8][32];
   const int b = blockIdx.y;
-  const int rows = s_q * h_q;
-  const int flat = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  if (flat >= rows) return;
-  const int first = num_splits[b];
+  const int first = num_splits[b];  // written by the metadata kernel, before the decode
   const int n = num_splits[b + 1] - first;
-  if (n <= 1) return;
+  if (n < min_parts || n < 2) return;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows = s_q * h_q;
+  const int flat = blockIdx.x * 2 + (warp >> 2);
+  const int j = warp & 3;
+  MergeState st;
+  st.init();
+  if (flat < rows)
+    fold_parts<false>(st, part_o, part_lse, first, j, 4, n, static_cast<int64_t>(rows) * d_v, rows,
+                      static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
+  states[warp][lane] = st;
+  __syncthreads();
+  if (j != 0 || flat >= rows) return;
+#pragma unroll
+  for (int k = 1; k < 4; ++k) fold_state(st, states[warp + k][lane]);
   const int s = flat / h_q, h = flat % h_q;
-  T *o = out + b * o_sb + s * o_ss + h * o_sh;
-  const float l = merge_row<T>(part_o, part_lse, first, n, static_cast<int64_t>(rows) * d_v, rows,
-                               static_cast<int64_t>(flat) * d_v, flat, d_v, o, lane);
+  const float l = finish_row<T>(st, d_v, out + b * o_sb + s * o_ss + h * o_sh, lane);
   if (lane == 0) lse[(static_cast<int64_t>(b) * h_q + h) * s_q + s] = l;
 }
 
@@ -168,23 +100,36 @@ void launch_lse_combine(const float *part_o, const float *part_lse, int num_part
                                 H, M, d_v, out, o_sb, o_sh, o_sm, lse, stream);
 }
 
-void launch_mla_combine(const float *part_o, const float *part_lse, const int32_t *num_splits,
-                        int batch, int s_q, int h_q, int d_v, void *out, int dtype, int64_t o_sb,
-                        int64_t o_ss, int64_t o_sh, float *lse, cudaStream_t stream) {
-  const int warps = 4;
-  dim3 grid((s_q * h_q + warps - 1) / warps, batch);
+template <typename T>
+cudaError_t launch_mla_combine_t(const float *part_o, const float *part_lse,
+                                 const int32_t *num_splits, int batch, int s_q, int h_q, int d_v,
+                                 int min_parts, void *out, int64_t o_sb, int64_t o_ss,
+                                 int64_t o_sh, float *lse, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((s_q * h_q + 1) / 2, batch);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, mla_combine_kernel<T>, part_o, part_lse, num_splits, s_q, h_q,
+                            d_v, min_parts, static_cast<T *>(out), o_sb, o_ss, o_sh, lse);
+}
+
+cudaError_t launch_mla_combine(const float *part_o, const float *part_lse,
+                               const int32_t *num_splits, int batch, int s_q, int h_q, int d_v,
+                               int min_parts, void *out, int dtype, int64_t o_sb, int64_t o_ss,
+                               int64_t o_sh, float *lse, cudaStream_t stream) {
   if (dtype == FA_DTYPE_BF16)
-    mla_combine_kernel<__nv_bfloat16><<<grid, warps * 32, 0, stream>>>(
-        part_o, part_lse, num_splits, s_q, h_q, d_v, static_cast<__nv_bfloat16 *>(out), o_sb,
-        o_ss, o_sh, lse);
-  else if (dtype == FA_DTYPE_F32)
-    mla_combine_kernel<float><<<grid, warps * 32, 0, stream>>>(
-        part_o, part_lse, num_splits, s_q, h_q, d_v, static_cast<float *>(out), o_sb, o_ss, o_sh,
-        lse);
-  else
-    mla_combine_kernel<__half><<<grid, warps * 32, 0, stream>>>(
-        part_o, part_lse, num_splits, s_q, h_q, d_v, static_cast<__half *>(out), o_sb, o_ss, o_sh,
-        lse);
+    return launch_mla_combine_t<__nv_bfloat16>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v,
+                                               min_parts, out, o_sb, o_ss, o_sh, lse, stream);
+  if (dtype == FA_DTYPE_F32)
+    return launch_mla_combine_t<float>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v,
+                                       min_parts, out, o_sb, o_ss, o_sh, lse, stream);
+  return launch_mla_combine_t<__half>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v,
+                                      min_parts, out, o_sb, o_ss, o_sh, lse, stream);
 }
 
 }  // namespace fa

@@ -35,6 +35,7 @@
 // status word and the kernel unwinds instead of hanging.
 #include "common.cuh"
 #include "flagattn_b200.h"
+#include "merge.cuh"
 
 namespace fa {
 namespace sv {
@@ -57,10 +58,12 @@ constexpr int kPBytes = kRows * kRowBytes;          // 16 KB: P of one 64-token 
 constexpr int kMetaAlpha = kPBytes;                 // f32[128] O rescale factors
 constexpr int kMetaFlags = kPBytes + 512;           // int[4] "rows of quadrant q rescale"
 constexpr int kMetaInvL = kPBytes + 1024;           // f32[128] 1 / row sum (last block)
+constexpr int kMetaLse = kPBytes + 1536;            // f32[128] LSE of the piece (last block)
 constexpr int kPSlotBytes = kPBytes + 2048;         // 18 KB
 constexpr int kPSlots = 4;
 constexpr uint32_t kColQ = 0, kColS = 256, kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;           // log2 units (factor 256)
+
 constexpr int kOffBar = 0;
 constexpr int kOffData = 1024;
 // score CTA
@@ -103,6 +106,7 @@ struct Bars {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
+  int merge_flag;  // value CTA: this CTA finished the last piece of a split sequence
   // sparse: per tile (g % 4), one byte per 4-row group with the invalid-index
   // bits of its key rows (row 4 group + j: bit j)
   alignas(16) uint8_t inval[4][32];
@@ -135,6 +139,9 @@ struct Params {
   int32_t topk;  // 0: dense
   int64_t total_rows;
   int32_t uniform_rows;  // sparse: pool rows at one stride (2-D gather map)
+  // [batch][m_blocks] pieces of each split sequence finished so far (zero
+  // between calls); null: split sequences are left to the combine kernel
+  int32_t *split_counters;
 };
 
 struct Piece {
@@ -147,12 +154,24 @@ __device__ __forceinline__ int seq_len(const Params &p, int b) {
   return p.topk ? p.topk : (p.seq_lens ? p.seq_lens[b] : p.n_ctx);
 }
 
-// Piece i of a part (tile_meta row: begin batch, begin block, end batch, end
-// block, split index of the first piece, number of pieces).  Out of line:
-// every role walks the pieces, once per piece.
+// Order in which a part runs its pieces: the first, then the last, then the
+// ones in between.  Only the first and the last piece of a part can belong to
+// a sequence split with a neighbouring part (the tail of one the previous part
+// began, the head of one the next part finishes), so with both run early the
+// last piece of every split sequence finishes early too, and it merges the
+// sequence's partials while they are still in L2; a part then ends on a
+// whole sequence, written straight to the output.
+__device__ __forceinline__ int piece_order(int i, int n) {
+  return (i == 0 || n <= 2) ? i : (i == 1 ? n - 1 : i - 1);
+}
+
+// Piece i (in run order) of a part (tile_meta row: begin batch, begin block,
+// end batch, end block, split index of the first piece, number of pieces).
+// Out of line: every role walks the pieces, once per piece.
 __device__ __noinline__ Piece get_piece_at(const int32_t *seq_lens, int n_ctx,
                                            const int32_t *meta, int i) {
   Piece pc;
+  i = piece_order(i, meta[5]);
   pc.b = meta[0] + i;
   const int len = seq_lens ? seq_lens[pc.b] : n_ctx;
   const int nblk = len > 0 ? (len + kBlk - 1) / kBlk : 0;
@@ -393,6 +412,49 @@ __device__ __noinline__ void write_o_half(uint32_t trow, int ch, int q4, int lan
   }
 }
 
+// Value CTA, after writing a split piece's partial rows and LSEs (all 256
+// epilogue threads, index tt): count the piece, and if it was the sequence's
+// last, merge the sequence's partials of this query block into the output.
+// Writers fence before the count and the merger fences after it, so the
+// other CTAs' partials are visible to its L2 (ld.global.cg) loads.  The merge
+// folds the partials in slot order: the result is the same whichever piece
+// finishes last.
+template <typename T>
+__device__ __noinline__ void merge_if_last(const Params &p, int b, int mb, int first_slot,
+                                           int n_split, int row0, int n_rows, int tt,
+                                           volatile int *flag) {
+  __threadfence();
+  named_bar_sync(1, 256);
+  if (tt == 0) {
+    int *cnt = p.split_counters + static_cast<int64_t>(b) * gridDim.y + mb;
+    const bool last = atomicAdd(cnt, 1) + 1 == n_split;
+    if (last) *cnt = 0;  // zero again for the next call
+    __threadfence();
+    *flag = last ? 1 : 0;
+  }
+  named_bar_sync(1, 256);
+  if (!*flag) return;
+  const int rows_total = p.s_q * p.h_q;
+  const int lane = tt & 31;
+  for (int r = tt >> 5; r < n_rows; r += 8) {
+    const int flat = row0 + r;
+    const int s_tok = flat / p.h_q, h = flat % p.h_q;
+    const int64_t o_off = static_cast<int64_t>(b) * p.o_sb + s_tok * p.o_ss + h * p.o_sh;
+    float l;
+    if (p.out_f32)
+      l = merge_row<float, true>(p.part_o, p.part_lse, first_slot, n_split,
+                                 static_cast<int64_t>(rows_total) * p.d_v, rows_total,
+                                 static_cast<int64_t>(flat) * p.d_v, flat, p.d_v,
+                                 static_cast<float *>(p.out) + o_off, lane);
+    else
+      l = merge_row<T, true>(p.part_o, p.part_lse, first_slot, n_split,
+                             static_cast<int64_t>(rows_total) * p.d_v, rows_total,
+                             static_cast<int64_t>(flat) * p.d_v, flat, p.d_v,
+                             static_cast<T *>(p.out) + o_off, lane);
+    if (lane == 0) p.lse[(static_cast<int64_t>(b) * p.h_q + h) * p.s_q + s_tok] = l;
+  }
+}
+
 template <typename T, bool kSparse>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mla_decode_sv_kernel(const __grid_constant__ CUtensorMap q_map,
@@ -463,6 +525,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   cluster_sync();  // the peer's barriers exist before any remote access
+  // every CTA of the grid is resident: the combine kernel queued behind this
+  // one may start (its blocks with nothing to merge finish meanwhile)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (rank == 0) {
     // ================================================================ score CTA
@@ -747,8 +812,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int flat = row0 + t;
       const bool row_ok = t < n_rows;
       const int s_tok = row_ok ? flat / p.h_q : 0;
-      const int h = row_ok ? flat % p.h_q : 0;
-      const int out_flat = s_tok * p.h_q + h;
       const uint32_t p_remote = map_to_rank(s_base + kOffP, 1);
       const uint32_t pfull_remote = map_to_rank(smem_u32(&bars->p_full[0]), 1);
       bool ok = true;
@@ -756,9 +819,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t stg_uses[2] = {0, 0};
       for (int i = 0; i < n_pieces && ok; ++i) {
         const Piece pc = get_piece(p, meta, i);
-        const int first_slot = p.num_splits[pc.b];
-        const int n_split = p.num_splits[pc.b + 1] - first_slot;
-        const int slot_o = first_slot + pc.split_idx;
         const int len = seq_len(p, pc.b);
         const int row_len = p.causal ? len - (p.s_q - 1 - s_tok) : len;
         float m_run = -INFINITY, l_half = 0.f, l_run = 0.f;
@@ -904,21 +964,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             rslot[ch * kRows + t] = l_half;
             if (!(ok = pair_sync())) break;
             l_run = l_half + rslot[(ch ^ 1) * kRows + t];
-            if (ch == n_blk - 1)
+            if (ch == n_blk - 1) {
+              // 1 / row sum and the piece's LSE (natural log of the scaled
+              // row sum) travel with the piece's last block: the value CTA
+              // writes the piece's output and LSE together
+              const float ms = (m_run == -INFINITY) ? 0.f : m_run;
+              const float lse = l_run > 0.f ? ms * 0.69314718055994531f + logf(l_run) : -INFINITY;
               st_async_u32(pdst + kMetaInvL + 4 * t, __float_as_uint(l_run > 0.f ? 1.f / l_run : 0.f),
                            pbar);
+              st_async_u32(pdst + kMetaLse + 4 * t, __float_as_uint(lse), pbar);
+            }
           }
           gb += n_blk;
-        }
-        if (!ok) break;
-        // LSE of the piece (natural log of the scaled row sum)
-        const float ms = (m_run == -INFINITY) ? 0.f : m_run;
-        const float lse = l_run > 0.f ? ms * 0.69314718055994531f + logf(l_run) : -INFINITY;
-        if (ch == 0 && row_ok) {
-          if (n_split == 1)
-            p.lse[(static_cast<int64_t>(pc.b) * p.h_q + h) * p.s_q + s_tok] = lse;
-          else
-            p.part_lse[static_cast<int64_t>(slot_o) * rows_total + out_flat] = lse;
         }
       }
     }
@@ -1048,7 +1105,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t ph = (gb / kPSlots) & 1;
           if (lane == 0)
             mbar_arrive_expect_tx(smem_u32(&bars->p_full[ps]),
-                                  kPBytes + (tile_first ? 512 + 16 : 0) + (piece_last ? 512 : 0));
+                                  kPBytes + (tile_first ? 512 + 16 : 0) + (piece_last ? 1024 : 0));
           ok = wait(smem_u32(&bars->p_full[ps]), ph);
           // the block's P has landed: the score CTA may restage its buffer
           if (ok && lane == 0) mbar_arrive_remote(stg_free_remote + (gb & 1) * 8);
@@ -1102,7 +1159,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int n_split = p.num_splits[pc.b + 1] - first_slot;
         const int slot_o = first_slot + pc.split_idx;
         const bool has_tiles = pc.tok_end > pc.tok0;
-        float inv_l = 0.f;
+        float inv_l = 0.f, lse_row = -INFINITY;
         for (int bt = pc.tok0; bt < pc.tok_end && ok; bt += kBlk, ++gb) {
           const int vb = min(kBlk, pc.tok_end - bt);
           const int n_sub = vb > kVRows ? 2 : 1;
@@ -1128,7 +1185,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               }
             }
           }
-          if (bt + kBlk >= pc.tok_end) inv_l = reinterpret_cast<const float *>(slotp + kMetaInvL)[t];
+          if (bt + kBlk >= pc.tok_end) {
+            inv_l = reinterpret_cast<const float *>(slotp + kMetaInvL)[t];
+            lse_row = reinterpret_cast<const float *>(slotp + kMetaLse)[t];
+          }
           if (vb < kBlk) {
             // rows past the sequence end may hold any bits (even NaN); P is 0
             // there but 0 * NaN is not, so clear them before the PV product.
@@ -1179,6 +1239,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tc_fence_before();
           mbar_arrive(smem_u32(&bars->o_empty));
         }
+        if (ch == 0 && t < n_rows) {
+          const int flat = row0 + t;
+          if (final_out)
+            p.lse[(static_cast<int64_t>(pc.b) * p.h_q + flat % p.h_q) * p.s_q + flat / p.h_q] = lse_row;
+          else
+            p.part_lse[static_cast<int64_t>(slot_o) * rows_total + flat] = lse_row;
+        }
+        if (!final_out && p.split_counters != nullptr && n_split <= kMlaMergeInKernelMax)
+          merge_if_last<T>(p, pc.b, mb, first_slot, n_split, row0, n_rows, tt, &bars->merge_flag);
       }
     }
   }
@@ -1252,6 +1321,7 @@ cudaError_t launch_mla_sv(const CUtensorMap &qm, const CUtensorMap &km, const CU
   p.topk = sparse ? a->topk : 0;
   p.total_rows = static_cast<int64_t>(a->num_pages) * a->page_size;
   p.uniform_rows = a->kv_stride_page == static_cast<int64_t>(a->page_size) * a->kv_stride_tok;
+  p.split_counters = a->split_counters;
   const dim3 grid(2 * a->num_sm_parts, m_blocks);
   if (a->dtype == FA_DTYPE_F16)
     return sparse ? launch_sv_t<__half, true>(qm, km, vm, gm, p, grid, stream)
