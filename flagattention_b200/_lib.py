@@ -64,7 +64,7 @@ class MlaArgs(ctypes.Structure):
         ("lse", _vp), ("part_o", _vp), ("part_lse", _vp),
         ("batch", _i32), ("s_q", _i32), ("h_q", _i32), ("d_qk", _i32), ("d_v", _i32),
         ("causal", _i32), ("dtype", _i32), ("out_dtype", _i32), ("scale", _f32),
-        ("status", _vp), ("split_counters", _vp),
+        ("status", _vp),
     ]
 
 

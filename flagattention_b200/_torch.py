@@ -54,13 +54,9 @@ def status_word(device):
 
 
 def read_status(device):
-    """Synchronise and return (then clear) the device status word (0 = ok).
-    A nonzero status means a kernel stopped part-way: the cached split
-    counters are zeroed so the next decode starts from a clean state."""
+    """Synchronise and return (then clear) the device status word (0 = ok)."""
     t = status_word(device)
     v = int(t.item())
     if v:
         t.zero_()
-        from flagattention_b200 import mla
-        mla.reset_workspaces()
     return v

@@ -28,42 +28,32 @@ __global__ void __launch_bounds__(128, 8) lse_combine_kernel(const float *__rest
 }
 
 // MLA: sequence b owns slots num_splits[b] .. num_splits[b+1]-1 of
-// part_o [slot][s_q*h_q][d_v].  Sequences with fewer than min_parts pieces
-// are skipped: single pieces were written straight to the output, and when
-// the decode merges short splits itself (split counters given) those too.
-// Two rows per 256-thread block, four warps per row: warp j folds partials
-// j, j + 4, ... (a long split, e.g. one 1M-token sequence over 37 parts,
-// keeps four times the loads in flight), then the row's four states are
-// folded in warp order through shared memory.
-// Launched as a programmatic dependent of the decode kernel: blocks with
-// nothing to merge exit while the decode still runs; the others wait for the
-// decode grid to complete (griddepcontrol.wait) before reading partials.
+// part_o [slot][s_q*h_q][d_v]; a sequence of one piece was written straight to
+// the output.  One warp per row, partials loaded four at a time (a long split
+// -- one 1M-token sequence spread over 37 parts -- waits for 10 memory round
+// trips instead of 19).  Launched as a programmatic dependent of the decode
+// kernel: its launch overlaps the decode, blocks of unsplit sequences exit
+// while the decode still runs, and the others wait for the decode grid to
+// complete (griddepcontrol.wait) before reading partials.
 template <typename T>
-__global__ void __launch_bounds__(256) mla_combine_kernel(const float *__restrict__ part_o,
+__global__ void __launch_bounds__(128, 4) mla_combine_kernel(const float *__restrict__ part_o,
                                    const float *__restrict__ part_lse,
                                    const int32_t *__restrict__ num_splits, int s_q, int h_q,
-                                   int d_v, int min_parts, T *__restrict__ out, int64_t o_sb,
-                                   int64_t o_ss, int64_t o_sh, float *__restrict__ lse) {
-  __shared__ MergeState states[8][32];
+                                   int d_v, T *__restrict__ out, int64_t o_sb, int64_t o_ss,
+                                   int64_t o_sh, float *__restrict__ lse) {
   const int b = blockIdx.y;
   const int first = num_splits[b];  // written by the metadata kernel, before the decode
   const int n = num_splits[b + 1] - first;
-  if (n < min_parts || n < 2) return;
+  if (n < 2) return;
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31;
   const int rows = s_q * h_q;
-  const int flat = blockIdx.x * 2 + (warp >> 2);
-  const int j = warp & 3;
+  const int flat = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (flat >= rows) return;
   MergeState st;
   st.init();
-  if (flat < rows)
-    fold_parts<false>(st, part_o, part_lse, first, j, 4, n, static_cast<int64_t>(rows) * d_v, rows,
-                      static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
-  states[warp][lane] = st;
-  __syncthreads();
-  if (j != 0 || flat >= rows) return;
-#pragma unroll
-  for (int k = 1; k < 4; ++k) fold_state(st, states[warp + k][lane]);
+  fold_parts<false, 4>(st, part_o, part_lse, first, 0, 1, n, static_cast<int64_t>(rows) * d_v,
+                       rows, static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
   const int s = flat / h_q, h = flat % h_q;
   const float l = finish_row<T>(st, d_v, out + b * o_sb + s * o_ss + h * o_sh, lane);
   if (lane == 0) lse[(static_cast<int64_t>(b) * h_q + h) * s_q + s] = l;
@@ -103,11 +93,11 @@ void launch_lse_combine(const float *part_o, const float *part_lse, int num_part
 template <typename T>
 cudaError_t launch_mla_combine_t(const float *part_o, const float *part_lse,
                                  const int32_t *num_splits, int batch, int s_q, int h_q, int d_v,
-                                 int min_parts, void *out, int64_t o_sb, int64_t o_ss,
-                                 int64_t o_sh, float *lse, cudaStream_t stream) {
+                                 void *out, int64_t o_sb, int64_t o_ss, int64_t o_sh, float *lse,
+                                 cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((s_q * h_q + 1) / 2, batch);
-  cfg.blockDim = dim3(256);
+  cfg.gridDim = dim3((s_q * h_q + 3) / 4, batch);
+  cfg.blockDim = dim3(128);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -115,21 +105,21 @@ cudaError_t launch_mla_combine_t(const float *part_o, const float *part_lse,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, mla_combine_kernel<T>, part_o, part_lse, num_splits, s_q, h_q,
-                            d_v, min_parts, static_cast<T *>(out), o_sb, o_ss, o_sh, lse);
+                            d_v, static_cast<T *>(out), o_sb, o_ss, o_sh, lse);
 }
 
 cudaError_t launch_mla_combine(const float *part_o, const float *part_lse,
                                const int32_t *num_splits, int batch, int s_q, int h_q, int d_v,
-                               int min_parts, void *out, int dtype, int64_t o_sb, int64_t o_ss,
-                               int64_t o_sh, float *lse, cudaStream_t stream) {
+                               void *out, int dtype, int64_t o_sb, int64_t o_ss, int64_t o_sh,
+                               float *lse, cudaStream_t stream) {
   if (dtype == FA_DTYPE_BF16)
     return launch_mla_combine_t<__nv_bfloat16>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v,
-                                               min_parts, out, o_sb, o_ss, o_sh, lse, stream);
+                                               out, o_sb, o_ss, o_sh, lse, stream);
   if (dtype == FA_DTYPE_F32)
-    return launch_mla_combine_t<float>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v,
-                                       min_parts, out, o_sb, o_ss, o_sh, lse, stream);
-  return launch_mla_combine_t<__half>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v,
-                                      min_parts, out, o_sb, o_ss, o_sh, lse, stream);
+    return launch_mla_combine_t<float>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v, out,
+                                       o_sb, o_ss, o_sh, lse, stream);
+  return launch_mla_combine_t<__half>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v, out,
+                                      o_sb, o_ss, o_sh, lse, stream);
 }
 
 }  // namespace fa

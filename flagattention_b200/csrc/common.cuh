@@ -32,12 +32,6 @@ enum DeviceStatus : int {
 // a few cycles where the global timer costs hundreds, on every slow wait.
 constexpr long long kWaitLimitCycles = 4000000000ll;
 
-// MLA decode: a sequence split into at most this many pieces is merged inside
-// the decode kernel by the CTA pair that finishes its last piece (it reads
-// every partial of its 128 query rows, n x 256 KB); longer splits are left to
-// the combine kernel, which spreads them over many SMs.
-constexpr int kMlaMergeInKernelMax = 4;
-
 template <typename T> struct Elem;
 template <> struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }

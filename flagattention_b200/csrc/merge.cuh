@@ -52,17 +52,16 @@ struct MergeState {
 
 // Fold partials s = s0, s0 + step, ... < n of one row into st, partial s at
 // part_o[(first_slot + s) * o_slot_stride + o_row_off] and part_lse[(first_slot
-// + s) * lse_slot_stride + lse_row].  Partials go in groups of two: a group's
-// LSEs and value rows are all loaded before any is used, and the groups are
-// folded with a running maximum, so a warp waits for one memory round trip
-// per group instead of one for the LSEs and then one per partial.
-template <bool kCoherent>
+// + s) * lse_slot_stride + lse_row].  Partials go in groups of kGroup: a
+// group's LSEs and value rows are all loaded before any is used, and the
+// groups are folded with a running maximum, so a warp waits for one memory
+// round trip per group instead of one for the LSEs and then one per partial.
+template <bool kCoherent, int kGroup = 2>
 __device__ __forceinline__ void fold_parts(MergeState &st, const float *__restrict__ part_o,
                                            const float *__restrict__ part_lse, int first_slot,
                                            int s0, int step, int n, int64_t o_slot_stride,
                                            int64_t lse_slot_stride, int64_t o_row_off,
                                            int64_t lse_row, int d_v, int lane) {
-  constexpr int kGroup = 2;
   for (int s = s0; s < n; s += kGroup * step) {
     float ls[kGroup];
     float4 v[kGroup][4];
@@ -106,23 +105,6 @@ __device__ __forceinline__ void fold_parts(MergeState &st, const float *__restri
     }
     st.m = mg;
   }
-}
-
-// a <- a folded with b (both states of the same row).
-__device__ __forceinline__ void fold_state(MergeState &a, const MergeState &b) {
-  const float m = fmaxf(a.m, b.m);
-  if (m == -INFINITY) return;
-  const float ka = (a.m == -INFINITY) ? 0.f : __expf(a.m - m);
-  const float kb = (b.m == -INFINITY) ? 0.f : __expf(b.m - m);
-  a.z = a.z * ka + b.z * kb;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    a.acc[k].x = a.acc[k].x * ka + b.acc[k].x * kb;
-    a.acc[k].y = a.acc[k].y * ka + b.acc[k].y * kb;
-    a.acc[k].z = a.acc[k].z * ka + b.acc[k].z * kb;
-    a.acc[k].w = a.acc[k].w * ka + b.acc[k].w * kb;
-  }
-  a.m = m;
 }
 
 // Normalised output row and merged LSE of a state.

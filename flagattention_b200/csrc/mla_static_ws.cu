@@ -130,7 +130,6 @@ extern "C" int fa_mla_decode_static_workspace(const fa_mla_args *args, void *str
     }
   }
   fa_mla_args a = *args;
-  a.split_counters = nullptr;  // every split goes through the combine kernel
   a.part_o = static_cast<float *>(base);
   a.part_lse = reinterpret_cast<float *>(static_cast<unsigned char *>(base) + round_up_256(po));
   return fa_mla_decode(&a, stream);

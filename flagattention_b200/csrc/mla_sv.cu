@@ -35,7 +35,6 @@
 // status word and the kernel unwinds instead of hanging.
 #include "common.cuh"
 #include "flagattn_b200.h"
-#include "merge.cuh"
 
 namespace fa {
 namespace sv {
@@ -95,7 +94,6 @@ struct Bars {
   uint64_t s_full[2], s_empty[2];
   uint64_t pair[4];
   uint64_t stg_ready[2];     // the 128 rows of a P block are staged (one per block half)
-  uint64_t stg_free[2];      // P staging buffer j's last copy has landed in the value CTA
   uint64_t p_free[kPSlots];  // arrived by the value CTA's PV commit
   // value CTA
   uint64_t v_full[kVStages], v_empty[kVStages];
@@ -106,7 +104,6 @@ struct Bars {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
-  int merge_flag;  // value CTA: this CTA finished the last piece of a split sequence
   // sparse: per tile (g % 4), one byte per 4-row group with the invalid-index
   // bits of its key rows (row 4 group + j: bit j)
   alignas(16) uint8_t inval[4][32];
@@ -139,9 +136,6 @@ struct Params {
   int32_t topk;  // 0: dense
   int64_t total_rows;
   int32_t uniform_rows;  // sparse: pool rows at one stride (2-D gather map)
-  // [batch][m_blocks] pieces of each split sequence finished so far (zero
-  // between calls); null: split sequences are left to the combine kernel
-  int32_t *split_counters;
 };
 
 struct Piece {
@@ -154,24 +148,12 @@ __device__ __forceinline__ int seq_len(const Params &p, int b) {
   return p.topk ? p.topk : (p.seq_lens ? p.seq_lens[b] : p.n_ctx);
 }
 
-// Order in which a part runs its pieces: the first, then the last, then the
-// ones in between.  Only the first and the last piece of a part can belong to
-// a sequence split with a neighbouring part (the tail of one the previous part
-// began, the head of one the next part finishes), so with both run early the
-// last piece of every split sequence finishes early too, and it merges the
-// sequence's partials while they are still in L2; a part then ends on a
-// whole sequence, written straight to the output.
-__device__ __forceinline__ int piece_order(int i, int n) {
-  return (i == 0 || n <= 2) ? i : (i == 1 ? n - 1 : i - 1);
-}
-
-// Piece i (in run order) of a part (tile_meta row: begin batch, begin block,
-// end batch, end block, split index of the first piece, number of pieces).
-// Out of line: every role walks the pieces, once per piece.
+// Piece i of a part (tile_meta row: begin batch, begin block, end batch, end
+// block, split index of the first piece, number of pieces).  Out of line:
+// every role walks the pieces, once per piece.
 __device__ __noinline__ Piece get_piece_at(const int32_t *seq_lens, int n_ctx,
                                            const int32_t *meta, int i) {
   Piece pc;
-  i = piece_order(i, meta[5]);
   pc.b = meta[0] + i;
   const int len = seq_lens ? seq_lens[pc.b] : n_ctx;
   const int nblk = len > 0 ? (len + kBlk - 1) / kBlk : 0;
@@ -412,49 +394,6 @@ __device__ __noinline__ void write_o_half(uint32_t trow, int ch, int q4, int lan
   }
 }
 
-// Value CTA, after writing a split piece's partial rows and LSEs (all 256
-// epilogue threads, index tt): count the piece, and if it was the sequence's
-// last, merge the sequence's partials of this query block into the output.
-// Writers fence before the count and the merger fences after it, so the
-// other CTAs' partials are visible to its L2 (ld.global.cg) loads.  The merge
-// folds the partials in slot order: the result is the same whichever piece
-// finishes last.
-template <typename T>
-__device__ __noinline__ void merge_if_last(const Params &p, int b, int mb, int first_slot,
-                                           int n_split, int row0, int n_rows, int tt,
-                                           volatile int *flag) {
-  __threadfence();
-  named_bar_sync(1, 256);
-  if (tt == 0) {
-    int *cnt = p.split_counters + static_cast<int64_t>(b) * gridDim.y + mb;
-    const bool last = atomicAdd(cnt, 1) + 1 == n_split;
-    if (last) *cnt = 0;  // zero again for the next call
-    __threadfence();
-    *flag = last ? 1 : 0;
-  }
-  named_bar_sync(1, 256);
-  if (!*flag) return;
-  const int rows_total = p.s_q * p.h_q;
-  const int lane = tt & 31;
-  for (int r = tt >> 5; r < n_rows; r += 8) {
-    const int flat = row0 + r;
-    const int s_tok = flat / p.h_q, h = flat % p.h_q;
-    const int64_t o_off = static_cast<int64_t>(b) * p.o_sb + s_tok * p.o_ss + h * p.o_sh;
-    float l;
-    if (p.out_f32)
-      l = merge_row<float, true>(p.part_o, p.part_lse, first_slot, n_split,
-                                 static_cast<int64_t>(rows_total) * p.d_v, rows_total,
-                                 static_cast<int64_t>(flat) * p.d_v, flat, p.d_v,
-                                 static_cast<float *>(p.out) + o_off, lane);
-    else
-      l = merge_row<T, true>(p.part_o, p.part_lse, first_slot, n_split,
-                             static_cast<int64_t>(rows_total) * p.d_v, rows_total,
-                             static_cast<int64_t>(flat) * p.d_v, flat, p.d_v,
-                             static_cast<T *>(p.out) + o_off, lane);
-    if (lane == 0) p.lse[(static_cast<int64_t>(b) * p.h_q + h) * p.s_q + s_tok] = l;
-  }
-}
-
 template <typename T, bool kSparse>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mla_decode_sv_kernel(const __grid_constant__ CUtensorMap q_map,
@@ -497,10 +436,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&bars->ch_empty[i]), 1);
     }
     for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&bars->pair[i]), 64);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&bars->stg_ready[i]), 128);
-      mbar_init(smem_u32(&bars->stg_free[i]), 1);
-    }
+    for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bars->stg_ready[i]), 128);
     for (int i = 0; i < kPSlots; ++i) {
       mbar_init(smem_u32(&bars->p_free[i]), 1);
       mbar_init(smem_u32(&bars->p_full[i]), 1);
@@ -526,7 +462,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bars->tmem_base;
   cluster_sync();  // the peer's barriers exist before any remote access
   // every CTA of the grid is resident: the combine kernel queued behind this
-  // one may start (its blocks with nothing to merge finish meanwhile)
+  // one may be launched (its blocks with nothing to merge finish meanwhile,
+  // the others wait for this grid to complete)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (rank == 0) {
@@ -918,20 +855,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // pb & 1) and sent with one bulk copy: 1024 separate 16-byte
             // remote stores per block crowd the memory-instruction queues
             // that the producer's and MMA warp's instructions also use.
-            // The staging buffer (pb & 1) was last sent for block pb - 2: it
-            // may be rewritten once that copy has landed in the value CTA,
-            // which the value CTA's MMA warp relays (stg_free) as soon as it
-            // sees the block's P arrive -- not once the block's PV is done,
-            // which would tie every softmax step to the value CTA's tensor
-            // pipe two blocks back.
+            // The staging buffer was last sent for block pb - 2, whose PV has
+            // finished once p_free of its slot has (its copy had landed).
+            // (Relaying the copy's arrival back from the value CTA instead
+            // measured no faster: this wait is not what paces the pair.)
             ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->p_free[pslot]),
                                                    ((pb / kPSlots) & 1) ^ 1, abort_flag, p.status,
                                                    kDevTimeoutSoftmax));
             if (ok && pb >= 2)
-              ok = __all_sync(0xffffffffu,
-                              mbar_wait<true>(smem_u32(&bars->stg_free[pb & 1]),
-                                              ((pb - 2) >> 1) & 1, abort_flag, p.status,
-                                              kDevTimeoutSoftmax));
+              ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->p_free[(pb - 2) % kPSlots]),
+                                                     ((pb - 2) / kPSlots) & 1, abort_flag,
+                                                     p.status, kDevTimeoutSoftmax));
             if (!ok) break;
             const uint32_t stg = s_base + kOffStgP + (pb & 1) * kPBytes;
 #pragma unroll
@@ -1088,7 +1022,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (mbar_probe(bar, parity)) return true;
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma)) != 0;
       };
-      const uint32_t stg_free_remote = map_to_rank(smem_u32(&bars->stg_free[0]), 0);
       uint32_t vs = 0, gb = 0;
       int pi = 0;
       bool ok = true;
@@ -1107,8 +1040,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_arrive_expect_tx(smem_u32(&bars->p_full[ps]),
                                   kPBytes + (tile_first ? 512 + 16 : 0) + (piece_last ? 1024 : 0));
           ok = wait(smem_u32(&bars->p_full[ps]), ph);
-          // the block's P has landed: the score CTA may restage its buffer
-          if (ok && lane == 0) mbar_arrive_remote(stg_free_remote + (gb & 1) * 8);
           ok = ok && wait(smem_u32(&bars->m_read[ps]), ph);
           if (ok && first_blk) ok = wait(smem_u32(&bars->o_empty), (pi & 1) ^ 1);
           if (!ok) break;
@@ -1246,8 +1177,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           else
             p.part_lse[static_cast<int64_t>(slot_o) * rows_total + flat] = lse_row;
         }
-        if (!final_out && p.split_counters != nullptr && n_split <= kMlaMergeInKernelMax)
-          merge_if_last<T>(p, pc.b, mb, first_slot, n_split, row0, n_rows, tt, &bars->merge_flag);
       }
     }
   }
@@ -1321,7 +1250,6 @@ cudaError_t launch_mla_sv(const CUtensorMap &qm, const CUtensorMap &km, const CU
   p.topk = sparse ? a->topk : 0;
   p.total_rows = static_cast<int64_t>(a->num_pages) * a->page_size;
   p.uniform_rows = a->kv_stride_page == static_cast<int64_t>(a->page_size) * a->kv_stride_tok;
-  p.split_counters = a->split_counters;
   const dim3 grid(2 * a->num_sm_parts, m_blocks);
   if (a->dtype == FA_DTYPE_F16)
     return sparse ? launch_sv_t<__half, true>(qm, km, vm, gm, p, grid, stream)

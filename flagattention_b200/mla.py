@@ -65,42 +65,19 @@ def get_mla_metadata(cache_seqlens, num_q_tokens_per_head_k, num_heads_k, num_he
 _workspaces = {}
 
 
-def counter_count(batch, s_q, h_q):
-    """int32 split counters the decode needs: batch * s_q * ceil(h_q / 128)."""
-    return batch * s_q * -(-h_q // 128)
-
-
 def _workspace(device, batch, s_q, h_q, parts):
-    """Split scratch (f32 partial O and LSE, contents never read before the
-    same call writes them) and the split counters (zero between calls: every
-    completed decode leaves them zero), each cached per device and grown.
-    They are separate buffers: calls of other shapes use other parts of the
-    scratch, but every call relies on the counters it touches being zero."""
+    """Split scratch (f32 partial O and LSE), cached per device and grown;
+    returns (buffer, part_o address, part_lse address)."""
     po, pl = ctypes.c_size_t(0), ctypes.c_size_t(0)
     _lib.check(_lib.lib().fa_mla_workspace_size(batch, s_q, h_q, D_V, parts, ctypes.byref(po),
                                                 ctypes.byref(pl)), "fa_mla_workspace_size")
-    off_l = (po.value + 255) // 256 * 256
+    off = (po.value + 255) // 256 * 256
     key = device.index if device.index is not None else torch.cuda.current_device()
     buf = _workspaces.get(key)
-    if buf is None or buf.numel() < off_l + pl.value:
-        buf = torch.empty(off_l + pl.value, dtype=torch.uint8, device=device)
+    if buf is None or buf.numel() < off + pl.value:
+        buf = torch.empty(off + pl.value, dtype=torch.uint8, device=device)
         _workspaces[key] = buf
-    n_cnt = counter_count(batch, s_q, h_q)
-    cnt = _counters.get(key)
-    if cnt is None or cnt.numel() < n_cnt:
-        cnt = torch.zeros(n_cnt, dtype=torch.int32, device=device)
-        _counters[key] = cnt
-    return buf, buf.data_ptr() + off_l, cnt
-
-
-_counters = {}
-
-
-def reset_workspaces():
-    """Zero the cached split counters.  Needed only after a decode reported a
-    device status error: it may have stopped with counters part-way."""
-    for c in _counters.values():
-        c.zero_()
+    return buf, buf.data_ptr(), buf.data_ptr() + off
 
 
 class MlaCall:
@@ -109,23 +86,19 @@ class MlaCall:
     q: [B, s_q, h_q, 576] view (last dim dense); out: [B, s_q, h_q, 512]
     view of q's dtype or float32; lse: f32 [B, h_q, s_q] contiguous.
     Strides are read off the views.  ``run`` = decode + combine;
-    ``partial`` / ``combine`` launch the two kernels separately.  With
-    ``merge_in_kernel`` (the default) the decode kernel merges sequences
-    split into at most four pieces itself and the combine kernel only the
-    longer splits; without, the combine kernel merges every split.
+    ``partial`` / ``combine`` launch the two kernels separately.
     """
 
     def __init__(self, q, kcache, kv_stride_page, kv_stride_tok, num_pages, page_size,
                  block_table, seq_lens, n_ctx, tile_meta, num_splits, out, lse, scale,
-                 causal=False, indices=None, merge_in_kernel=True):
+                 causal=False, indices=None):
         B, s_q, h_q, d_qk = q.shape
         parts = tile_meta.shape[0]
-        ws, pl, cnt = _workspace(q.device, B, s_q, h_q, parts)
-        po = ws.data_ptr()
+        ws, po, pl = _workspace(q.device, B, s_q, h_q, parts)
         # the workspace is kept alive with the call: a later, larger call
         # replaces the cached buffer but must not free this one under it
         self._keep = (q, kcache, block_table, seq_lens, tile_meta, num_splits, out, lse, indices,
-                      ws, cnt)
+                      ws)
         a = _lib.MlaArgs()
         a.q = q.data_ptr()
         a.q_stride_b, a.q_stride_s, a.q_stride_h = q.stride(0), q.stride(1), q.stride(2)
@@ -153,7 +126,6 @@ class MlaCall:
         a.out_dtype = dtype_code(out)
         a.scale = float(scale)
         a.status = status_word(q.device).data_ptr()
-        a.split_counters = cnt.data_ptr() if merge_in_kernel else None
         self.args = a
         self._ref = ctypes.byref(a)
         self._stream = stream_of(q)

@@ -189,12 +189,6 @@ typedef struct fa_mla_args {
   float scale;
   int32_t *status; /* device int32 (nullable): nonzero after a bounded wait
                       inside the kernel gave up                             */
-  int32_t *split_counters; /* nullable: int32 [batch * s_q * ceil(h_q/128)],
-                      zero before the first call; every completed call
-                      leaves it zero.  Given, the decode kernel itself merges
-                      each sequence split into at most 4 pieces (the CTA pair
-                      finishing its last piece does); longer splits, and all
-                      splits when NULL, are merged by the combine kernel.   */
 } fa_mla_args;
 
 /* Number of 2-SM parts the scheduler should use on `device`: SMs / 2 / the
@@ -210,14 +204,13 @@ int fa_mla_get_metadata(const int32_t *seq_lens, int batch, int topk,
                         int num_sm_parts, int32_t *tile_meta,
                         int32_t *num_splits, void *stream);
 /* Decode kernel, then the combine kernel (queued as a programmatic
- * dependent: its blocks with nothing to merge finish during the decode). */
+ * dependent of the decode: its launch overlaps the decode, and its blocks for
+ * sequences that were not split exit before the decode ends). */
 int fa_mla_decode(const fa_mla_args *args, void *stream);
 /* Decode kernel only: sequences handled by one part are final in out / lse,
- * and so are the short splits merged in the kernel (split_counters given);
- * the other split sequences leave their partials in the workspace for
- * fa_mla_combine. */
+ * split sequences leave their partials in the workspace for fa_mla_combine. */
 int fa_mla_decode_partial(const fa_mla_args *args, void *stream);
-/* Combine only (the decode kernel's remaining split partials -> out / lse). */
+/* Combine only (the decode kernel's split partials -> out / lse). */
 int fa_mla_combine(const fa_mla_args *args, void *stream);
 
 /* Write n latent rows (576 dims, bf16 / f16 as dtype; row r at

@@ -33,11 +33,8 @@ def _prepared(seed, lens, parts):
     kc = d["kc"]
 
     def call(out, lse):
-        # merge_in_kernel=False: every split goes through the combine kernel,
-        # the same kernels the static-workspace entry point launches
         return MlaCall(d["q"], kc, kc.stride(0), kc.stride(1), kc.shape[0], kc.shape[1],
-                       d["bt"], d["lens"], 0, meta, splits, out, lse, 576 ** -0.5,
-                       merge_in_kernel=False)
+                       d["bt"], d["lens"], 0, meta, splits, out, lse, 576 ** -0.5)
     return d, call
 
 
@@ -45,7 +42,6 @@ def _static_decode(call):
     a = _lib.MlaArgs.from_buffer_copy(call.args)
     a.part_o = None              # the entry point must not need a workspace
     a.part_lse = None
-    a.split_counters = None
     st = _lib.lib().fa_mla_decode_static_workspace(ctypes.byref(a), fat.stream_of(call._keep[0]))
     _lib.check(st, "fa_mla_decode_static_workspace")
 
