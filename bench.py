@@ -13,10 +13,11 @@ of 64*N sequences is sharded by sequence across the ranks (greedy by KV bytes,
 no collective on the data path): weak scaling.
 
 The same line carries ``long_context``: BASELINE config 5 (2 sequences of
-1,048,576 tokens) with the KV pages split evenly over the N ranks, each rank
-decoding its pages into a packed f32 partial, one NCCL all-gather, and the
-on-device combine -- strong scaling, with the all-gather and combine times
-broken out.
+1,048,576 tokens) with the KV pages split evenly over the N ranks -- strong
+scaling.  Each rank decodes its pages; the kernel merging its split pieces
+stores every row into every rank's gather buffer over NVLink (peer stores,
+no collective), and a merge kernel waits for all rows and merges them.  The
+same step with one NCCL all-gather of packed partials is timed beside it.
 
 Inputs of sequence i (query and its KV rows) come from a CPU generator seeded
 with i, so both arms decode the same values.  ``--impl reference`` times the
@@ -373,11 +374,14 @@ LC_WORKLOAD = "long_context_mla_decode_b2_h128_ctx1m_bf16_kv_page_sharded"
 
 def run_long_context(args, world, rank, dev, flush):
     """BASELINE config 5 with the KV pages of both 1M-token sequences split
-    evenly over the ranks (strong scaling).  A step: decode of this rank's
-    pages (+ the combine of its own split pieces) into a packed f32 partial,
-    one NCCL all-gather of the partials, the log-sum-exp merge on the GPU.
-    At N = 1 the step is the plain decode to bf16.  Every phase is timed with
-    CUDA events on the launching stream; the figures are the max over ranks."""
+    evenly over the ranks (strong scaling).  A step: the decode of this
+    rank's pages; the kernel merging its split pieces, which stores every row
+    into every rank's gather buffer over NVLink; the kernel that waits for all
+    ranks' rows and merges them.  The same step with one NCCL all-gather of
+    packed partials (decode + combine, all-gather, merge) is timed beside it.
+    At N = 1 the step is the plain decode (+ combine) to bf16.  Every phase is
+    timed with CUDA events on the launching stream; the figures are the max
+    over ranks."""
     import torch
     import torch.distributed as dist
 
@@ -401,66 +405,103 @@ def run_long_context(args, world, rank, dev, flush):
     gq = torch.Generator(device=dev).manual_seed(SEED + 5999)          # same q on every rank
     q = torch.randn((LC_BATCH, 1, H_Q, D_QK), generator=gq, device=dev).to(torch.bfloat16)
     rows = LC_BATCH * H_Q
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(step, n_ev):
+        for _ in range(args.warmup):
+            step([torch.cuda.Event(enable_timing=True) for _ in range(n_ev)])
+        torch.cuda.synchronize()
+        assert fat.read_status(dev) == 0, "device wait timeout during warm-up (long context)"
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(steps)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(steps):
+            step(evs[i])
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        assert fat.read_status(dev) == 0, "device wait timeout in the timed region (long context)"
+        t = torch.tensor([sum(e[k].elapsed_time(e[k + 1]) for e in evs) / steps
+                          for k in range(n_ev - 1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    steps = max(3, min(args.steps, 100))
+    extra = {}
     if world == 1:
         meta, splits = fa.get_mla_metadata(seq, H_Q, 1)
         out = torch.empty((LC_BATCH, 1, H_Q, D_V), dtype=torch.bfloat16, device=dev)
         lse = torch.empty((LC_BATCH, H_Q, 1), dtype=torch.float32, device=dev)
         call = MlaCall(q, pool, pool.stride(0), pool.stride(1), pool.shape[0], PAGE, bt, seq, 0,
                        meta, splits, out, lse, D_QK ** -0.5)
-    else:
-        part = shard.PartialDecode(q, pool, bt, seq, D_QK ** -0.5)
-        call = part.call
-        gathered = torch.empty((world, part.packed.numel()), dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
 
-    def step(ev):
-        flush.fill_(1)
-        ev[0].record(stream)
-        call.run()
-        ev[1].record(stream)
-        if world > 1:
+        def step(ev):
+            flush.fill_(1)
+            ev[0].record(stream)
+            call.run()
+            ev[1].record(stream)
+
+        dec_ms, = timed(step, 2)
+        step_ms, push_ms, merge_ms = dec_ms, None, None
+        launches = 2
+    else:
+        # the product path: partials exchanged by peer stores (no collective)
+        peer = shard.PeerLongContextDecode(q, pool, bt, seq, D_QK ** -0.5)
+
+        def step(ev):
+            flush.fill_(1)
+            ev[0].record(stream)
+            peer.decode()
+            ev[1].record(stream)
+            peer.push()
+            ev[2].record(stream)
+            peer.merge()
+            ev[3].record(stream)
+
+        dec_ms, push_ms, merge_ms = timed(step, 4)
+        step_ms = dec_ms + push_ms + merge_ms
+        launches = 3
+        # for comparison: the same step with one NCCL all-gather of packed partials
+        part = shard.PartialDecode(q, pool, bt, seq, D_QK ** -0.5)
+        gathered = torch.empty((world, part.packed.numel()), dtype=torch.float32, device=dev)
+
+        def step_nccl(ev):
+            flush.fill_(1)
+            ev[0].record(stream)
+            part.call.run()
+            ev[1].record(stream)
             dist.all_gather_into_tensor(gathered.view(-1), part.packed)
             ev[2].record(stream)
             shard.merge_partials(gathered, rows, D_V, torch.bfloat16)
-        else:
-            ev[2].record(stream)
-        ev[3].record(stream)
+            ev[3].record(stream)
 
-    for _ in range(args.warmup):
-        step([torch.cuda.Event(enable_timing=True) for _ in range(4)])
-    torch.cuda.synchronize()
-    assert fat.read_status(dev) == 0, "device wait timeout during warm-up (long context)"
-    steps = max(3, min(args.steps, 100))
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
-    if world > 1:
+        n_dec, n_gather, n_merge = timed(step_nccl, 4)
+        extra = {"nccl_allgather_path": {"ms_per_step": n_dec + n_gather + n_merge,
+                                         "ms_decode_and_combine": n_dec,
+                                         "us_allgather": n_gather * 1e3, "us_merge": n_merge * 1e3}}
         dist.barrier()
-    torch.cuda.synchronize()
-    for i in range(steps):
-        step(evs[i])
-    torch.cuda.synchronize()
-    if world > 1:
+        peer.close()
         dist.barrier()
-    assert fat.read_status(dev) == 0, "device wait timeout in the timed region (long context)"
-    mean = lambda k0, k1: sum(e[k0].elapsed_time(e[k1]) for e in evs) / steps  # noqa: E731
-    t = torch.tensor([mean(0, 3), mean(0, 1), mean(1, 2), mean(2, 3)], dtype=torch.float64,
-                     device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, dec_ms, gather_ms, merge_ms = t.tolist()
     peak_gbs, _, peak_kind = measured_peaks()
     kv_bytes = LC_BATCH * local_len * D_QK * 2 + rows * (D_QK * 2 + D_V * 4 + 4)
-    return {"workload": LC_WORKLOAD, "baseline_config": 5, "n_gpus": world,
-            "scaling": "strong", "steps": steps,
-            "tokens_per_s": LC_BATCH / (step_ms * 1e-3), "ms_per_step": step_ms,
-            "ms_decode": dec_ms,
-            "us_allgather": gather_ms * 1e3 if world > 1 else None,
-            "us_merge": merge_ms * 1e3 if world > 1 else None,
-            "gpu_launches_per_step": 2 + (1 if world > 1 else 0),
-            "nccl_collectives_per_step": 1 if world > 1 else 0,
-            "allgather_bytes_per_rank": rows * (D_V + 1) * 4 if world > 1 else 0,
-            "tokens_per_rank": LC_BATCH * local_len,
-            "hbm_frac_decode": kv_bytes / (dec_ms * 1e-3) / 1e9 / peak_gbs,
-            "peak_source": peak_kind}
+    rec = {"workload": LC_WORKLOAD, "baseline_config": 5, "n_gpus": world,
+           "scaling": "strong", "steps": steps,
+           "tokens_per_s": LC_BATCH / (step_ms * 1e-3), "ms_per_step": step_ms,
+           "ms_decode": dec_ms,
+           "us_combine_push": push_ms * 1e3 if push_ms is not None else None,
+           "us_merge_wait": merge_ms * 1e3 if merge_ms is not None else None,
+           "exchange": ("peer stores over NVLink from the combine kernel into every rank's "
+                        "gather buffer, bounded wait + merge kernel (no collective)"
+                        if world > 1 else None),
+           "gpu_launches_per_step": launches,
+           "exchange_bytes_per_rank": rows * (D_V + 1) * 4 * (world - 1) if world > 1 else 0,
+           "tokens_per_rank": LC_BATCH * local_len,
+           "hbm_frac_decode": kv_bytes / (dec_ms * 1e-3) / 1e9 / peak_gbs,
+           "peak_source": peak_kind}
+    rec.update(extra)
+    return rec
 
 
 # ------------------------------------------------------------ CPU timing

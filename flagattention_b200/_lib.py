@@ -20,6 +20,9 @@ FA_ERR_NO_DEVICE = -4
 
 FA_DTYPE_BF16, FA_DTYPE_F16, FA_DTYPE_F32 = 0, 1, 2
 FA_MLA_META_INTS = 8
+FA_EXCHANGE_MAX_RANKS = 8
+FA_IPC_HANDLE_BYTES = 64
+FA_DEVICE_TIMEOUT_EXCHANGE = 4
 
 _i32, _i64, _f32, _vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -98,6 +101,12 @@ SIGNATURES = [
     ("fa_mla_append_rows", _i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i32, _i32, _i32,
                                   _vp]),
     ("fa_selftest_wait_timeout", _i32, [_vp, _vp]),
+    ("fa_ipc_export", _i32, [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)]),
+    ("fa_ipc_open", _i32, [_vp, ctypes.POINTER(_vp)]),
+    ("fa_ipc_close", _i32, [_vp]),
+    ("fa_mla_combine_push", _i32, [ctypes.POINTER(MlaArgs), _vp, _vp, _i32, _i32, _vp]),
+    ("fa_lse_merge_wait", _i32, [_vp, _i32, _i64, _i32, _vp, ctypes.c_uint64, _vp, _i32, _vp,
+                                 _vp, _i64, _vp]),
 ]
 
 _lib = None

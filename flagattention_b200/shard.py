@@ -8,10 +8,13 @@ is what makes both modes exact:
   nothing on the data path: no collective.
 * **Long-context decode** -- ``page_range`` gives each rank an even,
   contiguous range of one sequence's KV pages.  Every rank decodes its range to
-  an f32 partial (O, LSE) packed in one buffer; ``exchange_partials``
-  all-gathers the buffers in one collective (NCCL over NVLink on GPUs, any
-  backend in tests) and ``merge_partials`` runs the log-sum-exp combine
-  kernel over them on every rank.
+  an f32 partial (O, LSE).  ``PeerLongContextDecode`` exchanges the partials
+  without a collective: the kernel that merges a rank's own split pieces
+  writes each row into every rank's gather buffer (peer stores over NVLink,
+  CUDA IPC mappings, ``PeerExchange``) and the merge kernel waits for all
+  rows, bounded in time.  ``long_context_decode`` is the collective form: one
+  all-gather of packed partials (NCCL, or any backend in tests) and
+  ``merge_partials``.
 """
 
 import ctypes
@@ -160,6 +163,132 @@ class PartialDecode:
         """Decode into ``self.packed`` (asynchronous on the current stream)."""
         self.call.run()
         return self.packed
+
+
+class PeerExchange:
+    """Gather buffer of packed partials shared by the ranks of ``group``
+    through CUDA IPC, for exchanging partials with peer stores instead of a
+    collective (``fa_mla_combine_push`` / ``fa_lse_merge_wait``).
+
+    Each rank allocates two gather buffers f32 [world][rows * (d_v + 1)]
+    plus uint64 counters [world] (zeroed), exports them, and maps every
+    peer's.  Exchange k uses buffer k % 2: a rank can push exchange k + 1
+    while a slower peer still merges exchange k, but not exchange k + 2 (its
+    own merge of k + 1 waited for that peer's push of k + 1, which the peer
+    issues after its merge of k).  ``parts(k)`` / ``counters`` are this rank's
+    device addresses of every rank's buffer for exchange k (ctypes arrays,
+    index = rank).  The process-group call is only the one-time exchange of
+    the IPC handles (``all_gather_object``).  Every rank must run the same
+    sequence of exchanges; ``epoch`` counts them.  ``close`` unmaps the peers
+    (call it on every rank, after a barrier, before the buffers are dropped).
+    """
+
+    def __init__(self, rows, d_v=512, device=None, group=None):
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        if world > _lib.FA_EXCHANGE_MAX_RANKS:
+            raise _lib.Unsupported(f"peer exchange supports up to {_lib.FA_EXCHANGE_MAX_RANKS} ranks")
+        self.world, self.rank, self.rows, self.d_v = world, rank, rows, d_v
+        self._half = (world * rows * (d_v + 1) * 4 + 255) // 256 * 256
+        self._cnt_off = 2 * self._half
+        self.buf = torch.zeros(self._cnt_off + 8 * world, dtype=torch.uint8, device=device)
+        handle = ctypes.create_string_buffer(_lib.FA_IPC_HANDLE_BYTES)
+        off = ctypes.c_uint64(0)
+        _lib.check(_lib.lib().fa_ipc_export(ctypes.c_void_p(self.buf.data_ptr()), handle,
+                                            ctypes.byref(off)), "fa_ipc_export")
+        mine = (bytes(handle.raw), int(off.value))
+        everyone = [None] * world
+        dist.all_gather_object(everyone, mine, group=group)
+        self._opened = []
+        addr = []
+        for r, (h, o) in enumerate(everyone):
+            if r == rank:
+                addr.append(self.buf.data_ptr())
+                continue
+            base = ctypes.c_void_p(0)
+            _lib.check(_lib.lib().fa_ipc_open(ctypes.create_string_buffer(h, len(h)),
+                                              ctypes.byref(base)), "fa_ipc_open")
+            self._opened.append(base)
+            addr.append(base.value + o)
+        self._parts = [(ctypes.c_void_p * world)(*[a + h * self._half for a in addr])
+                       for h in (0, 1)]
+        self.counters = (ctypes.c_void_p * world)(*[a + self._cnt_off for a in addr])
+        self.epoch = 0
+
+    def parts(self, epoch):
+        return self._parts[epoch % 2]
+
+    def local_parts(self, epoch):
+        return self.buf.data_ptr() + (epoch % 2) * self._half
+
+    @property
+    def local_counters(self):
+        return self.buf.data_ptr() + self._cnt_off
+
+    def close(self):
+        for base in self._opened:
+            _lib.check(_lib.lib().fa_ipc_close(base), "fa_ipc_close")
+        self._opened = []
+
+
+class PeerLongContextDecode:
+    """Long-context decode with the KV pages split over the ranks, partials
+    exchanged by peer stores: per call one decode kernel, one combine-and-push
+    kernel (this rank's merged rows straight into every rank's gather buffer,
+    over NVLink) and one merge kernel that waits for every rank's rows (at
+    most ``timeout_s``) and merges them.  No collective library call on the
+    data path.  q [B, 1, h_q, 576] replicated; kcache / block_table /
+    seq_lens are this rank's pages (``shard_pages``).  ``run`` returns
+    (out [B, 1, h_q, 512] of q's dtype, lse f32 [B, h_q, 1]); a timed-out wait
+    leaves them unwritten and sets the device status word (``read_status``).
+    """
+
+    def __init__(self, q, kcache, block_table, seq_lens, softmax_scale=None, group=None,
+                 timeout_s=2.0):
+        from flagattention_b200._torch import status_word
+        B, _, h_q, _ = q.shape
+        self.part = PartialDecode(q, kcache, block_table, seq_lens, softmax_scale)
+        self.rows = B * h_q
+        self.x = PeerExchange(self.rows, 512, q.device, group)
+        self.out = torch.empty((B, 1, h_q, 512), dtype=q.dtype, device=q.device)
+        self.lse = torch.empty((B, h_q, 1), dtype=torch.float32, device=q.device)
+        self.status = status_word(q.device)
+        self.timeout_ns = int(timeout_s * 1e9)
+        self._stream = stream_of(q)
+
+    def decode(self):
+        """This rank's decode kernel (its pages) into the split workspace /
+        its f32 rows."""
+        _lib.check(_lib.lib().fa_mla_decode_partial(self.part.call._ref, self._stream),
+                   "fa_mla_decode_partial")
+
+    def push(self):
+        """Merge this rank's split pieces and store every row into every
+        rank's gather buffer for the next exchange."""
+        x = self.x
+        x.epoch += 1
+        _lib.check(_lib.lib().fa_mla_combine_push(self.part.call._ref, x.parts(x.epoch),
+                                                  x.counters, x.world, x.rank, self._stream),
+                   "fa_mla_combine_push")
+
+    def merge(self):
+        """Wait for every rank's rows of the current exchange, merge them."""
+        x = self.x
+        _lib.check(_lib.lib().fa_lse_merge_wait(
+            ctypes.c_void_p(x.local_parts(x.epoch)), x.world, self.rows, 512,
+            ctypes.c_void_p(x.local_counters), x.epoch * self.rows,
+            ctypes.c_void_p(self.out.data_ptr()), dtype_code(self.out),
+            ctypes.c_void_p(self.lse.data_ptr()), ctypes.c_void_p(self.status.data_ptr()),
+            self.timeout_ns, self._stream), "fa_lse_merge_wait")
+
+    def run(self):
+        self.decode()
+        self.push()
+        self.merge()
+        return self.out, self.lse
+
+    def close(self):
+        self.x.close()
 
 
 def decode_partial(q, kcache, block_table, seq_lens, softmax_scale=None):

@@ -32,6 +32,9 @@
  *   fa_mla_append_rows        no reference function: writes new tokens'
  *                             latent rows into the paged pool read by the
  *                             decode (the cache layout of paged.py:22-23)
+ *   fa_mla_combine_push,      paged.py:366-449 / split_kv.py:198-228 merges
+ *   fa_lse_merge_wait         carried across GPUs (the reference has no
+ *                             multi-GPU code); fa_ipc_* map peer memory
  */
 #ifndef FLAGATTN_B200_H_
 #define FLAGATTN_B200_H_
@@ -212,6 +215,46 @@ int fa_mla_decode(const fa_mla_args *args, void *stream);
 int fa_mla_decode_partial(const fa_mla_args *args, void *stream);
 /* Combine only (the decode kernel's split partials -> out / lse). */
 int fa_mla_combine(const fa_mla_args *args, void *stream);
+
+/* ---- KV-page-sharded decode across GPUs (one process per GPU) -----------
+ * The reference is single-GPU; these entry points carry its split merge
+ * (split_kv.py:198-228) across GPUs with peer stores instead of a collective.
+ * Each rank keeps a gather buffer, f32 [world][rows * (d_v + 1)] (part r:
+ * O rows [rows][d_v] in (batch, token, head) order, then their LSEs), and
+ * uint64 counters [world] (zero when allocated; counter r = rows delivered by
+ * rank r, growing by `rows` per exchange, never reset).  dst_parts /
+ * dst_counters are HOST arrays of `world` device addresses: this rank's
+ * mappings of every rank's gather buffer / counters (its own included), e.g.
+ * opened with fa_ipc_open.  Alternate two gather buffers between
+ * consecutive exchanges: a rank may push exchange k + 1 while a slower peer
+ * still merges exchange k (never k + 2, as its merge of k + 1 waits for that
+ * peer's push of k + 1, issued after the peer's merge of k). */
+#define FA_EXCHANGE_MAX_RANKS 8
+#define FA_IPC_HANDLE_BYTES 64
+/* CUDA IPC export of the allocation holding `ptr` (a cudaMalloc block):
+ * writes the 64-byte handle and ptr's offset inside the block. */
+int fa_ipc_export(const void *ptr, void *handle, uint64_t *offset);
+/* Map a peer process's exported allocation into this process (peer access
+ * enabled); *base is the block's start.  fa_ipc_close unmaps it. */
+int fa_ipc_open(const void *handle, void **base);
+int fa_ipc_close(void *base);
+/* After fa_mla_decode_partial with out_dtype f32 (this rank's page range):
+ * merge each sequence's split pieces and write every query row (O, LSE) into
+ * slot `rank` of every rank's gather buffer, then add the rows delivered to
+ * counter `rank` of every rank.  Launched as a programmatic dependent of the
+ * decode.  paged.py:366-449 merge, fused with the exchange. */
+int fa_mla_combine_push(const fa_mla_args *args, float *const *dst_parts,
+                        unsigned long long *const *dst_counters, int world, int rank,
+                        void *stream);
+/* Wait until every counter holds `target` rows (k * rows after the k-th
+ * exchange), at most timeout_ns, then merge the `world` parts of every row
+ * (split_kv.py:198-228): out [rows][d_v] of dtype, lse f32 [rows].  On a
+ * timeout nothing is written and *status (device int32) becomes
+ * FA_DEVICE_TIMEOUT_EXCHANGE. */
+#define FA_DEVICE_TIMEOUT_EXCHANGE 4
+int fa_lse_merge_wait(const float *parts, int world, int64_t rows, int d_v,
+                      const unsigned long long *counters, unsigned long long target, void *out,
+                      int dtype, float *lse, int32_t *status, int64_t timeout_ns, void *stream);
 
 /* Write n latent rows (576 dims, bf16 / f16 as dtype; row r at
  * rows + r * rows_stride elements, unit inner stride) into the pool row
