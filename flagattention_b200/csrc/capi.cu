@@ -20,7 +20,7 @@ void launch_mla_metadata(const int32_t *, int, int, int, int32_t *, int32_t *, c
 void launch_lse_combine(const float *, const float *, int, int64_t, int64_t, int64_t, int, int,
                         int, void *, int, int64_t, int64_t, int64_t, float *, cudaStream_t);
 cudaError_t launch_mla_combine(const float *, const float *, const int32_t *, int, int, int, int,
-                               void *, int, int64_t, int64_t, int64_t, float *, cudaStream_t);
+                               bool, void *, int, int64_t, int64_t, int64_t, float *, cudaStream_t);
 cudaError_t launch_generic_decode(const fa_decode_args *, cudaStream_t);
 size_t generic_smem_bytes(int, int);
 cudaError_t launch_mla_sv(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
@@ -379,8 +379,11 @@ int fa_mla_combine(const fa_mla_args *a, void *stream) {
   int st = validate_mla(a);
   if (st != FA_OK) return st;
   if (a->batch == 0) return FA_OK;
+  // few sequences over many parts: each is split many ways, so the combine
+  // spreads a row's partials over four warps
+  const bool wide = static_cast<int64_t>(a->batch) * 4 <= a->num_sm_parts;
   cudaError_t e = fa::launch_mla_combine(a->part_o, a->part_lse, a->num_splits, a->batch, a->s_q,
-                                         a->h_q, a->d_v, a->out, a->out_dtype,
+                                         a->h_q, a->d_v, wide, a->out, a->out_dtype,
                                          a->o_stride_b, a->o_stride_s, a->o_stride_h, a->lse,
                                          static_cast<cudaStream_t>(stream));
   if (e == cudaSuccess) e = cudaGetLastError();

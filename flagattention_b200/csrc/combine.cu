@@ -29,31 +29,32 @@ __global__ void __launch_bounds__(128, 8) lse_combine_kernel(const float *__rest
 
 // MLA: sequence b owns slots num_splits[b] .. num_splits[b+1]-1 of
 // part_o [slot][s_q*h_q][d_v]; a sequence of one piece was written straight to
-// the output.  One warp per row, partials loaded four at a time (a long split
-// -- one 1M-token sequence spread over 37 parts -- waits for 10 memory round
-// trips instead of 19).  Launched as a programmatic dependent of the decode
-// kernel: its launch overlaps the decode, blocks of unsplit sequences exit
-// while the decode still runs, and the others wait for the decode grid to
-// complete (griddepcontrol.wait) before reading partials.
-template <typename T>
-__global__ void __launch_bounds__(128, 4) mla_combine_kernel(const float *__restrict__ part_o,
-                                   const float *__restrict__ part_lse,
-                                   const int32_t *__restrict__ num_splits, int s_q, int h_q,
-                                   int d_v, T *__restrict__ out, int64_t o_sb, int64_t o_ss,
-                                   int64_t o_sh, float *__restrict__ lse) {
+// the output.  Narrow form: 128-thread blocks, one warp per row (four rows),
+// partials loaded four at a time (one round trip per four partials).  Wide
+// form (few sequences each split over many parts): 256-thread blocks, two rows,
+// four warps per row (mla_row_state).  Launched as a programmatic dependent of
+// the decode kernel: its launch overlaps the decode, blocks of unsplit
+// sequences exit while the decode still runs, and the others wait for the
+// decode grid to complete (griddepcontrol.wait) before reading partials.
+template <typename T, bool kWide>
+__global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
+    mla_combine_kernel(const float *__restrict__ part_o, const float *__restrict__ part_lse,
+                       const int32_t *__restrict__ num_splits, int s_q, int h_q, int d_v,
+                       T *__restrict__ out, int64_t o_sb, int64_t o_ss, int64_t o_sh,
+                       float *__restrict__ lse) {
+  __shared__ MergeState states[kWide ? 8 : 1][32];
   const int b = blockIdx.y;
   const int first = num_splits[b];  // written by the metadata kernel, before the decode
   const int n = num_splits[b + 1] - first;
   if (n < 2) return;
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows = s_q * h_q;
-  const int flat = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  if (flat >= rows) return;
+  const int flat = kWide ? blockIdx.x * 2 + (warp >> 2) : blockIdx.x * 4 + warp;
+  const int j = kWide ? (warp & 3) : 0;
   MergeState st;
-  st.init();
-  fold_parts<false, 4>(st, part_o, part_lse, first, 0, 1, n, static_cast<int64_t>(rows) * d_v,
-                       rows, static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
+  mla_row_state<kWide>(st, part_o, part_lse, first, n, rows, flat, d_v, lane, j, warp, states);
+  if (j != 0 || flat >= rows) return;
   const int s = flat / h_q, h = flat % h_q;
   const float l = finish_row<T>(st, d_v, out + b * o_sb + s * o_ss + h * o_sh, lane);
   if (lane == 0) lse[(static_cast<int64_t>(b) * h_q + h) * s_q + s] = l;
@@ -93,33 +94,37 @@ void launch_lse_combine(const float *part_o, const float *part_lse, int num_part
 template <typename T>
 cudaError_t launch_mla_combine_t(const float *part_o, const float *part_lse,
                                  const int32_t *num_splits, int batch, int s_q, int h_q, int d_v,
-                                 void *out, int64_t o_sb, int64_t o_ss, int64_t o_sh, float *lse,
-                                 cudaStream_t stream) {
+                                 bool wide, void *out, int64_t o_sb, int64_t o_ss, int64_t o_sh,
+                                 float *lse, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((s_q * h_q + 3) / 4, batch);
-  cfg.blockDim = dim3(128);
+  const int rows = s_q * h_q;
+  cfg.gridDim = wide ? dim3((rows + 1) / 2, batch) : dim3((rows + 3) / 4, batch);
+  cfg.blockDim = dim3(wide ? 256 : 128);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, mla_combine_kernel<T>, part_o, part_lse, num_splits, s_q, h_q,
-                            d_v, static_cast<T *>(out), o_sb, o_ss, o_sh, lse);
+  if (wide)
+    return cudaLaunchKernelEx(&cfg, mla_combine_kernel<T, true>, part_o, part_lse, num_splits, s_q,
+                              h_q, d_v, static_cast<T *>(out), o_sb, o_ss, o_sh, lse);
+  return cudaLaunchKernelEx(&cfg, mla_combine_kernel<T, false>, part_o, part_lse, num_splits, s_q,
+                            h_q, d_v, static_cast<T *>(out), o_sb, o_ss, o_sh, lse);
 }
 
 cudaError_t launch_mla_combine(const float *part_o, const float *part_lse,
                                const int32_t *num_splits, int batch, int s_q, int h_q, int d_v,
-                               void *out, int dtype, int64_t o_sb, int64_t o_ss, int64_t o_sh,
-                               float *lse, cudaStream_t stream) {
+                               bool wide, void *out, int dtype, int64_t o_sb, int64_t o_ss,
+                               int64_t o_sh, float *lse, cudaStream_t stream) {
   if (dtype == FA_DTYPE_BF16)
     return launch_mla_combine_t<__nv_bfloat16>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v,
-                                               out, o_sb, o_ss, o_sh, lse, stream);
+                                               wide, out, o_sb, o_ss, o_sh, lse, stream);
   if (dtype == FA_DTYPE_F32)
-    return launch_mla_combine_t<float>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v, out,
-                                       o_sb, o_ss, o_sh, lse, stream);
-  return launch_mla_combine_t<__half>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v, out,
-                                      o_sb, o_ss, o_sh, lse, stream);
+    return launch_mla_combine_t<float>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v, wide,
+                                       out, o_sb, o_ss, o_sh, lse, stream);
+  return launch_mla_combine_t<__half>(part_o, part_lse, num_splits, batch, s_q, h_q, d_v, wide,
+                                      out, o_sb, o_ss, o_sh, lse, stream);
 }
 
 }  // namespace fa

@@ -32,17 +32,21 @@ struct PeerTargets {
   unsigned long long *counters[FA_EXCHANGE_MAX_RANKS];
 };
 
-// One warp per query row of the rank's decode (grid: row groups of four x
-// sequences).  A sequence split over several parts is merged from the split
-// workspace; a sequence decoded by one part is read from the decode's f32
-// output.  The row then goes to slot `rank` of every rank's gather buffer.
-// Launched as a programmatic dependent of the decode kernel.
-__global__ void __launch_bounds__(128, 4)
+// A query row of the rank's decode per warp (narrow form, four rows per
+// 128-thread block) or per four warps (wide form, two rows per 256-thread
+// block: few sequences split over many parts, see mla_row_state).  A
+// sequence split over several parts is merged from the split workspace; a
+// sequence decoded by one part is read from the decode's f32 output.  The
+// row then goes to slot `rank` of every rank's gather buffer.  Launched as a
+// programmatic dependent of the decode kernel.
+template <bool kWide>
+__global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
     mla_combine_push_kernel(const float *__restrict__ part_o, const float *__restrict__ part_lse,
                             const int32_t *__restrict__ num_splits, const float *__restrict__ out,
                             int64_t o_sb, int64_t o_ss, int64_t o_sh,
                             const float *__restrict__ lse_in, int batch, int s_q, int h_q, int d_v,
                             PeerTargets peers, int world, int rank) {
+  __shared__ MergeState states[kWide ? 8 : 1][32];
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode's outputs are complete
   const int b = blockIdx.y;
   const int first = num_splits[b];
@@ -51,34 +55,38 @@ __global__ void __launch_bounds__(128, 4)
   const int rows = s_q * h_q;
   const int64_t rows_all = static_cast<int64_t>(batch) * rows;
   const int64_t part_stride = rows_all * (d_v + 1);
-  const int flat = blockIdx.x * 4 + warp;
-  if (flat < rows) {
+  const int per_block = kWide ? 2 : 4;
+  const int flat = blockIdx.x * per_block + (kWide ? (warp >> 2) : warp);
+  const int j = kWide ? (warp & 3) : 0;
+  float4 v[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  float l = -INFINITY;
+  if (n >= 2) {
+    MergeState st;
+    mla_row_state<kWide>(st, part_o, part_lse, first, n, rows, flat, d_v, lane, j, warp, states);
+    l = (st.z > 0.f) ? st.m + __logf(st.z) : -INFINITY;
+    const float inv = (st.z > 0.f) ? 1.f / st.z : 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      v[k] = make_float4(st.acc[k].x * inv, st.acc[k].y * inv, st.acc[k].z * inv,
+                         st.acc[k].w * inv);
+  } else if (flat < rows && j == 0) {
     const int s = flat / h_q, h = flat % h_q;
-    float4 v[4];
-    float l;
-    if (n >= 2) {
-      MergeState st;
-      st.init();
-      fold_parts<false, 4>(st, part_o, part_lse, first, 0, 1, n, static_cast<int64_t>(rows) * d_v,
-                           rows, static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
-      l = (st.z > 0.f) ? st.m + __logf(st.z) : -INFINITY;
-      const float inv = (st.z > 0.f) ? 1.f / st.z : 0.f;
+    const float *src = out + b * o_sb + s * o_ss + h * o_sh;
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        v[k] = make_float4(st.acc[k].x * inv, st.acc[k].y * inv, st.acc[k].z * inv,
-                           st.acc[k].w * inv);
-    } else {
-      const float *src = out + b * o_sb + s * o_ss + h * o_sh;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int d = lane * 4 + k * 128;
-        v[k] = d < d_v ? __ldg(reinterpret_cast<const float4 *>(src + d))
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      l = __ldg(lse_in + (static_cast<int64_t>(b) * h_q + h) * s_q + s);
+    for (int k = 0; k < 4; ++k) {
+      const int d = lane * 4 + k * 128;
+      v[k] = d < d_v ? __ldg(reinterpret_cast<const float4 *>(src + d))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    l = __ldg(lse_in + (static_cast<int64_t>(b) * h_q + h) * s_q + s);
+  }
+  if (flat < rows && j == 0) {
     const int64_t grow = static_cast<int64_t>(b) * rows + flat;
-    for (int r = 0; r < world; ++r) {
+#pragma unroll
+    for (int r = 0; r < FA_EXCHANGE_MAX_RANKS; ++r) {  // unrolled: the pointers stay in registers
+      if (r >= world) break;
       float *dst = peers.parts[r] + rank * part_stride;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -93,10 +101,12 @@ __global__ void __launch_bounds__(128, 4)
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const int done = max(0, min(4, rows - static_cast<int>(blockIdx.x) * 4));
+    const int done = max(0, min(per_block, rows - static_cast<int>(blockIdx.x) * per_block));
     if (done > 0)
-      for (int r = 0; r < world; ++r)
-        atomicAdd_system(peers.counters[r] + rank, static_cast<unsigned long long>(done));
+#pragma unroll
+      for (int r = 0; r < FA_EXCHANGE_MAX_RANKS; ++r)
+        if (r < world)
+          atomicAdd_system(peers.counters[r] + rank, static_cast<unsigned long long>(done));
   }
 }
 
@@ -239,18 +249,22 @@ int fa_mla_combine_push(const fa_mla_args *a, float *const *dst_parts,
     t.counters[r] = dst_counters[r];
   }
   if (a->batch == 0) return FA_OK;
+  const int rows = a->s_q * a->h_q;
+  // few sequences over many parts: a row's partials spread over four warps
+  const bool wide = static_cast<int64_t>(a->batch) * 4 <= a->num_sm_parts;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a->s_q * a->h_q + 3) / 4, a->batch);
-  cfg.blockDim = dim3(128);
+  cfg.gridDim = wide ? dim3((rows + 1) / 2, a->batch) : dim3((rows + 3) / 4, a->batch);
+  cfg.blockDim = dim3(wide ? 256 : 128);
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, fa::mla_combine_push_kernel, a->part_o, a->part_lse,
-                                     a->num_splits, static_cast<const float *>(a->out),
-                                     a->o_stride_b, a->o_stride_s, a->o_stride_h,
+  auto kern = wide ? fa::mla_combine_push_kernel<true> : fa::mla_combine_push_kernel<false>;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a->part_o, a->part_lse, a->num_splits,
+                                     static_cast<const float *>(a->out), a->o_stride_b,
+                                     a->o_stride_s, a->o_stride_h,
                                      static_cast<const float *>(a->lse), a->batch, a->s_q, a->h_q,
                                      a->d_v, t, world, rank);
   if (e == cudaSuccess) e = cudaGetLastError();

@@ -107,6 +107,56 @@ __device__ __forceinline__ void fold_parts(MergeState &st, const float *__restri
   }
 }
 
+// a <- a folded with b (two states of the same row).
+__device__ __forceinline__ void fold_state(MergeState &a, const MergeState &b) {
+  const float m = fmaxf(a.m, b.m);
+  if (m == -INFINITY) return;
+  const float ka = (a.m == -INFINITY) ? 0.f : __expf(a.m - m);
+  const float kb = (b.m == -INFINITY) ? 0.f : __expf(b.m - m);
+  a.z = a.z * ka + b.z * kb;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    a.acc[k].x = a.acc[k].x * ka + b.acc[k].x * kb;
+    a.acc[k].y = a.acc[k].y * ka + b.acc[k].y * kb;
+    a.acc[k].z = a.acc[k].z * ka + b.acc[k].z * kb;
+    a.acc[k].w = a.acc[k].w * ka + b.acc[k].w * kb;
+  }
+  a.m = m;
+}
+
+// Merge state of query row `flat` of an MLA sequence whose n pieces sit in
+// split slots first .. first + n - 1 (part_o [slot][rows][d_v]).
+//   narrow (kWide false): the calling warp folds all n partials;
+//   wide (kWide true): the four warps w0 .. w0 + 3 of the block (warp j =
+//     w0 + j calls with j) fold partials j, j + 4, ... and the states meet in
+//     `states` (shared, [warps][32]) folded in warp order; the result is valid
+//     in warp w0.  Wide spreads one row's partials over four warps: for a few
+//     sequences split over many parts (one long sequence over 37 parts) the
+//     GPU has few rows but many partials per row.
+template <bool kWide>
+__device__ __forceinline__ void mla_row_state(MergeState &st, const float *__restrict__ part_o,
+                                              const float *__restrict__ part_lse, int first, int n,
+                                              int rows, int flat, int d_v, int lane, int j,
+                                              int warp, MergeState (*states)[32]) {
+  st.init();
+  if (!kWide) {
+    if (flat < rows)
+      fold_parts<false, 4>(st, part_o, part_lse, first, 0, 1, n,
+                           static_cast<int64_t>(rows) * d_v, rows,
+                           static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
+    return;
+  }
+  if (flat < rows && j < n)
+    fold_parts<false, 4>(st, part_o, part_lse, first, j, 4, n, static_cast<int64_t>(rows) * d_v,
+                         rows, static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
+  states[warp][lane] = st;
+  __syncthreads();
+  if (j == 0) {
+#pragma unroll
+    for (int k = 1; k < 4; ++k) fold_state(st, states[warp + k][lane]);
+  }
+}
+
 // Normalised output row and merged LSE of a state.
 template <typename T>
 __device__ __forceinline__ float finish_row(const MergeState &st, int d_v, T *out, int lane) {
