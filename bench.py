@@ -14,9 +14,9 @@ no collective on the data path): weak scaling.
 
 The same line carries ``long_context``: BASELINE config 5 (2 sequences of
 1,048,576 tokens) with the KV pages split evenly over the N ranks -- strong
-scaling.  Each rank decodes its pages; the kernel merging its split pieces
-stores every row into every rank's gather buffer over NVLink (peer stores,
-no collective), and a merge kernel waits for all rows and merges them.  The
+scaling.  Each rank decodes its pages; one cooperative kernel merges its
+split pieces, stores every row into every rank's gather buffer over NVLink
+(peer stores, no collective), waits for all ranks' rows and merges them.  The
 same step with one NCCL all-gather of packed partials is timed beside it.
 
 Inputs of sequence i (query and its KV rows) come from a CPU generator seeded
@@ -375,9 +375,9 @@ LC_WORKLOAD = "long_context_mla_decode_b2_h128_ctx1m_bf16_kv_page_sharded"
 def run_long_context(args, world, rank, dev, flush):
     """BASELINE config 5 with the KV pages of both 1M-token sequences split
     evenly over the ranks (strong scaling).  A step: the decode of this
-    rank's pages; the kernel merging its split pieces, which stores every row
-    into every rank's gather buffer over NVLink; the kernel that waits for all
-    ranks' rows and merges them.  The same step with one NCCL all-gather of
+    rank's pages; one cooperative kernel that merges its split pieces, stores
+    every row into every rank's gather buffer over NVLink, waits for all ranks'
+    rows and merges them.  The same step with one NCCL all-gather of
     packed partials (decode + combine, all-gather, merge) is timed beside it.
     At N = 1 the step is the plain decode (+ combine) to bf16.  Every phase is
     timed with CUDA events on the launching stream; the figures are the max
@@ -444,7 +444,7 @@ def run_long_context(args, world, rank, dev, flush):
             ev[1].record(stream)
 
         dec_ms, = timed(step, 2)
-        step_ms, push_ms, merge_ms = dec_ms, None, None
+        step_ms, xchg_ms = dec_ms, None
         launches = 2
     else:
         # the product path: partials exchanged by peer stores (no collective)
@@ -455,14 +455,12 @@ def run_long_context(args, world, rank, dev, flush):
             ev[0].record(stream)
             peer.decode()
             ev[1].record(stream)
-            peer.push()
+            peer.exchange()
             ev[2].record(stream)
-            peer.merge()
-            ev[3].record(stream)
 
-        dec_ms, push_ms, merge_ms = timed(step, 4)
-        step_ms = dec_ms + push_ms + merge_ms
-        launches = 3
+        dec_ms, xchg_ms = timed(step, 3)
+        step_ms = dec_ms + xchg_ms
+        launches = 2
         # for comparison: the same step with one NCCL all-gather of packed partials
         part = shard.PartialDecode(q, pool, bt, seq, D_QK ** -0.5)
         gathered = torch.empty((world, part.packed.numel()), dtype=torch.float32, device=dev)
@@ -490,10 +488,10 @@ def run_long_context(args, world, rank, dev, flush):
            "scaling": "strong", "steps": steps,
            "tokens_per_s": LC_BATCH / (step_ms * 1e-3), "ms_per_step": step_ms,
            "ms_decode": dec_ms,
-           "us_combine_push": push_ms * 1e3 if push_ms is not None else None,
-           "us_merge_wait": merge_ms * 1e3 if merge_ms is not None else None,
-           "exchange": ("peer stores over NVLink from the combine kernel into every rank's "
-                        "gather buffer, bounded wait + merge kernel (no collective)"
+           "us_exchange": xchg_ms * 1e3 if xchg_ms is not None else None,
+           "exchange": ("one cooperative kernel: merge this rank's split pieces, store every "
+                        "row into every rank's gather buffer over NVLink (peer stores), "
+                        "bounded wait for all ranks' rows, merge (no collective)"
                         if world > 1 else None),
            "gpu_launches_per_step": launches,
            "exchange_bytes_per_rank": rows * (D_V + 1) * 4 * (world - 1) if world > 1 else 0,

@@ -107,6 +107,8 @@ SIGNATURES = [
     ("fa_mla_combine_push", _i32, [ctypes.POINTER(MlaArgs), _vp, _vp, _i32, _i32, _vp]),
     ("fa_lse_merge_wait", _i32, [_vp, _i32, _i64, _i32, _vp, ctypes.c_uint64, _vp, _i32, _vp,
                                  _vp, _i64, _vp]),
+    ("fa_mla_combine_exchange", _i32, [ctypes.POINTER(MlaArgs), _vp, _vp, _i32, _i32,
+                                       ctypes.c_uint64, _vp, _i32, _vp, _vp, _i64, _vp]),
 ]
 
 _lib = None

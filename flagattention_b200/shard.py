@@ -233,10 +233,11 @@ class PeerExchange:
 
 class PeerLongContextDecode:
     """Long-context decode with the KV pages split over the ranks, partials
-    exchanged by peer stores: per call one decode kernel, one combine-and-push
-    kernel (this rank's merged rows straight into every rank's gather buffer,
-    over NVLink) and one merge kernel that waits for every rank's rows (at
-    most ``timeout_s``) and merges them.  No collective library call on the
+    exchanged by peer stores: per call one decode kernel and one cooperative
+    exchange kernel that merges this rank's split pieces, stores each row
+    straight into every rank's gather buffer (over NVLink), waits for every
+    rank's rows (at most ``timeout_s``) and merges them (``push`` / ``merge``
+    are the same two steps as separate launches).  No collective library call on the
     data path.  q [B, 1, h_q, 576] replicated; kcache / block_table /
     seq_lens are this rank's pages (``shard_pages``).  ``run`` returns
     (out [B, 1, h_q, 512] of q's dtype, lse f32 [B, h_q, 1]); a timed-out wait
@@ -281,10 +282,20 @@ class PeerLongContextDecode:
             ctypes.c_void_p(self.lse.data_ptr()), ctypes.c_void_p(self.status.data_ptr()),
             self.timeout_ns, self._stream), "fa_lse_merge_wait")
 
+    def exchange(self):
+        """Push and merge in one cooperative launch (fa_mla_combine_exchange)."""
+        x = self.x
+        x.epoch += 1
+        _lib.check(_lib.lib().fa_mla_combine_exchange(
+            self.part.call._ref, x.parts(x.epoch), x.counters, x.world, x.rank,
+            x.epoch * self.rows, ctypes.c_void_p(self.out.data_ptr()), dtype_code(self.out),
+            ctypes.c_void_p(self.lse.data_ptr()), ctypes.c_void_p(self.status.data_ptr()),
+            self.timeout_ns, self._stream), "fa_mla_combine_exchange")
+
     def run(self):
+        """Decode, then push + merge in one launch."""
         self.decode()
-        self.push()
-        self.merge()
+        self.exchange()
         return self.out, self.lse
 
     def close(self):

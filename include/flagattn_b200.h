@@ -256,6 +256,18 @@ int fa_lse_merge_wait(const float *parts, int world, int64_t rows, int d_v,
                       const unsigned long long *counters, unsigned long long target, void *out,
                       int dtype, float *lse, int32_t *status, int64_t timeout_ns, void *stream);
 
+/* fa_mla_combine_push and fa_lse_merge_wait in one cooperative launch (all
+ * blocks resident): every block merges and pushes its share of the rows and
+ * counts them, then waits (at most timeout_ns) for `target` rows from every
+ * rank and merges its share of the gathered rows (this rank's gather buffer
+ * and counters are dst_parts[rank] / dst_counters[rank]).  One launch after
+ * the decode instead of two; on a timeout nothing is merged and *status is
+ * FA_DEVICE_TIMEOUT_EXCHANGE. */
+int fa_mla_combine_exchange(const fa_mla_args *args, float *const *dst_parts,
+                            unsigned long long *const *dst_counters, int world, int rank,
+                            unsigned long long target, void *out, int dtype, float *lse,
+                            int32_t *status, int64_t timeout_ns, void *stream);
+
 /* Write n latent rows (576 dims, bf16 / f16 as dtype; row r at
  * rows + r * rows_stride elements, unit inner stride) into the pool row
  * slots[r] = page * page_size + offset of kcache (layout as in fa_mla_args;

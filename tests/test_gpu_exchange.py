@@ -134,6 +134,78 @@ def test_merge_wait_times_out_when_rows_never_arrive():
     assert_close("out after timeout", o.float().cpu().numpy(), want_o)
 
 
+def _exchange(pd, parts, cnts, world, rank, rows, target, timeout_ns=2_000_000_000):
+    """fa_mla_combine_exchange of one emulated rank: its merged output."""
+    out = torch.full((rows, D_V), float("nan"), dtype=torch.bfloat16, device="cuda")
+    lse = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+    st = fat.status_word(out.device)
+    arr_p = (ctypes.c_void_p * world)(*[p.data_ptr() for p in parts])
+    arr_c = (ctypes.c_void_p * world)(*[c.data_ptr() for c in cnts])
+    _lib.check(_lib.lib().fa_mla_combine_exchange(
+        pd.call._ref, arr_p, arr_c, world, rank, target, ctypes.c_void_p(out.data_ptr()),
+        fat.dtype_code(out), ctypes.c_void_p(lse.data_ptr()), ctypes.c_void_p(st.data_ptr()),
+        timeout_ns, fat.stream_of(out)), "exchange")
+    return out, lse
+
+
+def test_fused_exchange_with_emulated_peer():
+    """The one-launch exchange (push, wait, merge) on this GPU: rank 1's rows
+    are pushed first by the separate push kernel (which never waits), then
+    rank 0's fused kernel pushes its own rows, finds both ranks' rows and
+    merges; then rank 1's fused kernel does the same.  Both equal the
+    unsharded decode."""
+    world = 2
+    lens = np.array([20000, 777, 64 * 40], np.int32)
+    q, kc, bt = _inputs(95, lens)
+    B, h_q = len(lens), q.shape[2]
+    rows = B * h_q
+    meta, splits = fa.get_mla_metadata(torch.from_numpy(lens).cuda(), h_q, 1)
+    full, full_lse = fa.flash_mla_with_kvcache(q, kc, torch.from_numpy(bt).cuda(),
+                                               torch.from_numpy(lens).cuda(), D_V, meta, splits,
+                                               softmax_scale=SCALE)
+    parts, cnts = _buffers(world, rows)
+    pds = []
+    for rank in range(world):
+        lbt, llen = shard.shard_pages(bt, lens, PAGE, world, rank)
+        pds.append(shard.PartialDecode(q, kc, torch.from_numpy(lbt).cuda(),
+                                       torch.from_numpy(llen).cuda(), SCALE))
+    stream = fat.stream_of(q)
+    arr_p = (ctypes.c_void_p * world)(*[p.data_ptr() for p in parts])
+    arr_c = (ctypes.c_void_p * world)(*[c.data_ptr() for c in cnts])
+    L = _lib.lib()
+    _lib.check(L.fa_mla_decode_partial(pds[1].call._ref, stream), "decode 1")
+    _lib.check(L.fa_mla_combine_push(pds[1].call._ref, arr_p, arr_c, world, 1, stream), "push 1")
+    _lib.check(L.fa_mla_decode_partial(pds[0].call._ref, stream), "decode 0")
+    out0, lse0 = _exchange(pds[0], parts, cnts, world, 0, rows, rows)
+    _lib.check(L.fa_mla_decode_partial(pds[1].call._ref, stream), "decode 1")
+    out1, lse1 = _exchange(pds[1], parts, cnts, world, 1, rows, rows)
+    torch.cuda.synchronize()
+    assert fat.read_status(q.device) == 0
+    assert torch.equal(out0, out1) and torch.equal(lse0, lse1)
+    assert_close("out", out0.view(B, 1, h_q, D_V).float().cpu().numpy(),
+                 full.float().cpu().numpy())
+    assert_close("lse", lse0.view(B, h_q, 1).cpu().numpy(), full_lse.cpu().numpy())
+
+
+def test_fused_exchange_times_out_without_peer():
+    """A peer that never pushes: the fused kernel pushes its own rows, waits
+    at most its time limit, merges nothing and reports the exchange timeout."""
+    world = 2
+    lens = np.array([3000], np.int32)
+    q, kc, bt = _inputs(96, lens)
+    rows = q.shape[2]
+    parts, cnts = _buffers(world, rows)
+    lbt, llen = shard.shard_pages(bt, lens, PAGE, world, 0)
+    pd = shard.PartialDecode(q, kc, torch.from_numpy(lbt).cuda(), torch.from_numpy(llen).cuda(),
+                             SCALE)
+    _lib.check(_lib.lib().fa_mla_decode_partial(pd.call._ref, fat.stream_of(q)), "decode")
+    out, lse = _exchange(pd, parts, cnts, world, 0, rows, rows, timeout_ns=20_000_000)
+    torch.cuda.synchronize()
+    assert fat.read_status(q.device) == _lib.FA_DEVICE_TIMEOUT_EXCHANGE
+    assert torch.isnan(out.float()).all() and torch.isnan(lse).all()
+    assert int(cnts[1][0].item()) == rows                  # its own rows did reach the peer
+
+
 def _peer_worker(rank, world, port, outdir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     try:
@@ -147,8 +219,12 @@ def _peer_worker(rank, world, port, outdir):
         lbt, llen = shard.shard_pages(bt, lens, PAGE, world, rank)
         dec = shard.PeerLongContextDecode(q, kc, torch.from_numpy(lbt).cuda(),
                                           torch.from_numpy(llen).cuda(), SCALE)
-        for _ in range(3):                                          # three exchanges in a row
-            out, lse = dec.run()
+        for _ in range(2):                                          # exchanges in a row:
+            out, lse = dec.run()                                    # fused push + merge
+        dec.decode()
+        dec.push()                                                  # and as two launches
+        dec.merge()
+        out, lse = dec.out, dec.lse
         torch.cuda.synchronize()
         status = fat.read_status(q.device)
         np.savez(os.path.join(outdir, f"rank{rank}.npz"), out=out.float().cpu().numpy(),
