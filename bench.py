@@ -251,7 +251,7 @@ def run_ours(args):
     def decode_only(ev):
         flush.fill_(1)
         ev[0].record(stream)
-        call.partial()      # the decode kernel alone (its in-kernel merges included)
+        call.partial()      # the decode kernel alone
         ev[1].record(stream)
 
     for _ in range(args.warmup):
@@ -325,6 +325,8 @@ def run_ours(args):
     step_ms, dec_ms, e2e_ms = t.tolist()
 
     long_ctx = run_long_context(args, world, rank, dev, flush)
+    mtp = run_mtp_sharded(args, world, rank, dev, flush)
+    gqa = run_gqa(args, dev, flush)
 
     tokens = len(lens_all) * S_Q
     bytes_local = algorithmic_bytes(lens)
@@ -342,8 +344,7 @@ def run_ours(args):
             "hbm_frac_step": bytes_local / (step_ms * 1e-3) / 1e9 / peak_gbs,
             "tensor_tflops_decode": flops_local / (dec_ms * 1e-3) / 1e12,
             "ms_decode_kernel": dec_ms,
-            "ms_decode_kernel_note": "decode kernel timed alone in a second pass (in-kernel "
-                                     "merges of short splits included)",
+            "ms_decode_kernel_note": "decode kernel timed alone in a second pass",
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs,
                          "unit": "GB/s", "frac": achieved / peak_gbs,
                          "traffic": None, "peak_source": peak_kind,
@@ -358,6 +359,8 @@ def run_ours(args):
                                  "its blocks exit when every split was merged in the decode)",
             "clocks": clocks,
             "long_context": long_ctx,
+            "mtp_causal": mtp,
+            "gqa_paged": gqa,
         }
         if world == 1:
             rec["cpu_baseline"] = cpu_baseline(lens_all, args.cpu_seconds)
@@ -500,6 +503,138 @@ def run_long_context(args, world, rank, dev, flush):
            "peak_source": peak_kind}
     rec.update(extra)
     return rec
+
+
+# ------------------------- config 3: MTP causal, sequences over N ranks
+def run_mtp_sharded(args, world, rank, dev, flush):
+    """BASELINE config 3 (128 sequences, s_q = 2 causal, ctx log-uniform
+    [4096, 32768]) with the sequences split over the ranks by KV bytes (no
+    collective): strong scaling of the fixed batch.  A step: metadata-shared
+    decode + combine of this rank's sequences; max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import flagattention_b200 as fa
+    from flagattention_b200 import _torch as fat
+    from flagattention_b200.mla import MlaCall
+    from flagattention_b200.shard import partition_sequences
+
+    lens_all = other_lens(3)
+    mine = partition_sequences(lens_all, world)[rank]
+    lens = lens_all[mine]
+    B, s_q = len(lens), 2
+    g = torch.Generator(device=dev).manual_seed(SEED + 300 + rank)
+    npg = (lens + PAGE - 1) // PAGE
+    npages = int(npg.sum())
+    kc = torch.empty((npages, PAGE, 1, D_QK), dtype=torch.bfloat16, device=dev)
+    for a in range(0, npages, 8192):
+        b = min(npages, a + 8192)
+        kc[a:b] = torch.randn((b - a, PAGE, 1, D_QK), generator=g, device=dev)
+    q = torch.randn((B, s_q, H_Q, D_QK), generator=g, device=dev).to(torch.bfloat16)
+    perm = torch.randperm(npages, generator=g, device=dev).to(torch.int32)
+    bt = torch.zeros((B, int(npg.max())), dtype=torch.int32, device=dev)
+    off = 0
+    for i, k in enumerate(npg):
+        bt[i, :k] = perm[off:off + int(k)]
+        off += int(k)
+    seq = torch.from_numpy(lens).to(dev)
+    meta, splits = fa.get_mla_metadata(seq, s_q * H_Q, 1)
+    out = torch.empty((B, s_q, H_Q, D_V), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((B, H_Q, s_q), dtype=torch.float32, device=dev)
+    call = MlaCall(q, kc, kc.stride(0), kc.stride(1), npages, PAGE, bt, seq, 0, meta, splits,
+                   out, lse, D_QK ** -0.5, causal=True)
+    stream = torch.cuda.current_stream(dev)
+    steps = max(3, min(args.steps, 20))
+    for _ in range(args.warmup):
+        flush.fill_(1)
+        call.run()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for a, b in evs:
+        flush.fill_(1)
+        a.record(stream)
+        call.run()
+        b.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    assert fat.read_status(dev) == 0, "device wait timeout (config 3)"
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs) / steps], dtype=torch.float64,
+                     device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms = float(t.item())
+    flops = int(np.sum(lens_all.astype(np.int64))) * 2 * s_q * H_Q * (D_QK + D_V)
+    _, peak_tf, peak_kind = measured_peaks()
+    return {"workload": OTHER[3]["workload"], "baseline_config": 3, "n_gpus": world,
+            "scaling": "strong", "parallelism": f"seq-shard{world}", "steps": steps,
+            "global_batch": len(lens_all), "seq_q": s_q, "causal": True,
+            "tokens_per_s": len(lens_all) * s_q / (step_ms * 1e-3), "ms_per_step": step_ms,
+            "gpu_launches_per_step": 2,
+            "tensor_tflops_all_gpus": flops / (step_ms * 1e-3) / 1e12,
+            "tensor_frac_per_gpu": flops / (step_ms * 1e-3) / 1e12 / world / peak_tf,
+            "peak_source": peak_kind}
+
+
+# ------------------ the reference's own paged API at a GQA shape (per GPU)
+GQA = dict(seqs=32, heads_q=64, heads_kv=8, head=128, page=16, ctx=4096)
+
+
+def run_gqa(args, dev, flush):
+    """`paged_attention` (paged.py:20) at a grouped-query shape: 32 sequences
+    of 4096 tokens, 64 query heads over 8 kv heads (group 8), head size 128,
+    16-token pages in a random permutation, bf16.  Per GPU (each rank runs
+    its own).  Bytes: every K and V row once + Q + O."""
+    import torch
+
+    import flagattention_b200 as fa
+    from flagattention_b200 import _torch as fat
+
+    c = GQA
+    g = torch.Generator(device=dev).manual_seed(SEED + 400)
+    pages_per = c["ctx"] // c["page"]
+    npages = c["seqs"] * pages_per
+    shape = (npages, c["heads_kv"], c["page"], c["head"])
+    kc = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn((c["seqs"], c["heads_q"], c["head"]), generator=g, device=dev).to(torch.bfloat16)
+    bt = torch.randperm(npages, generator=g, device=dev).to(torch.int32).view(c["seqs"], -1)
+    lens = torch.full((c["seqs"],), c["ctx"], dtype=torch.int32, device=dev)
+    scale = c["head"] ** -0.5
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return fa.paged_attention(q, kc, vc, lens, bt, scale, c["ctx"])
+
+    for _ in range(args.warmup):
+        flush.fill_(1)
+        step()
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 50))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for a, b in evs:
+        flush.fill_(1)
+        a.record(stream)
+        step()
+        b.record(stream)
+    torch.cuda.synchronize()
+    assert fat.read_status(dev) == 0
+    ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    nbytes = 2 * kc.numel() * 2 + 2 * q.numel() * 2
+    peak_gbs, _, peak_kind = measured_peaks()
+    return {"workload": "gqa_paged_decode_b32_hq64_hkv8_d128_page16_ctx4096_bf16",
+            "api": "paged_attention (paged.py:20)", "steps": steps, "ms_per_step": ms,
+            "tokens_per_s": c["seqs"] / (ms * 1e-3),
+            "roofline": {"bound": "hbm", "achieved": nbytes / (ms * 1e-3) / 1e9,
+                         "peak": peak_gbs, "unit": "GB/s",
+                         "frac": nbytes / (ms * 1e-3) / 1e9 / peak_gbs,
+                         "algorithmic_bytes": nbytes, "peak_source": peak_kind},
+            "kernel": "generic_decode_kernel (+ lse combine when split)"}
 
 
 # ------------------------------------------------------------ CPU timing
@@ -686,9 +821,7 @@ def run_other(args):
                        "batch": B, "seq_q": s_q, "heads_q": H_Q, "topk": topk,
                        "causal": spec["causal"], "page_size": PAGE,
                        "l2": "flushed before every step (256 MB write, outside the events)"},
-            "ms_decode_kernel": dec_ms,
-            "ms_decode_kernel_note": "decode kernel timed alone in a second pass (in-kernel "
-                                     "merges of short splits included)",
+            "ms_decode_kernel": dec_ms, "ms_combine_kernel": step_ms - dec_ms,
             "roofline": {"bound": "hbm", "achieved": nbytes / (dec_ms * 1e-3) / 1e9,
                          "peak": peak_gbs, "unit": "GB/s",
                          "frac": nbytes / (dec_ms * 1e-3) / 1e9 / peak_gbs,
