@@ -634,7 +634,7 @@ def run_gqa(args, dev, flush):
                          "peak": peak_gbs, "unit": "GB/s",
                          "frac": nbytes / (ms * 1e-3) / 1e9 / peak_gbs,
                          "algorithmic_bytes": nbytes, "peak_source": peak_kind},
-            "kernel": "generic_decode_kernel (+ lse combine when split)"}
+            "kernel": "gqa_decode_kernel (tcgen05) after the entry scheduler, + merge of split entries"}
 
 
 # ------------------------------------------------------------ CPU timing

@@ -51,6 +51,7 @@ class DecodeArgs(ctypes.Structure):
         ("num_splits", _i32), ("partition_size", _i32),
         ("o", _vp), ("o_stride_b", _i64), ("o_stride_h", _i64), ("o_stride_m", _i64),
         ("lse", _vp), ("part_o", _vp), ("part_lse", _vp),
+        ("num_pages", _i32), ("sched", _vp), ("status", _vp),
     ]
 
 
@@ -81,9 +82,9 @@ SIGNATURES = [
                                    ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     ("fa_split_kv_num_splits", _i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                                       ctypes.POINTER(_i32)]),
-    ("fa_decode_workspace_size", _i32, [ctypes.POINTER(DecodeArgs),
-                                        ctypes.POINTER(ctypes.c_size_t),
-                                        ctypes.POINTER(ctypes.c_size_t)]),
+    ("fa_decode_uses_tensor_cores", _i32, [ctypes.POINTER(DecodeArgs)]),
+    ("fa_decode_workspace_size", _i32, [ctypes.POINTER(DecodeArgs), ctypes.POINTER(ctypes.c_size_t),
+                                        ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
     ("fa_paged_attention", _i32, [ctypes.POINTER(DecodeArgs), _vp]),
     ("fa_split_kv_attention", _i32, [ctypes.POINTER(DecodeArgs), _vp]),
     ("fa_lse_combine", _i32, [_vp, _vp, _i32, _i64, _i32, _vp, _i32, _vp, _vp]),
@@ -94,6 +95,7 @@ SIGNATURES = [
                                      ctypes.POINTER(ctypes.c_size_t),
                                      ctypes.POINTER(ctypes.c_size_t)]),
     ("fa_mla_get_metadata", _i32, [_vp, _i32, _i32, _i32, _vp, _vp, _vp]),
+    ("fa_schedule_entries", _i32, [_vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
     ("fa_mla_decode", _i32, [ctypes.POINTER(MlaArgs), _vp]),
     ("fa_mla_decode_partial", _i32, [ctypes.POINTER(MlaArgs), _vp]),
     ("fa_mla_combine", _i32, [ctypes.POINTER(MlaArgs), _vp]),

@@ -23,6 +23,14 @@ cudaError_t launch_mla_combine(const float *, const float *, const int32_t *, in
                                bool, void *, int, int64_t, int64_t, int64_t, float *, cudaStream_t);
 cudaError_t launch_generic_decode(const fa_decode_args *, cudaStream_t);
 size_t generic_smem_bytes(int, int);
+void launch_entry_metadata(const int32_t *, int, int, int, int, int, int, int32_t *, int32_t *,
+                           cudaStream_t);
+bool gqa_tc_eligible(const fa_decode_args *);
+cudaError_t launch_gqa_tc(const CUtensorMap &, const CUtensorMap &, const fa_decode_args *,
+                          const int32_t *, const int32_t *, int, int, bool, cudaStream_t);
+cudaError_t launch_gqa_combine(const float *, const float *, const int32_t *, int, int, int, int,
+                               int, int, int, int, bool, void *, int, int64_t, int64_t, int64_t,
+                               float *, cudaStream_t);
 cudaError_t launch_mla_sv(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                           const CUtensorMap &, const fa_mla_args *, int, cudaStream_t);
 }  // namespace fa
@@ -95,6 +103,36 @@ int encode_map(CUtensorMap *map, const void *base, int dtype, uint64_t d, uint64
   return FA_OK;
 }
 
+// 4-D map {d, rows, heads, groups} with a {64, box_rows, 1, 1} box and the
+// 128-byte swizzle: a grouped-query cache, paged ([pages][kv heads][page][d]
+// or any strides) or contiguous ([batch][kv heads][n][d] or any strides).
+int encode_map4(CUtensorMap *map, const void *base, int dtype, uint64_t d, uint64_t rows,
+                uint64_t heads, uint64_t groups, int64_t row_stride, int64_t head_stride,
+                int64_t group_stride, uint32_t box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[4] = {d, rows, heads, groups};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(row_stride) * 2,
+                           static_cast<cuuint64_t>(head_stride) * 2,
+                           static_cast<cuuint64_t>(group_stride) * 2};
+  cuuint32_t box[4] = {64, box_rows, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dtype == FA_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   4, const_cast<void *>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FA_ERR_INVALID_ARGUMENT,
+                "tensor map rejected (code %d): dims {%llu,%llu,%llu,%llu} strides "
+                "{%llu,%llu,%llu} B",
+                static_cast<int>(r), (unsigned long long)d, (unsigned long long)rows,
+                (unsigned long long)heads, (unsigned long long)groups,
+                (unsigned long long)strides[0], (unsigned long long)strides[1],
+                (unsigned long long)strides[2]);
+  return FA_OK;
+}
+
 // 2-D map over every row of a paged latent pool ({576, rows}, one row per
 // box, 128-byte swizzle) for tile::gather4 loads of index-listed rows.
 int encode_gather_map(CUtensorMap *map, const void *base, int dtype, uint64_t rows,
@@ -117,6 +155,43 @@ int encode_gather_map(CUtensorMap *map, const void *base, int dtype, uint64_t ro
   return FA_OK;
 }
 
+constexpr int kGqaBlockN = 128;   // tokens per scheduled block (one tile)
+constexpr int kGqaFixedCost = 1;  // per-piece overhead, in blocks
+
+// K and V tensor maps of the grouped-query kernel: boxes of 64 dims x one
+// page (at most 128 rows) over {d, page rows, kv heads, pages}, or 128 rows
+// over {d, n, kv heads, batch} for contiguous caches.
+int encode_kv_maps(const fa_decode_args *a, CUtensorMap *km, CUtensorMap *vm) {
+  const bool paged = a->block_table != nullptr;
+  const uint32_t box_rows =
+      paged ? static_cast<uint32_t>(a->page_size < kGqaBlockN ? a->page_size : kGqaBlockN)
+            : kGqaBlockN;
+  const uint64_t rows = paged ? a->page_size : static_cast<uint64_t>(a->n_ctx > 0 ? a->n_ctx : 1);
+  const uint64_t groups = paged ? a->num_pages : a->batch;
+  int st = encode_map4(km, a->k, a->dtype, a->d_qk, rows, a->num_kv_heads, groups,
+                       a->k_stride_tok, a->k_stride_head, a->k_stride_seq, box_rows);
+  if (st != FA_OK) return st;
+  return encode_map4(vm, a->v, a->dtype, a->d_v, rows, a->num_kv_heads, groups, a->k_stride_tok,
+                     a->k_stride_head, a->k_stride_seq, box_rows);
+}
+
+// Tensor-core kernel for these arguments?  Shapes, types and alignment
+// (gqa_tc_eligible), a batch the maps can describe, and strides the TMA unit
+// accepts (the encoder is asked; it runs on the host only).
+bool decode_on_tensor_cores(const fa_decode_args *a) {
+  if (a->block_table == nullptr && a->seq_lens == nullptr && a->n_ctx < 1) return false;
+  if (a->batch < 1 || !fa::gqa_tc_eligible(a)) return false;
+  CUtensorMap km, vm;
+  return encode_kv_maps(a, &km, &vm) == FA_OK;
+}
+
+int current_sm_count(int *sms) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  return fa_device_sm_count(dev, sms);
+}
+
 int validate_decode(const fa_decode_args *a) {
   if (!a) return fail(FA_ERR_INVALID_ARGUMENT, "null args");
   if (!a->q || !a->k || !a->v || !a->o) return fail(FA_ERR_INVALID_ARGUMENT, "null tensor");
@@ -133,16 +208,70 @@ int validate_decode(const fa_decode_args *a) {
   if (a->block_table) {
     if (a->page_size <= 0) return fail(FA_ERR_INVALID_ARGUMENT, "page_size %d", a->page_size);
     if (!a->seq_lens) return fail(FA_ERR_INVALID_ARGUMENT, "paged mode needs seq_lens");
+    if (a->num_pages < 0) return fail(FA_ERR_INVALID_ARGUMENT, "num_pages %d", a->num_pages);
   } else if (!a->seq_lens && a->n_ctx < 0) {
     return fail(FA_ERR_INVALID_ARGUMENT, "n_ctx %d", a->n_ctx);
   }
-  if (a->num_splits < 1) return fail(FA_ERR_INVALID_ARGUMENT, "num_splits %d", a->num_splits);
-  if (a->num_splits > 1 && (!a->part_o || !a->part_lse || !aligned16(a->part_o)))
-    return fail(FA_ERR_INVALID_ARGUMENT, "num_splits > 1 needs 16-byte aligned f32 workspace");
+  const bool tc = decode_on_tensor_cores(a);
+  if (a->num_splits < 0 || (a->num_splits == 0 && !tc))
+    return fail(FA_ERR_INVALID_ARGUMENT,
+                "num_splits %d (0 selects the balanced schedule of the tensor-core kernel)",
+                a->num_splits);
+  if (a->num_splits == 0 && !a->sched)
+    return fail(FA_ERR_INVALID_ARGUMENT, "the balanced schedule needs the sched scratch");
+  if (a->num_splits != 1 && (!a->part_o || !a->part_lse || !aligned16(a->part_o)))
+    return fail(FA_ERR_INVALID_ARGUMENT, "split decode needs 16-byte aligned f32 workspace");
   if (a->num_splits > 1 && a->partition_size <= 0)
     return fail(FA_ERR_INVALID_ARGUMENT, "num_splits > 1 needs partition_size > 0");
-  if (fa::generic_smem_bytes(a->d_qk, a->d_v) > 227 * 1024)
+  if (!tc && fa::generic_smem_bytes(a->d_qk, a->d_v) > 227 * 1024)
     return fail(FA_ERR_UNSUPPORTED, "head size too large for the generic kernel");
+  return FA_OK;
+}
+
+// The tensor-core path: K / V tensor maps, then (balanced schedule) the
+// scheduler kernel, the decode as its programmatic dependent and the merge
+// of split entries as the decode's.
+int run_decode_tc(const fa_decode_args *a, cudaStream_t s) {
+  int sms = 0;
+  int st = current_sm_count(&sms);
+  if (st != FA_OK) return st;
+  CUtensorMap km, vm;
+  st = encode_kv_maps(a, &km, &vm);
+  if (st != FA_OK) return st;
+  const int entries = a->batch * a->num_kv_heads;
+  const int group = a->num_q_heads / a->num_kv_heads;
+  const int qrows = group * a->m_q;
+  cudaError_t e;
+  if (a->num_splits == 0) {
+    const int parts = sms;
+    int32_t *meta = a->sched;
+    int32_t *prefix = a->sched + static_cast<int64_t>(parts) * FA_MLA_META_INTS;
+    fa::launch_entry_metadata(a->seq_lens, a->seq_lens ? 0 : a->n_ctx, entries, a->num_kv_heads,
+                              kGqaBlockN, kGqaFixedCost, parts, meta, prefix, s);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "scheduler launch");
+    e = fa::launch_gqa_tc(km, vm, a, meta, prefix, parts, parts, true, s);
+    if (e != cudaSuccess) return cuda_fail(e, "tensor-core decode launch");
+    e = fa::launch_gqa_combine(a->part_o, a->part_lse, prefix, 0, entries, qrows, a->m_q, group,
+                               a->num_kv_heads, a->num_q_heads, a->d_v,
+                               static_cast<int64_t>(entries) * 4 <= parts, a->o, a->dtype,
+                               a->o_stride_b, a->o_stride_h, a->o_stride_m, a->lse, s);
+    if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+    return FA_OK;
+  }
+  const int ns = a->num_splits;
+  const int64_t parts = static_cast<int64_t>(entries) * ns;
+  if (parts > INT32_MAX) return fail(FA_ERR_UNSUPPORTED, "too many partitions");
+  const int grid = static_cast<int>(parts < sms ? parts : sms);
+  e = fa::launch_gqa_tc(km, vm, a, nullptr, nullptr, static_cast<int>(parts), grid, false, s);
+  if (e != cudaSuccess) return cuda_fail(e, "tensor-core decode launch");
+  if (ns > 1) {
+    e = fa::launch_gqa_combine(a->part_o, a->part_lse, nullptr, ns, entries, qrows, a->m_q, group,
+                               a->num_kv_heads, a->num_q_heads, a->d_v,
+                               ns >= 8 && static_cast<int64_t>(entries) * 4 <= sms, a->o,
+                               a->dtype, a->o_stride_b, a->o_stride_h, a->o_stride_m, a->lse, s);
+    if (e != cudaSuccess) return cuda_fail(e, "merge launch");
+  }
   return FA_OK;
 }
 
@@ -151,6 +280,7 @@ int run_decode(const fa_decode_args *a, void *stream) {
   if (st != FA_OK) return st;
   if (a->batch == 0) return FA_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (decode_on_tensor_cores(a)) return run_decode_tc(a, s);
   cudaError_t e = fa::launch_generic_decode(a, s);
   if (e != cudaSuccess) return cuda_fail(e, "generic decode launch");
   if (a->num_splits > 1) {
@@ -212,7 +342,7 @@ int record_error(int status, const char *msg) { return fail(status, "%s", msg); 
 
 extern "C" {
 
-int fa_version(void) { return (0 << 16) | (2 << 8) | 0; }
+int fa_version(void) { return (0 << 16) | (3 << 8) | 0; }
 
 const char *fa_status_string(int status) {
   switch (status) {
@@ -293,13 +423,43 @@ int fa_split_kv_num_splits(int batch, int heads, int m, int n, int block_m, int 
   return FA_OK;
 }
 
+int fa_decode_uses_tensor_cores(const fa_decode_args *a) {
+  if (!a) return fail(FA_ERR_INVALID_ARGUMENT, "null args");
+  return decode_on_tensor_cores(a) ? 1 : 0;
+}
+
 int fa_decode_workspace_size(const fa_decode_args *a, size_t *part_o_bytes,
-                             size_t *part_lse_bytes) {
-  if (!a || !part_o_bytes || !part_lse_bytes) return fail(FA_ERR_INVALID_ARGUMENT, "null");
-  const size_t rows = static_cast<size_t>(a->batch) * a->num_q_heads * a->m_q;
-  const size_t s = a->num_splits > 1 ? static_cast<size_t>(a->num_splits) : 0;
-  *part_o_bytes = s * rows * a->d_v * sizeof(float);
-  *part_lse_bytes = s * rows * sizeof(float);
+                             size_t *part_lse_bytes, size_t *sched_bytes) {
+  if (!a || !part_o_bytes || !part_lse_bytes || !sched_bytes)
+    return fail(FA_ERR_INVALID_ARGUMENT, "null");
+  if (a->batch < 0 || a->num_q_heads <= 0 || a->num_kv_heads <= 0 || a->m_q <= 0 ||
+      a->d_v <= 0 || a->num_splits < 0)
+    return fail(FA_ERR_INVALID_ARGUMENT, "bad arguments");
+  size_t slots = 0, sched = 0;
+  if (a->num_splits == 0) {
+    if (!decode_on_tensor_cores(a))
+      return fail(FA_ERR_INVALID_ARGUMENT, "num_splits 0 needs the tensor-core kernel");
+    int sms = 0;
+    int st = current_sm_count(&sms);
+    if (st != FA_OK) return st;
+    const size_t entries = static_cast<size_t>(a->batch) * a->num_kv_heads;
+    // at most one extra piece per part beyond one per entry
+    slots = entries + sms;
+    sched = (static_cast<size_t>(sms) * FA_MLA_META_INTS + entries + 1) * sizeof(int32_t);
+  } else if (a->num_splits > 1) {
+    slots = static_cast<size_t>(a->batch) * a->num_kv_heads * a->num_splits;
+  }
+  // slot = the rows of one kv head's group (tensor-core layout) or, for the
+  // CUDA-core layout [split][batch][heads][m_q], the same total
+  const size_t rows = static_cast<size_t>(a->num_q_heads / a->num_kv_heads) * a->m_q;
+  size_t cells = 0, o_bytes = 0, lse_bytes = 0;
+  if (__builtin_mul_overflow(slots, rows, &cells) ||
+      __builtin_mul_overflow(cells, static_cast<size_t>(a->d_v) * sizeof(float), &o_bytes) ||
+      __builtin_mul_overflow(cells, sizeof(float), &lse_bytes))
+    return fail(FA_ERR_INVALID_ARGUMENT, "workspace size overflows size_t");
+  *part_o_bytes = o_bytes;
+  *part_lse_bytes = lse_bytes;
+  *sched_bytes = sched;
   return FA_OK;
 }
 
@@ -373,6 +533,18 @@ int fa_mla_get_metadata(const int32_t *seq_lens, int batch, int topk, int num_sm
                           static_cast<cudaStream_t>(stream));
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? FA_OK : cuda_fail(e, "metadata launch");
+}
+
+int fa_schedule_entries(const int32_t *seq_lens, int uniform_len, int entries, int rep,
+                        int block_n, int fixed_cost, int num_parts, int32_t *meta,
+                        int32_t *prefix, void *stream) {
+  if (entries < 0 || rep < 1 || block_n < 1 || fixed_cost < 0 || num_parts < 1 || !meta ||
+      !prefix || (!seq_lens && uniform_len < 1 && entries))
+    return fail(FA_ERR_INVALID_ARGUMENT, "bad scheduler arguments");
+  fa::launch_entry_metadata(seq_lens, seq_lens ? 0 : uniform_len, entries, rep, block_n,
+                            fixed_cost, num_parts, meta, prefix, static_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? FA_OK : cuda_fail(e, "scheduler launch");
 }
 
 int fa_mla_combine(const fa_mla_args *a, void *stream) {

@@ -60,6 +60,74 @@ __global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
   if (lane == 0) lse[(static_cast<int64_t>(b) * h_q + h) * s_q + s] = l;
 }
 
+// Grouped-query entries (entry e = sequence * kv_heads + kv head, rows r =
+// head-in-group * m_q + query token): entry e owns split slots prefix[e] ..
+// prefix[e+1]-1 (balanced schedule) or e * splits .. + splits - 1 (fixed
+// partitions, prefix == nullptr) of part_o [slot][rows][d_v].  Launched as a
+// programmatic dependent of the decode; the slot table itself comes from the
+// scheduler kernel before the decode, so it is read after the wait too.
+template <typename T, bool kWide>
+__global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
+    gqa_combine_kernel(const float *__restrict__ part_o, const float *__restrict__ part_lse,
+                       const int32_t *__restrict__ prefix, int splits, int rows, int m_q,
+                       int group, int hkv, int hq, int d_v, T *__restrict__ out, int64_t o_sb,
+                       int64_t o_sh, int64_t o_sm, float *__restrict__ lse) {
+  __shared__ MergeState states[kWide ? 8 : 1][32];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int row_blocks = kWide ? (rows + 1) / 2 : (rows + 3) / 4;
+  const int e = blockIdx.x / row_blocks, rb = blockIdx.x % row_blocks;
+  const int first = prefix ? prefix[e] : e * splits;
+  const int n = prefix ? prefix[e + 1] - first : splits;
+  if (n < 2) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int flat = kWide ? rb * 2 + (warp >> 2) : rb * 4 + warp;
+  const int j = kWide ? (warp & 3) : 0;
+  MergeState st;
+  mla_row_state<kWide>(st, part_o, part_lse, first, n, rows, flat, d_v, lane, j, warp, states);
+  if (j != 0 || flat >= rows) return;
+  const int b = e / hkv, h = (e % hkv) * group + flat / m_q, m = flat % m_q;
+  const float l = finish_row<T>(st, d_v, out + b * o_sb + h * o_sh + m * o_sm, lane);
+  if (lse != nullptr && lane == 0) lse[(static_cast<int64_t>(b) * hq + h) * m_q + m] = l;
+}
+
+template <typename T>
+cudaError_t launch_gqa_combine_t(const float *part_o, const float *part_lse,
+                                 const int32_t *prefix, int splits, int entries, int rows,
+                                 int m_q, int group, int hkv, int hq, int d_v, bool wide,
+                                 void *out, int64_t o_sb, int64_t o_sh, int64_t o_sm, float *lse,
+                                 cudaStream_t stream) {
+  if (entries == 0) return cudaSuccess;
+  cudaLaunchConfig_t cfg = {};
+  const int64_t blocks = static_cast<int64_t>(wide ? (rows + 1) / 2 : (rows + 3) / 4) * entries;
+  if (blocks > INT32_MAX) return cudaErrorInvalidConfiguration;
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(wide ? 256 : 128);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  T *o = static_cast<T *>(out);
+  if (wide)
+    return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<T, true>, part_o, part_lse, prefix, splits,
+                              rows, m_q, group, hkv, hq, d_v, o, o_sb, o_sh, o_sm, lse);
+  return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<T, false>, part_o, part_lse, prefix, splits,
+                            rows, m_q, group, hkv, hq, d_v, o, o_sb, o_sh, o_sm, lse);
+}
+
+cudaError_t launch_gqa_combine(const float *part_o, const float *part_lse, const int32_t *prefix,
+                               int splits, int entries, int rows, int m_q, int group, int hkv,
+                               int hq, int d_v, bool wide, void *out, int dtype, int64_t o_sb,
+                               int64_t o_sh, int64_t o_sm, float *lse, cudaStream_t stream) {
+  if (dtype == FA_DTYPE_BF16)
+    return launch_gqa_combine_t<__nv_bfloat16>(part_o, part_lse, prefix, splits, entries, rows,
+                                               m_q, group, hkv, hq, d_v, wide, out, o_sb, o_sh,
+                                               o_sm, lse, stream);
+  return launch_gqa_combine_t<__half>(part_o, part_lse, prefix, splits, entries, rows, m_q, group,
+                                      hkv, hq, d_v, wide, out, o_sb, o_sh, o_sm, lse, stream);
+}
+
 template <typename T>
 void launch_lse_combine_t(const float *part_o, const float *part_lse, int num_parts,
                           int64_t o_part_stride, int64_t lse_part_stride, int64_t rows, int H,

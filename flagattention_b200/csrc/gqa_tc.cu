@@ -1,0 +1,844 @@
+// gqa_tc.cu -- grouped-query decode on tcgen05, paged or contiguous caches.
+//
+// The reference's decode kernels (paged.py:208-363 for paged caches,
+// split_kv.py:28-174 for contiguous keys) compute, for each (sequence, kv
+// head), S = Q K^T over the query rows of the head's group (tl.dot at
+// paged.py:314), an online softmax, and O += P V (paged.py:333).  Here that
+// work runs on the fifth-generation tensor cores:
+//
+//   * one persistent CTA per SM walks "pieces": a token range of one entry
+//     (entry = sequence * kv_heads + kv head); with the balanced schedule a
+//     CTA owns one part of the device scheduler's metadata (sched.cu), with
+//     an explicit split count it takes the reference's fixed partitions
+//     round-robin;
+//   * K and V tiles of 128 tokens arrive by TMA, one box per page (64 dims x
+//     min(page, 128) rows, 128-byte swizzle), each into its own ring; boxes
+//     outside the piece or past the sequence end are requested at an
+//     out-of-range page coordinate, which the TMA unit fills with zeros
+//     without touching HBM;
+//   * Q and P live in TMEM and are the A operand of tcgen05.mma (M = 128):
+//     only the group's rows carry data, so the padding costs tensor-pipe
+//     time, of which a decode has plenty, and no shared memory;
+//   * S (two 128-column buffers, P written over S in place) and O (D
+//     columns) accumulate in TMEM.
+//
+// Row warps (0-3) own the query rows.  With R = group * m_q rows, each query
+// row is held by kC = 4 / ceil(R / 32) warps ("copies", kC in {1, 2, 4}):
+// copy c takes tile columns [c * 128 / kC, (c + 1) * 128 / kC) and keeps its
+// own running maximum, row sum and O row (its P row is zero outside its
+// columns), so four warps share the softmax of a small group and the
+// exponentials run on all four SM sub-partitions.  The copies are merged
+// once per piece in shared memory (the reference's split merge algebra,
+// split_kv.py:198-228).  Warp 4 is the TMA producer, warp 5 issues the MMAs.
+//
+// Every mbarrier wait is bounded (common.cuh); a timeout sets the device
+// status word and the kernel unwinds instead of hanging.
+#include "common.cuh"
+#include "flagattn_b200.h"
+
+namespace fa {
+namespace gqa {
+
+constexpr int kTileN = 128;                  // tokens per tile: QK N, PV K
+constexpr int kThreads = 192;                // warps 0-3 rows, 4 producer, 5 MMA
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kChunkBytes = kTileN * 128;    // 128 token rows x 64 dims
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;    // log2 units (factor 256)
+constexpr int kMaxStages = 6;
+
+template <int kD>
+struct Plan {
+  static constexpr int kChunks = kD / 64;
+  static constexpr int kTileBytes = kChunks * kChunkBytes;     // 16 or 32 KB
+  static constexpr int kStages = kD == 64 ? 6 : 3;             // per ring
+  static constexpr int kOffK = 1024;
+  static constexpr int kOffV = kOffK + kStages * kTileBytes;
+  static constexpr int kOffStage = kOffV + kStages * kTileBytes;  // copy merge: [warp][lane][33] f32
+  static constexpr int kStageBytes = 4 * 32 * 33 * 4;
+  static constexpr int kOffStats = kOffStage + kStageBytes;      // [2][warp][lane] f32
+  static constexpr int kSmemUsed = kOffStats + 2 * 4 * 32 * 4;
+  static constexpr int kSmemBytes = kSmemUsed + 1024;            // base alignment slack
+  // TMEM columns: O, two S / P buffers, two Q buffers (bf16 / f16 pairs)
+  static constexpr uint32_t kColO = 0;
+  static constexpr uint32_t kColS = kD;
+  static constexpr uint32_t kColQ = kD + 2 * kTileN;
+  static_assert(kColQ + kD <= kTmemCols, "TMEM plan");
+  static_assert(kStages <= kMaxStages, "ring");
+  static_assert(kSmemBytes <= 232448, "shared memory plan exceeds 227 KB");
+  static_assert(kOffK % 1024 == 0 && kOffV % 1024 == 0 && kTileBytes % 1024 == 0,
+                "swizzled tiles need 1024-byte alignment");
+};
+
+struct Bars {
+  uint64_t k_full[kMaxStages], k_empty[kMaxStages];
+  uint64_t v_full[kMaxStages], v_empty[kMaxStages];
+  uint64_t s_full[2];   // QK of a tile landed in S buffer (tile & 1)
+  uint64_t p_full[2];   // the row warps wrote P over that buffer (and rescaled O)
+  uint64_t q_full[2];   // the row warps wrote a piece's Q into TMEM buffer (piece & 1)
+  uint64_t pv_done;     // one phase per tile, in tile order
+  uint64_t merge;       // the row warps' meeting point when copies merge (4 arrivals)
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Bars) <= 1024, "barrier block");
+
+struct Params {
+  const void *q;
+  int64_t q_sb, q_sh, q_sm;
+  const int32_t *block_table;  // nullptr: contiguous [batch][n][kv heads] via strides
+  int64_t bt_stride;
+  int32_t page_size, num_pages, box_rows;
+  const int32_t *seq_lens;     // nullptr: every sequence has n_ctx tokens
+  int32_t n_ctx;
+  int32_t batch, hq, hkv, group, m_q, rows, causal;
+  float scale_log2;
+  // balanced schedule (meta != nullptr): parts of the device scheduler's
+  // metadata in 128-token blocks; prefix[e] .. prefix[e + 1] - 1 are entry
+  // e's split slots.  Otherwise the reference's fixed partition: part =
+  // entry * num_splits + split, partition_size tokens each.
+  const int32_t *meta;
+  const int32_t *prefix;
+  int32_t num_parts;
+  int32_t num_splits, partition_size;
+  void *o;
+  int64_t o_sb, o_sh, o_sm;
+  float *lse;       // nullable, [batch][hq][m_q]
+  float *part_o;    // [slot][rows][d]
+  float *part_lse;  // [slot][rows]
+  int *status;
+};
+
+struct Piece {
+  int e, b, kvh, tok0, tok_end, len, slot;
+  bool final_out;
+  __device__ __forceinline__ int tiles() const {
+    return tok_end > tok0 ? (tok_end - (tok0 & ~(kTileN - 1)) + kTileN - 1) / kTileN : 0;
+  }
+};
+
+__device__ __forceinline__ int entry_len(const Params &p, int e) {
+  return p.seq_lens ? __ldg(p.seq_lens + e / p.hkv) : p.n_ctx;
+}
+
+__device__ __forceinline__ int part_pieces(const Params &p, int part) {
+  return p.meta ? __ldg(p.meta + static_cast<int64_t>(part) * FA_MLA_META_INTS + 5) : 1;
+}
+
+// Position in the CTA's stream of pieces: part (blockIdx.x, + gridDim.x, ...)
+// and piece index i within it.
+struct Cursor {
+  int part, i;
+  __device__ __forceinline__ bool valid(const Params &p) const { return part < p.num_parts; }
+};
+
+__device__ __forceinline__ void settle(const Params &p, Cursor &c) {
+  while (c.part < p.num_parts && c.i >= part_pieces(p, c.part)) {
+    c.part += gridDim.x;
+    c.i = 0;
+  }
+}
+__device__ __forceinline__ Cursor first_cursor(const Params &p) {
+  Cursor c{static_cast<int>(blockIdx.x), 0};
+  settle(p, c);
+  return c;
+}
+__device__ __forceinline__ void advance(const Params &p, Cursor &c) {
+  ++c.i;
+  settle(p, c);
+}
+
+__device__ __noinline__ Piece get_piece(const Params &p, Cursor c) {
+  Piece pc;
+  int split;
+  if (p.meta) {
+    const int32_t *m = p.meta + static_cast<int64_t>(c.part) * FA_MLA_META_INTS;
+    pc.e = __ldg(m) + c.i;
+    pc.len = max(entry_len(p, pc.e), 0);
+    const int nblk = (pc.len + kTileN - 1) / kTileN;
+    const int lo = c.i == 0 ? __ldg(m + 1) : 0;
+    const int hi = pc.e == __ldg(m + 2) ? __ldg(m + 3) : nblk;
+    pc.tok0 = lo * kTileN;
+    pc.tok_end = min(hi * kTileN, pc.len);
+    split = c.i == 0 ? __ldg(m + 4) : 0;
+    const int first = __ldg(p.prefix + pc.e);
+    pc.final_out = __ldg(p.prefix + pc.e + 1) - first == 1;
+    pc.slot = first + split;
+  } else {
+    pc.e = c.part / p.num_splits;
+    split = c.part % p.num_splits;
+    pc.len = max(entry_len(p, pc.e), 0);
+    if (p.num_splits == 1) {
+      pc.tok0 = 0;
+      pc.tok_end = pc.len;
+    } else {
+      pc.tok0 = split * p.partition_size;
+      pc.tok_end = min(pc.len, pc.tok0 + p.partition_size);
+    }
+    pc.final_out = p.num_splits == 1;
+    pc.slot = c.part;
+  }
+  pc.b = pc.e / p.hkv;
+  pc.kvh = pc.e % p.hkv;
+  return pc;
+}
+
+// Next piece with at least one tile (the Q buffers alternate over those).
+__device__ __forceinline__ void next_with_tiles(const Params &p, Cursor &c) {
+  while (c.valid(p) && get_piece(p, c).tiles() == 0) advance(p, c);
+}
+
+// Warp-wide bounded wait: all lanes return the same verdict.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                          int *status, int code) {
+  if (mbar_probe(bar, parity)) return true;
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, status, code)) != 0;
+}
+
+// ------------------------------------------------------------------ rows
+// Query row r of an entry: head kvh * group + r / m_q, query token r % m_q.
+template <typename T, int kD>
+__device__ __forceinline__ void write_q(const Params &p, const Piece &pc, bool live, int g_idx,
+                                        int m_idx, uint32_t t_q, uint32_t bar, int lane) {
+  uint32_t w[kD / 2];
+  if (live) {
+    const int h = pc.kvh * p.group + g_idx;
+    const uint4 *src = reinterpret_cast<const uint4 *>(
+        static_cast<const T *>(p.q) + pc.b * p.q_sb + h * p.q_sh + m_idx * p.q_sm);
+#pragma unroll
+    for (int i = 0; i < kD / 8; ++i) {
+      const uint4 v = __ldg(src + i);
+      w[4 * i] = v.x;
+      w[4 * i + 1] = v.y;
+      w[4 * i + 2] = v.z;
+      w[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kD / 2; ++i) w[i] = 0u;
+  }
+#pragma unroll
+  for (int j = 0; j < kD / 64; ++j) tmem_st32(t_q + 32 * j, w + 32 * j);
+  tmem_wait_st();
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
+
+// Barrier of the four row warps on an mbarrier (bounded, unlike bar.sync:
+// a warp that unwound after a timeout cannot leave the others stuck).
+struct RowSync {
+  uint32_t bar, phase = 0;
+  __device__ __forceinline__ bool sync(volatile int *abort_flag, int *status) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+    const bool ok = warp_wait(bar, phase & 1u, abort_flag, status, kDevTimeoutSoftmax);
+    ++phase;
+    return ok;
+  }
+};
+
+// Normalised rows of one piece into the output (final) or a split slot.
+// kC == 1: each lane writes its own row.  kC > 1: the copies of a row meet in
+// shared memory, 32 columns at a time; thread (warp w, lane j) then writes
+// column j of rows w, w + 4, ...
+template <typename T, int kD, int kC>
+__device__ __forceinline__ bool epilogue(const Params &p, const Piece &pc, bool has_tiles,
+                                         bool live, int r, int g_idx, int m_idx, int warp,
+                                         int lane, int quads, float m_use, float l,
+                                         uint32_t t_o, float *stage, float *stat_m,
+                                         float *stat_l, RowSync &rs, volatile int *abort_flag) {
+  constexpr float kLn2 = 0.6931471805599453f;
+  float f, lse;
+  if (kC == 1) {
+    f = l > 0.f ? 1.f / l : 0.f;
+    lse = l > 0.f ? (m_use + __log2f(l)) * kLn2 : -INFINITY;
+  } else {
+    stat_m[warp * 32 + lane] = live ? m_use : -INFINITY;
+    stat_l[warp * 32 + lane] = live ? l : 0.f;
+    if (!rs.sync(abort_flag, p.status)) return false;
+    const int q = warp % quads;
+    float M = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kC; ++c) M = fmaxf(M, stat_m[(c * quads + q) * 32 + lane]);
+    float L = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int c = 0; c < kC; ++c) {
+        const float mc = stat_m[(c * quads + q) * 32 + lane];
+        L += mc == -INFINITY ? 0.f : stat_l[(c * quads + q) * 32 + lane] * fast_exp2(mc - M);
+      }
+    }
+    f = (L > 0.f && m_use != -INFINITY) ? fast_exp2(m_use - M) / L : 0.f;
+    lse = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
+  }
+  const int h = pc.kvh * p.group + g_idx;
+  T *orow = static_cast<T *>(p.o) + pc.b * p.o_sb + h * p.o_sh + m_idx * p.o_sm;
+  float *prow = p.part_o + (static_cast<int64_t>(pc.slot) * p.rows + r) * kD;
+#pragma unroll 1
+  for (int j = 0; j < kD / 32; ++j) {
+    float v[32];
+    if (has_tiles) {
+      tmem_ld32(t_o + 32 * j, v);
+      tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] *= f;
+    if (kC == 1) {
+      if (live) {
+        if (pc.final_out) {
+          uint4 *dst = reinterpret_cast<uint4 *>(orow + 32 * j);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 u;
+            u.x = Elem<T>::pack2(v[8 * i], v[8 * i + 1]);
+            u.y = Elem<T>::pack2(v[8 * i + 2], v[8 * i + 3]);
+            u.z = Elem<T>::pack2(v[8 * i + 4], v[8 * i + 5]);
+            u.w = Elem<T>::pack2(v[8 * i + 6], v[8 * i + 7]);
+            dst[i] = u;
+          }
+        } else {
+          float4 *dst = reinterpret_cast<float4 *>(prow + 32 * j);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+      }
+    } else {
+      float *mine = stage + (warp * 32 + lane) * 33;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) mine[i] = v[i];
+      if (!rs.sync(abort_flag, p.status)) return false;
+      for (int rr = warp; rr < p.rows; rr += 4) {
+        const int q = rr >> 5, i = rr & 31;
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < kC; ++c) sum += stage[((c * quads + q) * 32 + i) * 33 + lane];
+        const int g2 = rr / p.m_q, m2 = rr % p.m_q;
+        if (pc.final_out) {
+          T *o2 = static_cast<T *>(p.o) + pc.b * p.o_sb + (pc.kvh * p.group + g2) * p.o_sh +
+                  m2 * p.o_sm;
+          o2[32 * j + lane] = Elem<T>::from_f(sum);
+        } else {
+          p.part_o[(static_cast<int64_t>(pc.slot) * p.rows + rr) * kD + 32 * j + lane] = sum;
+        }
+      }
+      if (!rs.sync(abort_flag, p.status)) return false;
+    }
+  }
+  const bool writer = live && (kC == 1 || warp < quads);
+  if (writer) {
+    if (pc.final_out) {
+      if (p.lse) p.lse[(static_cast<int64_t>(pc.b) * p.hq + h) * p.m_q + m_idx] = lse;
+    } else {
+      p.part_lse[static_cast<int64_t>(pc.slot) * p.rows + r] = lse;
+    }
+  }
+  tc_fence_before();  // the O reads above precede the next piece's first PV
+  return true;
+}
+
+template <typename T, int kD, int kC>
+__device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *smem,
+                                         uint32_t tmem, int warp, int lane) {
+  using PL = Plan<kD>;
+  constexpr int kCols = kTileN / kC;   // tile columns of one copy
+  constexpr int kWords = kCols / 2;    // packed P words of one copy
+  volatile int *abort_flag = &bars->abort_flag;
+  const int quads = kC == 1 ? (p.rows + 31) / 32 : 4 / kC;
+  if (warp >= quads * kC) return;      // kC == 1 with three quadrants: warp 3 idles
+  const int copy = warp / quads;
+  const int r = (warp % quads) * 32 + lane;
+  const bool live = r < p.rows;
+  const int g_idx = live ? r / p.m_q : 0;
+  const int m_idx = live ? r % p.m_q : 0;
+  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t t_o = tmem + lane_off + PL::kColO;
+  float *stage = reinterpret_cast<float *>(smem + PL::kOffStage);
+  float *stat_m = reinterpret_cast<float *>(smem + PL::kOffStats);
+  float *stat_l = stat_m + 128;
+  const uint32_t vbase = smem_u32(smem + PL::kOffV);
+  RowSync rs{smem_u32(&bars->merge)};
+
+  Cursor cur = first_cursor(p);
+  next_with_tiles(p, cur);  // first piece that has tiles: its Q goes first
+  uint32_t g = 0;           // tiles so far
+  uint32_t k = 0;           // pieces with tiles so far
+  if (cur.valid(p))
+    write_q<T, kD>(p, get_piece(p, cur), live, g_idx, m_idx, tmem + lane_off + PL::kColQ,
+                   smem_u32(&bars->q_full[0]), lane);
+  bool ok = true;
+  for (Cursor c = first_cursor(p); c.valid(p) && ok; advance(p, c)) {
+    const Piece pc = get_piece(p, c);
+    const int n_tiles = pc.tiles();
+    if (n_tiles > 0) {
+      // Q of the next piece with tiles, into the other buffer: its previous
+      // user (two pieces back) finished all QKs before this piece started
+      Cursor nq = c;
+      advance(p, nq);
+      next_with_tiles(p, nq);
+      if (nq.valid(p))
+        write_q<T, kD>(p, get_piece(p, nq), live, g_idx, m_idx,
+                       tmem + lane_off + PL::kColQ + ((k + 1) & 1) * (kD / 2),
+                       smem_u32(&bars->q_full[(k + 1) & 1]), lane);
+    }
+    // valid tokens of this row: [tok0, hi_tok); causal rows stop at
+    // m + len - m_q (bottom-right alignment, split_kv.py:88-92)
+    const int row_end = p.causal ? min(pc.tok_end, m_idx + pc.len - p.m_q + 1) : pc.tok_end;
+    float m_use = -INFINITY, l = 0.f;
+    int n0 = pc.tok0 & ~(kTileN - 1);
+    for (int t = 0; t < n_tiles; ++t, ++g, n0 += kTileN) {
+      const uint32_t buf = g & 1u;
+      if (!(ok = warp_wait(smem_u32(&bars->s_full[buf]), (g >> 1) & 1u, abort_flag, p.status,
+                           kDevTimeoutSoftmax)))
+        break;
+      tc_fence_after();
+      const uint32_t t_s = tmem + lane_off + PL::kColS + buf * kTileN;
+      float s[kCols];
+#pragma unroll
+      for (int j = 0; j < kCols / 32; ++j) tmem_ld32(t_s + copy * kCols + 32 * j, s + 32 * j);
+      tmem_wait_ld();
+      // rows past the group (zero Q, so S = 0) count as fully valid: their
+      // P and O rows are never read
+      const int c0 = n0 + copy * kCols;
+      const int lo = live ? pc.tok0 - c0 : 0;
+      const int hi = live ? row_end - c0 : kCols;
+      float mx = -INFINITY;
+      if (__all_sync(0xffffffffu, lo <= 0 && hi >= kCols)) {
+#pragma unroll
+        for (int j = 0; j < kCols; j += 2) mx = fmax3(mx, s[j], s[j + 1]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kCols; ++j) {
+          s[j] = (j >= lo && j < hi) ? s[j] : -INFINITY;  // select: NaN-safe
+          mx = fmaxf(mx, s[j]);
+        }
+      }
+      const float m_tile = mx * p.scale_log2;
+      bool resc = false;
+      float alpha = 1.f;
+      if (t == 0) {
+        m_use = m_tile;
+      } else if (m_tile > m_use + kRescaleThreshold) {
+        alpha = m_use == -INFINITY ? 0.f : fast_exp2(m_use - m_tile);
+        resc = m_use != -INFINITY;  // O is all zeros while nothing was valid
+        l *= alpha;
+        m_use = m_tile;
+      }
+      const float msafe = m_use == -INFINITY ? 0.f : m_use;
+      const uint64_t c2 = f32x2(p.scale_log2, p.scale_log2);
+      const uint64_t nm2 = f32x2(-msafe, -msafe);
+      uint32_t w[kWords];
+      uint64_t acc2 = f32x2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < kWords; ++j) {
+        float x0, x1;
+        f32x2_split(ffma2(f32x2(s[2 * j], s[2 * j + 1]), c2, nm2), x0, x1);
+        const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+        acc2 = fadd2(acc2, f32x2(p0, p1));
+        w[j] = Elem<T>::pack2(p0, p1);
+      }
+      float a0, a1;
+      f32x2_split(acc2, a0, a1);
+      l += a0 + a1;
+      // P over the S buffer: this copy's words, zeros over the other copies'
+      if constexpr (kC == 1) {
+        tmem_st32(t_s, w);
+        tmem_st32(t_s + 32, w + 32);
+      } else if constexpr (kC == 2) {
+        uint32_t z[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) z[j] = 0u;
+        tmem_st32(t_s + copy * 32, w);
+        tmem_st32(t_s + (copy ^ 1) * 32, z);
+      } else {
+        uint32_t z[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) z[j] = 0u;
+        tmem_st16p(t_s + copy * 16, w);
+#pragma unroll
+        for (int cc = 1; cc < 4; ++cc) tmem_st16p(t_s + ((copy + cc) & 3) * 16, z);
+      }
+      if (t > 0) {
+        // PV of the previous tile must be complete before O is rescaled
+        // (every row warp waits on every pv_done phase, in tile order)
+        if (!(ok = warp_wait(smem_u32(&bars->pv_done), (g - 1) & 1u, abort_flag, p.status,
+                             kDevTimeoutSoftmax)))
+          break;
+        if (__any_sync(0xffffffffu, resc)) {
+          tc_fence_after();
+          const float a = resc ? alpha : 1.f;
+#pragma unroll 1
+          for (int j = 0; j < kD / 32; ++j) {
+            float v[32];
+            uint32_t u[32];
+            tmem_ld32(t_o + 32 * j, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(v[i] * a);
+            tmem_st32(t_o + 32 * j, u);
+          }
+        }
+      }
+      // Value rows past the sequence end inside the last loaded page may
+      // hold any bits (even NaN); P is 0 there but 0 * NaN is not, so clear
+      // them before the PV product.
+      if (warp == 0 && pc.len > n0 && pc.len < n0 + kTileN && pc.len <= pc.tok_end) {
+        const int jb = (pc.len - 1 - n0) / p.box_rows;
+        const int r0 = pc.len - n0, r1 = (jb + 1) * p.box_rows;
+        const int btok = n0 + jb * p.box_rows;
+        if (r1 > r0 && btok < pc.tok_end && btok + p.box_rows > pc.tok0) {
+          const uint32_t st = g % PL::kStages;
+          if (!(ok = warp_wait(smem_u32(&bars->v_full[st]), (g / PL::kStages) & 1u, abort_flag,
+                               p.status, kDevTimeoutSoftmax)))
+            break;
+          const uint32_t tile = vbase + st * PL::kTileBytes;
+          const int units = (r1 - r0) * 8;
+          for (int u = lane; u < units * PL::kChunks; u += 32) {
+            const int ch = u / units, rem = u % units;
+            const uint32_t addr = tile + ch * kChunkBytes + (r0 + rem / 8) * 128 + (rem % 8) * 16;
+            asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u)
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[buf]));
+    }
+    if (!ok) break;
+    if (n_tiles > 0) {
+      if (!(ok = warp_wait(smem_u32(&bars->pv_done), (g - 1) & 1u, abort_flag, p.status,
+                           kDevTimeoutSoftmax)))
+        break;
+      tc_fence_after();
+      ++k;
+    }
+    if (!(ok = epilogue<T, kD, kC>(p, pc, n_tiles > 0, live, r, g_idx, m_idx, warp, lane, quads,
+                                   m_use, l, t_o, stage, stat_m, stat_l, rs, abort_flag)))
+      break;
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+template <typename T, int kD, int kC>
+__global__ void __launch_bounds__(kThreads, 1)
+    gqa_decode_kernel(const __grid_constant__ CUtensorMap k_map,
+                      const __grid_constant__ CUtensorMap v_map,
+                      const __grid_constant__ Params p) {
+  using PL = Plan<kD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  if (smem + PL::kSmemUsed > smem_raw + PL::kSmemBytes) {
+    if (threadIdx.x == 0 && p.status) atomicExch(p.status, kDevBadSmemAlign);
+    return;
+  }
+  Bars *bars = reinterpret_cast<Bars *>(smem);
+  volatile int *abort_flag = &bars->abort_flag;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr int fmt = std::is_same<T, __half>::value ? 0 : 1;
+  const int quads = kC == 1 ? (p.rows + 31) / 32 : 4 / kC;
+  const uint32_t row_warps = static_cast<uint32_t>(quads * kC);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < PL::kStages; ++i) {
+      mbar_init(smem_u32(&bars->k_full[i]), 1);
+      mbar_init(smem_u32(&bars->k_empty[i]), 1);
+      mbar_init(smem_u32(&bars->v_full[i]), 1);
+      mbar_init(smem_u32(&bars->v_empty[i]), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&bars->s_full[i]), 1);
+      mbar_init(smem_u32(&bars->p_full[i]), row_warps);
+      mbar_init(smem_u32(&bars->q_full[i]), row_warps);
+    }
+    mbar_init(smem_u32(&bars->pv_done), 1);
+    mbar_init(smem_u32(&bars->merge), 4);
+    mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    tma_prefetch_desc(&k_map);
+    tma_prefetch_desc(&v_map);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_u32(&bars->tmem_base), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  // The schedule comes from the kernel this one may overlap (programmatic
+  // dependent launch); wait for it before the first metadata read, then let
+  // the merge kernel queued behind this one launch.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp < 4) {
+    row_role<T, kD, kC>(p, bars, smem, tmem, warp, lane);
+  } else if (warp == kProducerWarp) {
+    // ------------------------------------------------------- TMA producer
+    const uint32_t kbase = smem_u32(smem + PL::kOffK), vbase = smem_u32(smem + PL::kOffV);
+    const int nbox = kTileN / p.box_rows;
+    uint32_t g = 0, gk = 0, gv = 0;  // tiles begun, K tiles issued, V tiles issued
+    bool ok = true;
+    for (Cursor c = first_cursor(p); c.valid(p) && ok; advance(p, c)) {
+      const Piece pc = get_piece(p, c);
+      const int n_tiles = pc.tiles();
+      int n0 = pc.tok0 & ~(kTileN - 1);
+      for (int t = 0; t < n_tiles; ++t, ++g, n0 += kTileN) {
+        // box of lane j: tokens [n0 + j * box_rows, + box_rows); boxes that
+        // miss the piece read an out-of-range page (zero fill, no traffic)
+        int y = 0, page = p.block_table ? p.num_pages : p.batch;
+        if (lane < nbox) {
+          const int tok = n0 + lane * p.box_rows;
+          if (tok < pc.tok_end && tok + p.box_rows > pc.tok0) {
+            if (p.block_table) {
+              page = __ldg(p.block_table + pc.b * p.bt_stride + tok / p.page_size);
+              y = tok % p.page_size;
+            } else {
+              page = pc.b;
+              y = tok;
+            }
+          }
+        }
+        const uint32_t st = g % PL::kStages, ph = ((g / PL::kStages) & 1u) ^ 1u;
+        if (!(ok = warp_wait(smem_u32(&bars->k_empty[st]), ph, abort_flag, p.status,
+                             kDevTimeoutProducer)))
+          break;
+        const uint32_t kf = smem_u32(&bars->k_full[st]);
+        if (lane == 0) mbar_arrive_expect_tx(kf, PL::kTileBytes);
+        __syncwarp();
+        if (lane < nbox) {
+#pragma unroll
+          for (int ch = 0; ch < PL::kChunks; ++ch)
+            tma_load_4d(kbase + st * PL::kTileBytes + ch * kChunkBytes + lane * p.box_rows * 128,
+                        &k_map, kf, ch * 64, y, pc.kvh, page);
+        }
+        ++gk;
+        if (!(ok = warp_wait(smem_u32(&bars->v_empty[st]), ph, abort_flag, p.status,
+                             kDevTimeoutProducer)))
+          break;
+        const uint32_t vf = smem_u32(&bars->v_full[st]);
+        if (lane == 0) mbar_arrive_expect_tx(vf, PL::kTileBytes);
+        __syncwarp();
+        if (lane < nbox) {
+#pragma unroll
+          for (int ch = 0; ch < PL::kChunks; ++ch)
+            tma_load_4d(vbase + st * PL::kTileBytes + ch * kChunkBytes + lane * p.box_rows * 128,
+                        &v_map, vf, ch * 64, y, pc.kvh, page);
+        }
+        ++gv;
+      }
+    }
+    if (*abort_flag) {
+      // copies in flight must land before the CTA may exit: wait (bounded)
+      // on the full barrier of every slot filled in the last ring's worth
+      volatile int never = 0;
+      for (uint32_t t = gk > PL::kStages ? gk - PL::kStages : 0; t < gk; ++t)
+        mbar_wait(smem_u32(&bars->k_full[t % PL::kStages]), (t / PL::kStages) & 1u, &never,
+                  nullptr, 0);
+      for (uint32_t t = gv > PL::kStages ? gv - PL::kStages : 0; t < gv; ++t)
+        mbar_wait(smem_u32(&bars->v_full[t % PL::kStages]), (t / PL::kStages) & 1u, &never,
+                  nullptr, 0);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------- MMA issuer
+    constexpr uint32_t kIdescQK = umma_idesc_f16(128, kTileN, fmt, 0);
+    constexpr uint32_t kIdescPV = umma_idesc_f16(128, kD, fmt, 1);
+    const uint32_t kbase = smem_u32(smem + PL::kOffK), vbase = smem_u32(smem + PL::kOffV);
+    const uint64_t k_desc = smem_desc_sw128(kbase, 16, 1024);
+    const uint64_t v_desc = smem_desc_sw128(vbase, kChunkBytes, 1024);
+    uint32_t g = 0, k = 0;
+    bool ok = true;
+    int pend = -1;             // tile whose PV is still to be issued
+    bool pend_first = false;   // ... and whether it opens its piece
+    auto issue_pv = [&](uint32_t gp, bool first) -> bool {
+      const uint32_t buf = gp & 1u, st = gp % PL::kStages;
+      if (!warp_wait(smem_u32(&bars->p_full[buf]), (gp >> 1) & 1u, abort_flag, p.status,
+                     kDevTimeoutMma))
+        return false;
+      if (!warp_wait(smem_u32(&bars->v_full[st]), (gp / PL::kStages) & 1u, abort_flag, p.status,
+                     kDevTimeoutMma))
+        return false;
+      tc_fence_after();
+      const uint64_t vd = v_desc + static_cast<uint64_t>((st * PL::kTileBytes) >> 4);
+#pragma unroll
+      for (int kk = 0; kk < kTileN / 16; ++kk)
+        umma_ts_warp(tmem + PL::kColO, tmem + PL::kColS + buf * kTileN + kk * 8,
+                     vd + static_cast<uint64_t>((kk * 16 * 128) >> 4), kIdescPV,
+                     (first && kk == 0) ? 0u : 1u);
+      tc_commit_warp(smem_u32(&bars->v_empty[st]));
+      tc_commit_warp(smem_u32(&bars->pv_done));
+      return true;
+    };
+    for (Cursor c = first_cursor(p); c.valid(p) && ok; advance(p, c)) {
+      const Piece pc = get_piece(p, c);
+      const int n_tiles = pc.tiles();
+      if (n_tiles == 0) continue;
+      if (!(ok = warp_wait(smem_u32(&bars->q_full[k & 1u]), (k >> 1) & 1u, abort_flag, p.status,
+                           kDevTimeoutMma)))
+        break;
+      const uint32_t qcol = tmem + PL::kColQ + (k & 1u) * (kD / 2);
+      for (int t = 0; t < n_tiles && ok; ++t, ++g) {
+        const uint32_t st = g % PL::kStages;
+        if (!(ok = warp_wait(smem_u32(&bars->k_full[st]), (g / PL::kStages) & 1u, abort_flag,
+                             p.status, kDevTimeoutMma)))
+          break;
+        tc_fence_after();
+        const uint32_t sd = tmem + PL::kColS + (g & 1u) * kTileN;
+        const uint64_t kd = k_desc + static_cast<uint64_t>((st * PL::kTileBytes) >> 4);
+#pragma unroll
+        for (int ch = 0; ch < PL::kChunks; ++ch)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_ts_warp(sd, qcol + ch * 32 + kk * 8,
+                         kd + static_cast<uint64_t>((ch * kChunkBytes + kk * 32) >> 4), kIdescQK,
+                         (ch | kk) ? 1u : 0u);
+        tc_commit_warp(smem_u32(&bars->k_empty[st]));
+        tc_commit_warp(smem_u32(&bars->s_full[g & 1u]));
+        // the previous tile's PV goes after this QK, so the tensor pipe
+        // computes S of tile g while the row warps still work on tile g - 1
+        if (pend >= 0 && !(ok = issue_pv(static_cast<uint32_t>(pend), pend_first))) break;
+        pend = static_cast<int>(g);
+        pend_first = t == 0;
+      }
+      ++k;
+    }
+    if (ok && pend >= 0) ok = issue_pv(static_cast<uint32_t>(pend), pend_first);
+    // every issued MMA must finish before TMEM is released
+    tc_commit_warp(smem_u32(&bars->drain));
+    volatile int never = 0;
+    mbar_wait(smem_u32(&bars->drain), 0, &never, p.status, kDevTimeoutDrain);
+    __syncwarp();
+  }
+
+  // -------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <typename T, int kD, int kC>
+cudaError_t launch_t(const CUtensorMap &km, const CUtensorMap &vm, const Params &p, int grid,
+                     bool pdl, cudaStream_t stream) {
+  auto kern = gqa_decode_kernel<T, kD, kC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Plan<kD>::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Plan<kD>::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, km, vm, p);
+}
+
+template <typename T, int kD>
+cudaError_t launch_d(const CUtensorMap &km, const CUtensorMap &vm, const Params &p, int grid,
+                     bool pdl, cudaStream_t stream) {
+  if (p.rows <= 32) return launch_t<T, kD, 4>(km, vm, p, grid, pdl, stream);
+  if (p.rows <= 64) return launch_t<T, kD, 2>(km, vm, p, grid, pdl, stream);
+  return launch_t<T, kD, 1>(km, vm, p, grid, pdl, stream);
+}
+
+}  // namespace gqa
+
+size_t gqa_smem_bytes(int d) {
+  return d == 64 ? gqa::Plan<64>::kSmemBytes : gqa::Plan<128>::kSmemBytes;
+}
+
+// The tensor-core kernel serves bf16 / f16 with d_qk == d_v in {64, 128},
+// at most 128 query rows per kv head, a positive scale, 16-byte aligned rows
+// and pages of a power-of-two size >= 16 or a multiple of 128 tokens.
+bool gqa_tc_eligible(const fa_decode_args *a) {
+  auto al16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+  auto m8 = [](int64_t x) { return x % 8 == 0; };
+  if (a->dtype != FA_DTYPE_BF16 && a->dtype != FA_DTYPE_F16) return false;
+  if (a->d_qk != a->d_v || (a->d_qk != 64 && a->d_qk != 128)) return false;
+  if (a->num_kv_heads <= 0 || a->num_q_heads % a->num_kv_heads) return false;
+  const int64_t rows = static_cast<int64_t>(a->num_q_heads / a->num_kv_heads) * a->m_q;
+  if (rows < 1 || rows > 128) return false;
+  if (!(a->scale > 0.f)) return false;
+  if (!al16(a->q) || !al16(a->k) || !al16(a->v) || !al16(a->o)) return false;
+  if (!m8(a->q_stride_b) || !m8(a->q_stride_h) || !m8(a->q_stride_m)) return false;
+  if (!m8(a->o_stride_b) || !m8(a->o_stride_h) || !m8(a->o_stride_m)) return false;
+  if (!m8(a->k_stride_seq) || !m8(a->k_stride_tok) || !m8(a->k_stride_head)) return false;
+  if (a->block_table) {
+    const int ps = a->page_size;
+    if (ps < 16 || ps % 16) return false;
+    if (ps <= gqa::kTileN ? (gqa::kTileN % ps) : (ps % gqa::kTileN)) return false;
+    if (a->num_pages <= 0) return false;
+  }
+  return true;
+}
+
+// Launch the decode (and, when pieces were split, the merge) for eligible
+// arguments.  Balanced schedule (a->num_splits == 0): `meta` / `prefix` were
+// written by the scheduler kernel just before on the same stream.
+cudaError_t launch_gqa_tc(const CUtensorMap &km, const CUtensorMap &vm, const fa_decode_args *a,
+                          const int32_t *meta, const int32_t *prefix, int num_parts, int grid,
+                          bool pdl, cudaStream_t stream) {
+  gqa::Params p;
+  p.q = a->q;
+  p.q_sb = a->q_stride_b;
+  p.q_sh = a->q_stride_h;
+  p.q_sm = a->q_stride_m;
+  p.block_table = a->block_table;
+  p.bt_stride = a->bt_stride;
+  p.page_size = a->page_size;
+  p.num_pages = a->num_pages;
+  p.box_rows = a->block_table ? (a->page_size < gqa::kTileN ? a->page_size : gqa::kTileN)
+                              : gqa::kTileN;
+  p.seq_lens = a->seq_lens;
+  p.n_ctx = a->n_ctx;
+  p.batch = a->batch;
+  p.hq = a->num_q_heads;
+  p.hkv = a->num_kv_heads;
+  p.group = a->num_q_heads / a->num_kv_heads;
+  p.m_q = a->m_q;
+  p.rows = p.group * a->m_q;
+  p.causal = a->causal;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.meta = meta;
+  p.prefix = prefix;
+  p.num_parts = num_parts;
+  p.num_splits = a->num_splits > 0 ? a->num_splits : 1;
+  p.partition_size = a->partition_size;
+  p.o = a->o;
+  p.o_sb = a->o_stride_b;
+  p.o_sh = a->o_stride_h;
+  p.o_sm = a->o_stride_m;
+  p.lse = a->lse;
+  p.part_o = a->part_o;
+  p.part_lse = a->part_lse;
+  p.status = a->status;
+  const bool f16 = a->dtype == FA_DTYPE_F16;
+  if (a->d_qk == 64)
+    return f16 ? gqa::launch_d<__half, 64>(km, vm, p, grid, pdl, stream)
+               : gqa::launch_d<__nv_bfloat16, 64>(km, vm, p, grid, pdl, stream);
+  return f16 ? gqa::launch_d<__half, 128>(km, vm, p, grid, pdl, stream)
+             : gqa::launch_d<__nv_bfloat16, 128>(km, vm, p, grid, pdl, stream);
+}
+
+}  // namespace fa

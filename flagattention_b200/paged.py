@@ -10,17 +10,21 @@ Two paths, chosen by shape:
 * the MLA latent shape (one kv head, 576-dim keys, values = the first 512
   dims of the same cache rows, block size a multiple of 64, bf16/f16) runs on
   the tcgen05 tensor-core kernel with the balanced tile scheduler;
-* every other shape (the reference's own test grid: head sizes 16..512,
-  grouped heads, f16/bf16/f32) runs the generic kernel with the reference's
-  split rule (``paged.py:54-67``, bit-exact through ``fa_paged_num_splits``).
+* bf16/f16 with head size 64 or 128 and up to 128 query heads per kv head
+  runs the tcgen05 grouped-query kernel (``csrc/gqa_tc.cu``); with the
+  default ``num_splits=0`` the device scheduler balances the key blocks over
+  the SMs, an explicit ``num_splits`` keeps the reference's partitions;
+* every other shape (head sizes 16..512, f32) runs the CUDA-core kernel with
+  the reference's split rule (``paged.py:54-67``, bit-exact through
+  ``fa_paged_num_splits``).
 """
 
 import ctypes
 
 import torch
 
-from flagattention_b200 import _lib
-from flagattention_b200._torch import dtype_code, ptr, require_cuda, sm_count, stream_of
+from flagattention_b200 import _decode, _lib
+from flagattention_b200._torch import dtype_code, require_cuda, sm_count, status_word, stream_of
 
 
 def paged_num_splits(num_seqs, num_kv_heads, max_context_len, kv_block_size, num_sms,
@@ -73,11 +77,15 @@ def paged_attention(query, key_cache, value_cache, context_lens, block_tables, a
     if query.stride(-1) != 1 or key_cache.stride(-1) != 1:
         raise _lib.InvalidArgument("last dims must be contiguous")
     d_v = value_cache.shape[3]
-    ns, ps = paged_num_splits(num_seqs, num_kv_heads, int(max_context_len), block_size,
-                              sm_count(query.device), int(num_splits))
-    if ns > 1 and not (ps >= block_size and ps % block_size == 0):
-        # the reference asserts this (paged.py:124)
-        raise _lib.InvalidArgument(f"partition_size={ps}, kv_block_size={block_size}")
+
+    def reference_splits():
+        ns, ps = paged_num_splits(num_seqs, num_kv_heads, int(max_context_len), block_size,
+                                  sm_count(query.device), int(num_splits))
+        if ns > 1 and not (ps >= block_size and ps % block_size == 0):
+            # the reference asserts this (paged.py:124)
+            raise _lib.InvalidArgument(f"partition_size={ps}, kv_block_size={block_size}")
+        return ns, ps
+
     out = torch.empty((num_seqs, num_q_heads, d_v), dtype=query.dtype, device=query.device)
     a = _lib.DecodeArgs()
     a.q = query.data_ptr()
@@ -88,21 +96,16 @@ def paged_attention(query, key_cache, value_cache, context_lens, block_tables, a
     a.block_table = block_tables.data_ptr()
     a.bt_stride = block_tables.stride(0)
     a.page_size = block_size
+    a.num_pages = key_cache.shape[0]
     a.seq_lens = context_lens.data_ptr()
     a.batch, a.num_q_heads, a.num_kv_heads, a.m_q = num_seqs, num_q_heads, num_kv_heads, 1
     a.d_qk, a.d_v = head_size, d_v
     a.causal = 0
     a.dtype = dtype_code(query)
     a.scale = float(attn_scale)
-    a.num_splits, a.partition_size = ns, ps
     a.o = out.data_ptr()
     a.o_stride_b, a.o_stride_h, a.o_stride_m = out.stride(0), out.stride(1), 0
-    part = None
-    if ns > 1:
-        rows = num_seqs * num_q_heads
-        part = torch.empty(ns * rows * (d_v + 1), dtype=torch.float32, device=query.device)
-        a.part_o = part.data_ptr()
-        a.part_lse = part.data_ptr() + ns * rows * d_v * 4
-    _lib.check(_lib.lib().fa_paged_attention(ctypes.byref(a), stream_of(query)),
-               "fa_paged_attention")
+    a.status = status_word(query.device).data_ptr()
+    _decode.run(a, "fa_paged_attention", query.device, stream_of(query), int(num_splits),
+                reference_splits)
     return out

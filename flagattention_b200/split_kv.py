@@ -4,11 +4,13 @@
 ``split_kv.py:279-344`` and ``flash_attention(..., return_log_normalizer=True)``
 the split branch of ``flash.py:72-171`` (forward only): q [B, H, M, D],
 k [B, Hk, N, D], v [B, Hk, N, Dv], bottom-right causal masking, grouped
-heads.  The split count is the reference heuristic (``num_splits_herustic``,
-``split_kv.py:247-276``, bit-exact through ``fa_split_kv_num_splits``) with its
-split size ``cdiv(cdiv(N, 128), S) * 128`` (``split_kv.py:313``).  The MLA
-shape (one kv head, 576-dim keys, v = k[..., :512] sharing storage) runs on
-the tensor-core kernel instead.
+heads.  bf16/f16 with head size 64 or 128 (up to 128 query rows per kv
+head) runs the tcgen05 grouped-query kernel with the device scheduler's
+balanced split; other shapes run the CUDA-core kernel with the reference
+heuristic (``num_splits_herustic``, ``split_kv.py:247-276``, bit-exact through
+``fa_split_kv_num_splits``) and its split size ``cdiv(cdiv(N, 128), S) * 128``
+(``split_kv.py:313``).  The MLA shape (one kv head, 576-dim keys, v =
+k[..., :512] sharing storage) runs on the MLA kernel.
 """
 
 import ctypes
@@ -16,8 +18,8 @@ import math
 
 import torch
 
-from flagattention_b200 import _lib
-from flagattention_b200._torch import dtype_code, require_cuda, sm_count, stream_of
+from flagattention_b200 import _decode, _lib
+from flagattention_b200._torch import dtype_code, require_cuda, sm_count, status_word, stream_of
 
 BLOCK_M, BLOCK_N, MAX_SPLITS = 16, 128, 128
 
@@ -74,9 +76,12 @@ def _attention(q, k, v, causal, sm_scale):
         v = v.contiguous()
         k = k.contiguous()
     d_v = v.shape[3]
-    S = split_kv_num_splits(B, H, M, N, sm_count(q.device))
-    # split_kv.py:313: N_SPLIT_SIZE = cdiv(cdiv(N, BLOCK_N), S) * BLOCK_N
-    split_size = _cdiv(_cdiv(N, BLOCK_N), S) * BLOCK_N if S > 1 else 0
+
+    def reference_splits():
+        S = split_kv_num_splits(B, H, M, N, sm_count(q.device))
+        # split_kv.py:313: N_SPLIT_SIZE = cdiv(cdiv(N, BLOCK_N), S) * BLOCK_N
+        return S, (_cdiv(_cdiv(N, BLOCK_N), S) * BLOCK_N if S > 1 else 0)
+
     out = torch.empty((B, H, M, d_v), dtype=q.dtype, device=q.device)
     lse = torch.empty((B, H, M), dtype=torch.float32, device=q.device)
     a = _lib.DecodeArgs()
@@ -92,18 +97,11 @@ def _attention(q, k, v, causal, sm_scale):
     a.causal = int(bool(causal))
     a.dtype = dtype_code(q)
     a.scale = float(sm_scale)
-    a.num_splits, a.partition_size = S, split_size
     a.o = out.data_ptr()
     a.o_stride_b, a.o_stride_h, a.o_stride_m = out.stride(0), out.stride(1), out.stride(2)
     a.lse = lse.data_ptr()
-    part = None
-    if S > 1:
-        rows = B * H * M
-        part = torch.empty(S * rows * (d_v + 1), dtype=torch.float32, device=q.device)
-        a.part_o = part.data_ptr()
-        a.part_lse = part.data_ptr() + S * rows * d_v * 4
-    _lib.check(_lib.lib().fa_split_kv_attention(ctypes.byref(a), stream_of(q)),
-               "fa_split_kv_attention")
+    a.status = status_word(q.device).data_ptr()
+    _decode.run(a, "fa_split_kv_attention", q.device, stream_of(q), 0, reference_splits)
     return out, lse
 
 

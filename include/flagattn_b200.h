@@ -22,6 +22,8 @@
  *   fa_mla_get_metadata       no reference function: the FlashMLA-style
  *                             metadata call (get_mla_metadata) that the MLA
  *                             decode path needs; format defined in this file
+ *                             (fa_schedule_entries: the same scheduler for the
+ *                             grouped-query decode's balanced schedule)
  *   fa_mla_decode             paged.py:208-363 generalised to the MLA shape
  *                             (576-dim latent+rope keys, values = first 512
  *                             dims of the same rows, 128 query heads sharing
@@ -101,9 +103,21 @@ int fa_split_kv_num_splits(int batch, int heads, int m, int n, int block_m,
  * bottom-right causal masking for m_q > 1, f16/bf16/f32.
  * Query row (b, h, m) lives at q + b*q_stride_b + h*q_stride_h + m*q_stride_m;
  * the output uses the same scheme with o_* strides; lse (nullable) is f32
- * [batch][num_q_heads][m_q] contiguous.  With num_splits > 1 the partials go
- * to part_o (f32 [num_splits][batch][num_q_heads][m_q][d_v]) and part_lse
- * (f32 [num_splits][batch][num_q_heads][m_q]) and are merged in place. */
+ * [batch][num_q_heads][m_q] contiguous.
+ *
+ * Two kernels serve it:
+ *  - the tensor-core kernel (tcgen05 + TMA), used whenever
+ *    fa_decode_uses_tensor_cores() says so: bf16/f16, d_qk == d_v in
+ *    {64, 128}, at most 128 query rows per kv head (group * m_q), scale > 0,
+ *    16-byte aligned rows, and (paged) num_pages > 0 with a page size that is
+ *    a power of two >= 16 or a multiple of 128.  num_splits == 0 selects its
+ *    balanced schedule (pieces cut by the device scheduler so that every SM
+ *    gets the same work; needs `sched`); num_splits >= 1 keeps the
+ *    reference's fixed partitions of partition_size tokens.
+ *  - the CUDA-core kernel for every other shape (num_splits >= 1).
+ * With splits, partials go to part_o / part_lse and are merged in place.
+ * fa_decode_workspace_size gives the bytes of part_o, part_lse and sched for
+ * the kernel the arguments select (zero when nothing is split). */
 typedef struct fa_decode_args {
   const void *q;
   int64_t q_stride_b, q_stride_h, q_stride_m;
@@ -119,17 +133,23 @@ typedef struct fa_decode_args {
   int32_t causal;
   int32_t dtype;
   float scale;
-  int32_t num_splits;     /* >= 1 */
+  int32_t num_splits;     /* >= 1, or 0 = balanced (tensor-core kernel)   */
   int32_t partition_size; /* tokens per split; 0 = ceil-divide evenly    */
   void *o;
   int64_t o_stride_b, o_stride_h, o_stride_m;
   float *lse;
   float *part_o;
   float *part_lse;
+  int32_t num_pages; /* paged: pages in k / v (the TMA bound); 0 = unknown,
+                        which keeps the CUDA-core kernel                 */
+  int32_t *sched;    /* int32 scheduler scratch (balanced schedule)      */
+  int *status;       /* nullable device status word (kernel time-outs)   */
 } fa_decode_args;
 
+/* 1 when `args` run on the tensor-core kernel, 0 when on the CUDA-core one. */
+int fa_decode_uses_tensor_cores(const fa_decode_args *args);
 int fa_decode_workspace_size(const fa_decode_args *args, size_t *part_o_bytes,
-                             size_t *part_lse_bytes);
+                             size_t *part_lse_bytes, size_t *sched_bytes);
 int fa_paged_attention(const fa_decode_args *args, void *stream);
 int fa_split_kv_attention(const fa_decode_args *args, void *stream);
 
@@ -206,6 +226,17 @@ int fa_mla_workspace_size(int batch, int s_q, int h_q, int d_v,
 int fa_mla_get_metadata(const int32_t *seq_lens, int batch, int topk,
                         int num_sm_parts, int32_t *tile_meta,
                         int32_t *num_splits, void *stream);
+/* The same device scheduler over generic entries: entry e has
+ * seq_lens[e / rep] tokens (uniform_len tokens when seq_lens is NULL),
+ * counted in blocks of block_n tokens plus fixed_cost blocks per piece.
+ * meta is int32 [num_parts][FA_MLA_META_INTS] in the format above with
+ * blocks of block_n tokens, prefix int32 [entries + 1].  The grouped-query
+ * decode's balanced schedule is this call with entries = batch *
+ * num_kv_heads, rep = num_kv_heads, block_n = 128 (its sched scratch holds
+ * meta, then prefix). */
+int fa_schedule_entries(const int32_t *seq_lens, int uniform_len, int entries,
+                        int rep, int block_n, int fixed_cost, int num_parts,
+                        int32_t *meta, int32_t *prefix, void *stream);
 /* Decode kernel, then the combine kernel (queued as a programmatic
  * dependent of the decode: its launch overlaps the decode, and its blocks for
  * sequences that were not split exit before the decode ends). */

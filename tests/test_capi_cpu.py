@@ -39,7 +39,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_status_strings():
     lib = _lib.lib()
-    assert lib.fa_version() == 0x000200
+    assert lib.fa_version() == 0x000300
     assert lib.fa_status_string(0) == b"ok"
     assert lib.fa_status_string(-1) == b"invalid argument"
 
