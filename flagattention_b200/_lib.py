@@ -83,8 +83,10 @@ SIGNATURES = [
     ("fa_split_kv_num_splits", _i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                                       ctypes.POINTER(_i32)]),
     ("fa_decode_uses_tensor_cores", _i32, [ctypes.POINTER(DecodeArgs)]),
-    ("fa_decode_workspace_size", _i32, [ctypes.POINTER(DecodeArgs), ctypes.POINTER(ctypes.c_size_t),
-                                        ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
+    ("fa_decode_workspace_size", _i32, [ctypes.POINTER(DecodeArgs),
+                                        ctypes.POINTER(ctypes.c_size_t),
+                                        ctypes.POINTER(ctypes.c_size_t),
+                                        ctypes.POINTER(ctypes.c_size_t)]),
     ("fa_paged_attention", _i32, [ctypes.POINTER(DecodeArgs), _vp]),
     ("fa_split_kv_attention", _i32, [ctypes.POINTER(DecodeArgs), _vp]),
     ("fa_lse_combine", _i32, [_vp, _vp, _i32, _i64, _i32, _vp, _i32, _vp, _vp]),
@@ -95,7 +97,6 @@ SIGNATURES = [
                                      ctypes.POINTER(ctypes.c_size_t),
                                      ctypes.POINTER(ctypes.c_size_t)]),
     ("fa_mla_get_metadata", _i32, [_vp, _i32, _i32, _i32, _vp, _vp, _vp]),
-    ("fa_schedule_entries", _i32, [_vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp]),
     ("fa_mla_decode", _i32, [ctypes.POINTER(MlaArgs), _vp]),
     ("fa_mla_decode_partial", _i32, [ctypes.POINTER(MlaArgs), _vp]),
     ("fa_mla_combine", _i32, [ctypes.POINTER(MlaArgs), _vp]),

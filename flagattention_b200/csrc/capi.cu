@@ -23,14 +23,13 @@ cudaError_t launch_mla_combine(const float *, const float *, const int32_t *, in
                                bool, void *, int, int64_t, int64_t, int64_t, float *, cudaStream_t);
 cudaError_t launch_generic_decode(const fa_decode_args *, cudaStream_t);
 size_t generic_smem_bytes(int, int);
-void launch_entry_metadata(const int32_t *, int, int, int, int, int, int, int32_t *, int32_t *,
-                           cudaStream_t);
 bool gqa_tc_eligible(const fa_decode_args *);
 cudaError_t launch_gqa_tc(const CUtensorMap &, const CUtensorMap &, const fa_decode_args *,
-                          const int32_t *, const int32_t *, int, int, bool, cudaStream_t);
-cudaError_t launch_gqa_combine(const float *, const float *, const int32_t *, int, int, int, int,
+                          int4 *, int, int, bool, cudaStream_t);
+cudaError_t launch_gqa_combine(const float *, const float *, const int4 *, int, int, int, int,
                                int, int, int, int, bool, void *, int, int64_t, int64_t, int64_t,
                                float *, cudaStream_t);
+int gqa_max_balanced_batch();
 cudaError_t launch_mla_sv(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                           const CUtensorMap &, const fa_mla_args *, int, cudaStream_t);
 }  // namespace fa
@@ -155,8 +154,7 @@ int encode_gather_map(CUtensorMap *map, const void *base, int dtype, uint64_t ro
   return FA_OK;
 }
 
-constexpr int kGqaBlockN = 128;   // tokens per scheduled block (one tile)
-constexpr int kGqaFixedCost = 1;  // per-piece overhead, in blocks
+constexpr int kGqaBlockN = 128;   // tokens per tile (page boxes hold at most this many rows)
 
 // K and V tensor maps of the grouped-query kernel: boxes of 64 dims x one
 // page (at most 128 rows) over {d, page rows, kv heads, pages}, or 128 rows
@@ -178,11 +176,14 @@ int encode_kv_maps(const fa_decode_args *a, CUtensorMap *km, CUtensorMap *vm) {
 // Tensor-core kernel for these arguments?  Shapes, types and alignment
 // (gqa_tc_eligible), a batch the maps can describe, and strides the TMA unit
 // accepts (the encoder is asked; it runs on the host only).
-bool decode_on_tensor_cores(const fa_decode_args *a) {
+bool tc_maps(const fa_decode_args *a, CUtensorMap *km, CUtensorMap *vm) {
   if (a->block_table == nullptr && a->seq_lens == nullptr && a->n_ctx < 1) return false;
   if (a->batch < 1 || !fa::gqa_tc_eligible(a)) return false;
+  return encode_kv_maps(a, km, vm) == FA_OK;
+}
+bool decode_on_tensor_cores(const fa_decode_args *a) {
   CUtensorMap km, vm;
-  return encode_kv_maps(a, &km, &vm) == FA_OK;
+  return tc_maps(a, &km, &vm);
 }
 
 int current_sm_count(int *sms) {
@@ -192,7 +193,8 @@ int current_sm_count(int *sms) {
   return fa_device_sm_count(dev, sms);
 }
 
-int validate_decode(const fa_decode_args *a) {
+// `tc`: the arguments run on the tensor-core kernel (decode_on_tensor_cores).
+int validate_decode(const fa_decode_args *a, bool tc) {
   if (!a) return fail(FA_ERR_INVALID_ARGUMENT, "null args");
   if (!a->q || !a->k || !a->v || !a->o) return fail(FA_ERR_INVALID_ARGUMENT, "null tensor");
   if (a->batch < 0 || a->num_q_heads <= 0 || a->num_kv_heads <= 0 || a->m_q <= 0)
@@ -212,13 +214,15 @@ int validate_decode(const fa_decode_args *a) {
   } else if (!a->seq_lens && a->n_ctx < 0) {
     return fail(FA_ERR_INVALID_ARGUMENT, "n_ctx %d", a->n_ctx);
   }
-  const bool tc = decode_on_tensor_cores(a);
   if (a->num_splits < 0 || (a->num_splits == 0 && !tc))
     return fail(FA_ERR_INVALID_ARGUMENT,
                 "num_splits %d (0 selects the balanced schedule of the tensor-core kernel)",
                 a->num_splits);
   if (a->num_splits == 0 && !a->sched)
     return fail(FA_ERR_INVALID_ARGUMENT, "the balanced schedule needs the sched scratch");
+  if (a->num_splits == 0 && a->batch > fa::gqa_max_balanced_batch())
+    return fail(FA_ERR_UNSUPPORTED, "balanced schedule: at most %d sequences per call",
+                fa::gqa_max_balanced_batch());
   if (a->num_splits != 1 && (!a->part_o || !a->part_lse || !aligned16(a->part_o)))
     return fail(FA_ERR_INVALID_ARGUMENT, "split decode needs 16-byte aligned f32 workspace");
   if (a->num_splits > 1 && a->partition_size <= 0)
@@ -231,30 +235,24 @@ int validate_decode(const fa_decode_args *a) {
 // The tensor-core path: K / V tensor maps, then (balanced schedule) the
 // scheduler kernel, the decode as its programmatic dependent and the merge
 // of split entries as the decode's.
-int run_decode_tc(const fa_decode_args *a, cudaStream_t s) {
+int run_decode_tc(const fa_decode_args *a, const CUtensorMap &km, const CUtensorMap &vm,
+                  cudaStream_t s) {
   int sms = 0;
   int st = current_sm_count(&sms);
-  if (st != FA_OK) return st;
-  CUtensorMap km, vm;
-  st = encode_kv_maps(a, &km, &vm);
   if (st != FA_OK) return st;
   const int entries = a->batch * a->num_kv_heads;
   const int group = a->num_q_heads / a->num_kv_heads;
   const int qrows = group * a->m_q;
   cudaError_t e;
   if (a->num_splits == 0) {
-    const int parts = sms;
-    int32_t *meta = a->sched;
-    int32_t *prefix = a->sched + static_cast<int64_t>(parts) * FA_MLA_META_INTS;
-    fa::launch_entry_metadata(a->seq_lens, a->seq_lens ? 0 : a->n_ctx, entries, a->num_kv_heads,
-                              kGqaBlockN, kGqaFixedCost, parts, meta, prefix, s);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "scheduler launch");
-    e = fa::launch_gqa_tc(km, vm, a, meta, prefix, parts, parts, true, s);
+    // every CTA cuts its share of the work out of the sequence lengths;
+    // split entries leave merge records in the sched scratch
+    int4 *merge = reinterpret_cast<int4 *>(a->sched);
+    e = fa::launch_gqa_tc(km, vm, a, merge, sms, sms, true, s);
     if (e != cudaSuccess) return cuda_fail(e, "tensor-core decode launch");
-    e = fa::launch_gqa_combine(a->part_o, a->part_lse, prefix, 0, entries, qrows, a->m_q, group,
+    e = fa::launch_gqa_combine(a->part_o, a->part_lse, merge, 0, entries, qrows, a->m_q, group,
                                a->num_kv_heads, a->num_q_heads, a->d_v,
-                               static_cast<int64_t>(entries) * 4 <= parts, a->o, a->dtype,
+                               static_cast<int64_t>(entries) * 4 <= sms, a->o, a->dtype,
                                a->o_stride_b, a->o_stride_h, a->o_stride_m, a->lse, s);
     if (e != cudaSuccess) return cuda_fail(e, "merge launch");
     return FA_OK;
@@ -263,7 +261,7 @@ int run_decode_tc(const fa_decode_args *a, cudaStream_t s) {
   const int64_t parts = static_cast<int64_t>(entries) * ns;
   if (parts > INT32_MAX) return fail(FA_ERR_UNSUPPORTED, "too many partitions");
   const int grid = static_cast<int>(parts < sms ? parts : sms);
-  e = fa::launch_gqa_tc(km, vm, a, nullptr, nullptr, static_cast<int>(parts), grid, false, s);
+  e = fa::launch_gqa_tc(km, vm, a, nullptr, static_cast<int>(parts), grid, false, s);
   if (e != cudaSuccess) return cuda_fail(e, "tensor-core decode launch");
   if (ns > 1) {
     e = fa::launch_gqa_combine(a->part_o, a->part_lse, nullptr, ns, entries, qrows, a->m_q, group,
@@ -276,11 +274,15 @@ int run_decode_tc(const fa_decode_args *a, cudaStream_t s) {
 }
 
 int run_decode(const fa_decode_args *a, void *stream) {
-  int st = validate_decode(a);
+  if (!a) return fail(FA_ERR_INVALID_ARGUMENT, "null args");
+  // one eligibility test, one pair of tensor maps per call
+  CUtensorMap km, vm;
+  const bool tc = tc_maps(a, &km, &vm);
+  int st = validate_decode(a, tc);
   if (st != FA_OK) return st;
   if (a->batch == 0) return FA_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (decode_on_tensor_cores(a)) return run_decode_tc(a, s);
+  if (tc) return run_decode_tc(a, km, vm, s);
   cudaError_t e = fa::launch_generic_decode(a, s);
   if (e != cudaSuccess) return cuda_fail(e, "generic decode launch");
   if (a->num_splits > 1) {
@@ -442,10 +444,13 @@ int fa_decode_workspace_size(const fa_decode_args *a, size_t *part_o_bytes,
     int sms = 0;
     int st = current_sm_count(&sms);
     if (st != FA_OK) return st;
-    const size_t entries = static_cast<size_t>(a->batch) * a->num_kv_heads;
-    // at most one extra piece per part beyond one per entry
-    slots = entries + sms;
-    sched = (static_cast<size_t>(sms) * FA_MLA_META_INTS + entries + 1) * sizeof(int32_t);
+    if (a->batch > fa::gqa_max_balanced_batch())
+      return fail(FA_ERR_UNSUPPORTED, "balanced schedule: at most %d sequences per call",
+                  fa::gqa_max_balanced_batch());
+    // two split slots per CTA (its first and its last piece); one int4 merge
+    // record per entry
+    slots = 2 * static_cast<size_t>(sms);
+    sched = static_cast<size_t>(a->batch) * a->num_kv_heads * 4 * sizeof(int32_t);
   } else if (a->num_splits > 1) {
     slots = static_cast<size_t>(a->batch) * a->num_kv_heads * a->num_splits;
   }
@@ -533,18 +538,6 @@ int fa_mla_get_metadata(const int32_t *seq_lens, int batch, int topk, int num_sm
                           static_cast<cudaStream_t>(stream));
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? FA_OK : cuda_fail(e, "metadata launch");
-}
-
-int fa_schedule_entries(const int32_t *seq_lens, int uniform_len, int entries, int rep,
-                        int block_n, int fixed_cost, int num_parts, int32_t *meta,
-                        int32_t *prefix, void *stream) {
-  if (entries < 0 || rep < 1 || block_n < 1 || fixed_cost < 0 || num_parts < 1 || !meta ||
-      !prefix || (!seq_lens && uniform_len < 1 && entries))
-    return fail(FA_ERR_INVALID_ARGUMENT, "bad scheduler arguments");
-  fa::launch_entry_metadata(seq_lens, seq_lens ? 0 : uniform_len, entries, rep, block_n,
-                            fixed_cost, num_parts, meta, prefix, static_cast<cudaStream_t>(stream));
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? FA_OK : cuda_fail(e, "scheduler launch");
 }
 
 int fa_mla_combine(const fa_mla_args *a, void *stream) {

@@ -61,29 +61,53 @@ __global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
 }
 
 // Grouped-query entries (entry e = sequence * kv_heads + kv head, rows r =
-// head-in-group * m_q + query token): entry e owns split slots prefix[e] ..
-// prefix[e+1]-1 (balanced schedule) or e * splits .. + splits - 1 (fixed
-// partitions, prefix == nullptr) of part_o [slot][rows][d_v].  Launched as a
-// programmatic dependent of the decode; the slot table itself comes from the
-// scheduler kernel before the decode, so it is read after the wait too.
+// head-in-group * m_q + query token), partials part_o [slot][rows][d_v].
+// Balanced schedule: merge[e] = {slot of the entry's first piece (-1: not
+// split, written straight to the output), first slot of its later pieces,
+// number of later pieces}, written by the decode.  Fixed partitions (merge
+// == nullptr): slots e * splits .. + splits - 1.  Launched as a programmatic
+// dependent of the decode; everything it reads comes from the decode.
 template <typename T, bool kWide>
 __global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
     gqa_combine_kernel(const float *__restrict__ part_o, const float *__restrict__ part_lse,
-                       const int32_t *__restrict__ prefix, int splits, int rows, int m_q,
-                       int group, int hkv, int hq, int d_v, T *__restrict__ out, int64_t o_sb,
-                       int64_t o_sh, int64_t o_sm, float *__restrict__ lse) {
+                       const int4 *__restrict__ merge, int splits, int rows, int m_q, int group,
+                       int hkv, int hq, int d_v, T *__restrict__ out, int64_t o_sb, int64_t o_sh,
+                       int64_t o_sm, float *__restrict__ lse) {
   __shared__ MergeState states[kWide ? 8 : 1][32];
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int row_blocks = kWide ? (rows + 1) / 2 : (rows + 3) / 4;
   const int e = blockIdx.x / row_blocks, rb = blockIdx.x % row_blocks;
-  const int first = prefix ? prefix[e] : e * splits;
-  const int n = prefix ? prefix[e + 1] - first : splits;
-  if (n < 2) return;
+  int head = -1, first = e * splits, n = splits;
+  if (merge) {
+    const int4 m = merge[e];
+    if (m.x < 0) return;
+    head = m.x;
+    first = m.y;
+    n = m.z;
+  } else if (n < 2) {
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int flat = kWide ? rb * 2 + (warp >> 2) : rb * 4 + warp;
   const int j = kWide ? (warp & 3) : 0;
+  const int64_t os = static_cast<int64_t>(rows) * d_v;
   MergeState st;
-  mla_row_state<kWide>(st, part_o, part_lse, first, n, rows, flat, d_v, lane, j, warp, states);
+  st.init();
+  if (flat < rows) {
+    if (head >= 0 && j == 0)
+      fold_parts<false, 1>(st, part_o, part_lse, head, 0, 1, 1, os, rows,
+                           static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
+    fold_parts<false, 4>(st, part_o, part_lse, first, j, kWide ? 4 : 1, n, os, rows,
+                         static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
+  }
+  if (kWide) {
+    states[warp][lane] = st;
+    __syncthreads();
+    if (j == 0) {
+#pragma unroll
+      for (int k = 1; k < 4; ++k) fold_state(st, states[warp + k][lane]);
+    }
+  }
   if (j != 0 || flat >= rows) return;
   const int b = e / hkv, h = (e % hkv) * group + flat / m_q, m = flat % m_q;
   const float l = finish_row<T>(st, d_v, out + b * o_sb + h * o_sh + m * o_sm, lane);
@@ -92,7 +116,7 @@ __global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
 
 template <typename T>
 cudaError_t launch_gqa_combine_t(const float *part_o, const float *part_lse,
-                                 const int32_t *prefix, int splits, int entries, int rows,
+                                 const int4 *merge, int splits, int entries, int rows,
                                  int m_q, int group, int hkv, int hq, int d_v, bool wide,
                                  void *out, int64_t o_sb, int64_t o_sh, int64_t o_sm, float *lse,
                                  cudaStream_t stream) {
@@ -110,21 +134,21 @@ cudaError_t launch_gqa_combine_t(const float *part_o, const float *part_lse,
   cfg.numAttrs = 1;
   T *o = static_cast<T *>(out);
   if (wide)
-    return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<T, true>, part_o, part_lse, prefix, splits,
+    return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<T, true>, part_o, part_lse, merge, splits,
                               rows, m_q, group, hkv, hq, d_v, o, o_sb, o_sh, o_sm, lse);
-  return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<T, false>, part_o, part_lse, prefix, splits,
+  return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<T, false>, part_o, part_lse, merge, splits,
                             rows, m_q, group, hkv, hq, d_v, o, o_sb, o_sh, o_sm, lse);
 }
 
-cudaError_t launch_gqa_combine(const float *part_o, const float *part_lse, const int32_t *prefix,
+cudaError_t launch_gqa_combine(const float *part_o, const float *part_lse, const int4 *merge,
                                int splits, int entries, int rows, int m_q, int group, int hkv,
                                int hq, int d_v, bool wide, void *out, int dtype, int64_t o_sb,
                                int64_t o_sh, int64_t o_sm, float *lse, cudaStream_t stream) {
   if (dtype == FA_DTYPE_BF16)
-    return launch_gqa_combine_t<__nv_bfloat16>(part_o, part_lse, prefix, splits, entries, rows,
+    return launch_gqa_combine_t<__nv_bfloat16>(part_o, part_lse, merge, splits, entries, rows,
                                                m_q, group, hkv, hq, d_v, wide, out, o_sb, o_sh,
                                                o_sm, lse, stream);
-  return launch_gqa_combine_t<__half>(part_o, part_lse, prefix, splits, entries, rows, m_q, group,
+  return launch_gqa_combine_t<__half>(part_o, part_lse, merge, splits, entries, rows, m_q, group,
                                       hkv, hq, d_v, wide, out, o_sb, o_sh, o_sm, lse, stream);
 }
 

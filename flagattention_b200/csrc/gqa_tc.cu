@@ -71,6 +71,18 @@ struct Plan {
                 "swizzled tiles need 1024-byte alignment");
 };
 
+// Balanced schedule: the cost line of all entries (entry e = sequence b *
+// kv_heads + kv head; cost 1 + blocks(len_b) units, the unit before an
+// entry's blocks standing for its per-piece overhead) is cut into `parts`
+// equal shares; CTA p takes units [a0, a1) = [p T / parts, (p + 1) T / parts).
+struct Share {
+  long long a0, a1;     // this CTA's units
+  long long x_lo;       // first unit of entry e_lo
+  long long total;      // T
+  int e_lo, e_hi;       // entries overlapping [a0, a1) (e_hi < e_lo: none)
+  int parts;            // CTAs with work: min(gridDim.x, T)
+};
+
 struct Bars {
   uint64_t k_full[kMaxStages], k_empty[kMaxStages];
   uint64_t v_full[kMaxStages], v_empty[kMaxStages];
@@ -82,6 +94,8 @@ struct Bars {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
+  long long warp_sum[kThreads / 32];
+  Share share;
 };
 static_assert(sizeof(Bars) <= 1024, "barrier block");
 
@@ -95,14 +109,15 @@ struct Params {
   int32_t n_ctx;
   int32_t batch, hq, hkv, group, m_q, rows, causal;
   float scale_log2;
-  // balanced schedule (meta != nullptr): parts of the device scheduler's
-  // metadata in 128-token blocks; prefix[e] .. prefix[e + 1] - 1 are entry
-  // e's split slots.  Otherwise the reference's fixed partition: part =
-  // entry * num_splits + split, partition_size tokens each.
-  const int32_t *meta;
-  const int32_t *prefix;
-  int32_t num_parts;
-  int32_t num_splits, partition_size;
+  // num_splits == 0: the balanced schedule (Share); a split entry's pieces
+  // go to slot parts + p (its first piece, in CTA p) and slots p (every
+  // later piece, in CTA p), and the CTA holding an entry's first piece
+  // writes merge[e] = {first slot or -1 when unsplit, first later slot,
+  // number of later slots}.  num_splits >= 1: the reference's fixed
+  // partitions, part = entry * num_splits + split (partition_size tokens),
+  // taken round-robin; slot = part.
+  int32_t num_splits, partition_size, num_parts;
+  int4 *merge;
   void *o;
   int64_t o_sb, o_sh, o_sm;
   float *lse;       // nullable, [batch][hq][m_q]
@@ -113,63 +128,133 @@ struct Params {
 
 struct Piece {
   int e, b, kvh, tok0, tok_end, len, slot;
-  bool final_out;
+  bool present;     // the walk's entry has a piece in this CTA
+  bool final_out;   // written straight to the output
+  bool entry_first; // holds the entry's first block (or the entry is empty)
+  int p_lo, p_hi;   // CTAs holding the entry's first / last block (balanced)
   __device__ __forceinline__ int tiles() const {
     return tok_end > tok0 ? (tok_end - (tok0 & ~(kTileN - 1)) + kTileN - 1) / kTileN : 0;
   }
 };
 
-__device__ __forceinline__ int entry_len(const Params &p, int e) {
-  return p.seq_lens ? __ldg(p.seq_lens + e / p.hkv) : p.n_ctx;
+__device__ __forceinline__ int seq_len_of(const Params &p, int b) {
+  return p.seq_lens ? __ldg(p.seq_lens + b) : p.n_ctx;
+}
+__device__ __forceinline__ int blocks_of(int len) {
+  return len > 0 ? (len + kTileN - 1) / kTileN : 0;
 }
 
-__device__ __forceinline__ int part_pieces(const Params &p, int part) {
-  return p.meta ? __ldg(p.meta + static_cast<int64_t>(part) * FA_MLA_META_INTS + 5) : 1;
+// The CTA's share of the balanced schedule.  All threads take part: a block
+// scan of the per-sequence costs into `scan` (shared memory not yet used by
+// the TMA rings), then thread 0 locates the entries at both ends of the
+// share by binary search.  Ends with __syncthreads.
+__device__ __noinline__ void compute_share(const Params &p, long long *scan, Bars *bars) {
+  const int B = p.batch, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (B + kThreads - 1) / kThreads;
+  const int b0 = min(B, tid * per), b1 = min(B, b0 + per);
+  long long local = 0;
+  for (int b = b0; b < b1; ++b) local += 1 + blocks_of(seq_len_of(p, b));
+  long long incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) bars->warp_sum[warp] = incl;
+  __syncthreads();
+  long long run = incl - local;
+  for (int w = 0; w < warp; ++w) run += bars->warp_sum[w];
+  for (int b = b0; b < b1; ++b) {
+    scan[b] = run;
+    run += 1 + blocks_of(seq_len_of(p, b));
+  }
+  if (b1 == B && b0 < b1) scan[B] = run;
+  if (B == 0 && tid == 0) scan[0] = 0;
+  __syncthreads();
+  if (tid == 0) {
+    Share sh;
+    const long long hkv = p.hkv;
+    sh.total = hkv * scan[B];
+    sh.parts = static_cast<int>(min(static_cast<long long>(gridDim.x), sh.total));
+    sh.e_lo = 0;
+    sh.e_hi = -1;
+    sh.x_lo = sh.a0 = sh.a1 = 0;
+    if (static_cast<int>(blockIdx.x) < sh.parts) {
+      sh.a0 = blockIdx.x * sh.total / sh.parts;
+      sh.a1 = (blockIdx.x + 1) * sh.total / sh.parts;
+      // entry holding unit u: sequence b = last with hkv * scan[b] <= u
+      auto locate = [&](long long u, int &e, long long &x) {
+        int lo = 0, hi = B - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (hkv * scan[mid] <= u) lo = mid; else hi = mid - 1;
+        }
+        const long long c = scan[lo + 1] - scan[lo];
+        const long long h = (u - hkv * scan[lo]) / c;
+        e = lo * p.hkv + static_cast<int>(h);
+        x = hkv * scan[lo] + h * c;
+      };
+      long long x_hi;
+      locate(sh.a0, sh.e_lo, sh.x_lo);
+      locate(sh.a1 - 1, sh.e_hi, x_hi);
+    }
+    bars->share = sh;
+  }
+  __syncthreads();
 }
 
-// Position in the CTA's stream of pieces: part (blockIdx.x, + gridDim.x, ...)
-// and piece index i within it.
+// Position in the CTA's stream of pieces: balanced, entry e starting at unit
+// x (entries e_lo .. e_hi); fixed partitions, part (blockIdx.x, + gridDim.x,
+// ...).
 struct Cursor {
-  int part, i;
-  __device__ __forceinline__ bool valid(const Params &p) const { return part < p.num_parts; }
+  int e;
+  long long x;
+  int part;
 };
 
-__device__ __forceinline__ void settle(const Params &p, Cursor &c) {
-  while (c.part < p.num_parts && c.i >= part_pieces(p, c.part)) {
-    c.part += gridDim.x;
-    c.i = 0;
-  }
+__device__ __forceinline__ Cursor first_cursor(const Params &p, const Share *sh) {
+  return p.num_splits == 0 ? Cursor{sh->e_lo, sh->x_lo, 0}
+                           : Cursor{0, 0, static_cast<int>(blockIdx.x)};
 }
-__device__ __forceinline__ Cursor first_cursor(const Params &p) {
-  Cursor c{static_cast<int>(blockIdx.x), 0};
-  settle(p, c);
-  return c;
+__device__ __forceinline__ bool valid(const Params &p, const Share *sh, const Cursor &c) {
+  return p.num_splits == 0 ? c.e <= sh->e_hi : c.part < p.num_parts;
 }
 __device__ __forceinline__ void advance(const Params &p, Cursor &c) {
-  ++c.i;
-  settle(p, c);
+  if (p.num_splits == 0) {
+    c.x += 1 + blocks_of(seq_len_of(p, c.e / p.hkv));
+    ++c.e;
+  } else {
+    c.part += gridDim.x;
+  }
 }
 
-__device__ __noinline__ Piece get_piece(const Params &p, Cursor c) {
+__device__ __noinline__ Piece get_piece(const Params &p, const Share *sh, Cursor c) {
   Piece pc;
-  int split;
-  if (p.meta) {
-    const int32_t *m = p.meta + static_cast<int64_t>(c.part) * FA_MLA_META_INTS;
-    pc.e = __ldg(m) + c.i;
-    pc.len = max(entry_len(p, pc.e), 0);
-    const int nblk = (pc.len + kTileN - 1) / kTileN;
-    const int lo = c.i == 0 ? __ldg(m + 1) : 0;
-    const int hi = pc.e == __ldg(m + 2) ? __ldg(m + 3) : nblk;
-    pc.tok0 = lo * kTileN;
-    pc.tok_end = min(hi * kTileN, pc.len);
-    split = c.i == 0 ? __ldg(m + 4) : 0;
-    const int first = __ldg(p.prefix + pc.e);
-    pc.final_out = __ldg(p.prefix + pc.e + 1) - first == 1;
-    pc.slot = first + split;
+  if (p.num_splits == 0) {
+    pc.e = c.e;
+    pc.b = c.e / p.hkv;
+    pc.len = max(seq_len_of(p, pc.b), 0);
+    const int nb = blocks_of(pc.len);
+    // blocks of this entry inside [a0, a1): block j sits at unit x + 1 + j
+    const long long j0 = min(max(sh->a0 - c.x - 1, 0ll), static_cast<long long>(nb));
+    const long long j1 = min(max(sh->a1 - c.x - 1, 0ll), static_cast<long long>(nb));
+    pc.present = nb > 0 ? j1 > j0 : c.x >= sh->a0;
+    pc.tok0 = static_cast<int>(j0) * kTileN;
+    pc.tok_end = min(static_cast<int>(j1) * kTileN, pc.len);
+    auto part_of = [&](long long u) {
+      return static_cast<int>(min(static_cast<long long>(sh->parts - 1),
+                                  ((u + 1) * sh->parts + sh->total - 1) / sh->total - 1));
+    };
+    pc.p_lo = nb > 0 ? part_of(c.x + 1) : static_cast<int>(blockIdx.x);
+    pc.p_hi = nb > 0 ? part_of(c.x + nb) : static_cast<int>(blockIdx.x);
+    pc.entry_first = j0 == 0;
+    pc.final_out = pc.p_lo == pc.p_hi;
+    pc.slot = pc.entry_first ? sh->parts + static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x);
   } else {
     pc.e = c.part / p.num_splits;
-    split = c.part % p.num_splits;
-    pc.len = max(entry_len(p, pc.e), 0);
+    pc.b = pc.e / p.hkv;
+    const int split = c.part % p.num_splits;
+    pc.len = max(seq_len_of(p, pc.b), 0);
     if (p.num_splits == 1) {
       pc.tok0 = 0;
       pc.tok_end = pc.len;
@@ -177,17 +262,23 @@ __device__ __noinline__ Piece get_piece(const Params &p, Cursor c) {
       pc.tok0 = split * p.partition_size;
       pc.tok_end = min(pc.len, pc.tok0 + p.partition_size);
     }
+    pc.present = true;
+    pc.entry_first = split == 0;
     pc.final_out = p.num_splits == 1;
+    pc.p_lo = pc.p_hi = 0;
     pc.slot = c.part;
   }
-  pc.b = pc.e / p.hkv;
   pc.kvh = pc.e % p.hkv;
   return pc;
 }
 
 // Next piece with at least one tile (the Q buffers alternate over those).
-__device__ __forceinline__ void next_with_tiles(const Params &p, Cursor &c) {
-  while (c.valid(p) && get_piece(p, c).tiles() == 0) advance(p, c);
+__device__ __forceinline__ void next_with_tiles(const Params &p, const Share *sh, Cursor &c) {
+  while (valid(p, sh, c)) {
+    const Piece pc = get_piece(p, sh, c);
+    if (pc.present && pc.tiles() > 0) return;
+    advance(p, c);
+  }
 }
 
 // Warp-wide bounded wait: all lanes return the same verdict.
@@ -365,25 +456,27 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
   const uint32_t vbase = smem_u32(smem + PL::kOffV);
   RowSync rs{smem_u32(&bars->merge)};
 
-  Cursor cur = first_cursor(p);
-  next_with_tiles(p, cur);  // first piece that has tiles: its Q goes first
-  uint32_t g = 0;           // tiles so far
-  uint32_t k = 0;           // pieces with tiles so far
-  if (cur.valid(p))
-    write_q<T, kD>(p, get_piece(p, cur), live, g_idx, m_idx, tmem + lane_off + PL::kColQ,
+  const Share *sh = &bars->share;
+  Cursor cur = first_cursor(p, sh);
+  next_with_tiles(p, sh, cur);  // first piece that has tiles: its Q goes first
+  uint32_t g = 0;               // tiles so far
+  uint32_t k = 0;               // pieces with tiles so far
+  if (valid(p, sh, cur))
+    write_q<T, kD>(p, get_piece(p, sh, cur), live, g_idx, m_idx, tmem + lane_off + PL::kColQ,
                    smem_u32(&bars->q_full[0]), lane);
   bool ok = true;
-  for (Cursor c = first_cursor(p); c.valid(p) && ok; advance(p, c)) {
-    const Piece pc = get_piece(p, c);
+  for (Cursor c = first_cursor(p, sh); valid(p, sh, c) && ok; advance(p, c)) {
+    const Piece pc = get_piece(p, sh, c);
+    if (!pc.present) continue;
     const int n_tiles = pc.tiles();
     if (n_tiles > 0) {
       // Q of the next piece with tiles, into the other buffer: its previous
       // user (two pieces back) finished all QKs before this piece started
       Cursor nq = c;
       advance(p, nq);
-      next_with_tiles(p, nq);
-      if (nq.valid(p))
-        write_q<T, kD>(p, get_piece(p, nq), live, g_idx, m_idx,
+      next_with_tiles(p, sh, nq);
+      if (valid(p, sh, nq))
+        write_q<T, kD>(p, get_piece(p, sh, nq), live, g_idx, m_idx,
                        tmem + lane_off + PL::kColQ + ((k + 1) & 1) * (kD / 2),
                        smem_u32(&bars->q_full[(k + 1) & 1]), lane);
     }
@@ -565,6 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(&bars->merge), 4);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort_flag = 0;
+    bars->share = Share{0, 0, 0, 0, 0, -1, 0};
     fence_barrier_init();
   }
   if (warp == kProducerWarp && lane == 0) {
@@ -584,6 +678,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the merge kernel queued behind this one launch.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (p.num_splits == 0) {
+    // the rings are still empty: the schedule's scan uses their space, and
+    // the TMA writes that follow are ordered after it
+    compute_share(p, reinterpret_cast<long long *>(smem + PL::kOffK), bars);
+    fence_proxy_async_smem();
+  }
 
   if (warp < 4) {
     row_role<T, kD, kC>(p, bars, smem, tmem, warp, lane);
@@ -593,8 +693,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nbox = kTileN / p.box_rows;
     uint32_t g = 0, gk = 0, gv = 0;  // tiles begun, K tiles issued, V tiles issued
     bool ok = true;
-    for (Cursor c = first_cursor(p); c.valid(p) && ok; advance(p, c)) {
-      const Piece pc = get_piece(p, c);
+    const Share *sh = &bars->share;
+    for (Cursor c = first_cursor(p, sh); valid(p, sh, c) && ok; advance(p, c)) {
+      const Piece pc = get_piece(p, sh, c);
+      if (!pc.present) continue;
+      if (p.num_splits == 0 && pc.entry_first && lane == 0)
+        p.merge[pc.e] = make_int4(pc.final_out ? -1 : sh->parts + pc.p_lo, pc.p_lo + 1,
+                                  pc.p_hi - pc.p_lo, 0);
       const int n_tiles = pc.tiles();
       int n0 = pc.tok0 & ~(kTileN - 1);
       for (int t = 0; t < n_tiles; ++t, ++g, n0 += kTileN) {
@@ -684,8 +789,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit_warp(smem_u32(&bars->pv_done));
       return true;
     };
-    for (Cursor c = first_cursor(p); c.valid(p) && ok; advance(p, c)) {
-      const Piece pc = get_piece(p, c);
+    const Share *sh = &bars->share;
+    for (Cursor c = first_cursor(p, sh); valid(p, sh, c) && ok; advance(p, c)) {
+      const Piece pc = get_piece(p, sh, c);
+      if (!pc.present) continue;
       const int n_tiles = pc.tiles();
       if (n_tiles == 0) continue;
       if (!(ok = warp_wait(smem_u32(&bars->q_full[k & 1u]), (k >> 1) & 1u, abort_flag, p.status,
@@ -764,6 +871,15 @@ cudaError_t launch_d(const CUtensorMap &km, const CUtensorMap &vm, const Params 
 
 }  // namespace gqa
 
+int gqa_max_balanced_batch() {
+  // the scan holds batch + 1 int64 in the K and V rings (same size for both
+  // head sizes)
+  static_assert(gqa::Plan<64>::kOffStage - gqa::Plan<64>::kOffK ==
+                    gqa::Plan<128>::kOffStage - gqa::Plan<128>::kOffK,
+                "ring sizes");
+  return (gqa::Plan<128>::kOffStage - gqa::Plan<128>::kOffK) / 8 - 1;
+}
+
 size_t gqa_smem_bytes(int d) {
   return d == 64 ? gqa::Plan<64>::kSmemBytes : gqa::Plan<128>::kSmemBytes;
 }
@@ -793,12 +909,13 @@ bool gqa_tc_eligible(const fa_decode_args *a) {
   return true;
 }
 
-// Launch the decode (and, when pieces were split, the merge) for eligible
-// arguments.  Balanced schedule (a->num_splits == 0): `meta` / `prefix` were
-// written by the scheduler kernel just before on the same stream.
+// Launch the decode for eligible arguments.  Balanced schedule
+// (a->num_splits == 0): one CTA per part (grid), merge records into `merge`
+// (int4 per entry); fixed partitions: num_parts = entries * num_splits.
+// Sequences the balanced schedule can scan at once (the scan lives in the
+// rings' shared memory).
 cudaError_t launch_gqa_tc(const CUtensorMap &km, const CUtensorMap &vm, const fa_decode_args *a,
-                          const int32_t *meta, const int32_t *prefix, int num_parts, int grid,
-                          bool pdl, cudaStream_t stream) {
+                          int4 *merge, int num_parts, int grid, bool pdl, cudaStream_t stream) {
   gqa::Params p;
   p.q = a->q;
   p.q_sb = a->q_stride_b;
@@ -820,10 +937,9 @@ cudaError_t launch_gqa_tc(const CUtensorMap &km, const CUtensorMap &vm, const fa
   p.rows = p.group * a->m_q;
   p.causal = a->causal;
   p.scale_log2 = a->scale * 1.4426950408889634f;
-  p.meta = meta;
-  p.prefix = prefix;
+  p.merge = merge;
   p.num_parts = num_parts;
-  p.num_splits = a->num_splits > 0 ? a->num_splits : 1;
+  p.num_splits = a->num_splits;
   p.partition_size = a->partition_size;
   p.o = a->o;
   p.o_sb = a->o_stride_b;

@@ -1,12 +1,10 @@
-// sched.cu -- device tile scheduler for the decode kernels.
+// sched.cu -- device tile scheduler for the MLA decode kernels.
 //
 // Emits the metadata format declared in include/flagattn_b200.h: each of the
-// num_parts parts receives an equal budget of blocks (block_n tokens each)
-// plus a fixed per-piece cost, and walks the entries in order.  An entry is
-// one sequence (MLA: one latent head) or one (sequence, kv head) pair of a
-// grouped-query decode, whose length is seq_lens[entry / rep].  The loop is
-// pure integer arithmetic so it equals the host specification bit-for-bit;
-// the reference has no counterpart (its split count is one per call,
+// num_sm_parts 2-SM parts receives an equal budget of 64-token blocks plus a
+// fixed per-piece cost, and walks the sequences in order.  The loop is pure
+// integer arithmetic so it equals the host specification bit-for-bit; the
+// reference has no counterpart (its split count is one per call,
 // split_kv.py:247-276 / paged.py:54-67).
 #include "common.cuh"
 #include "flagattn_b200.h"
@@ -16,35 +14,30 @@ namespace fa {
 constexpr int kSchedThreads = 256;
 constexpr int kSchedSmemSeqs = 10240;  // sequences staged in shared memory
 
-__device__ __forceinline__ int blocks_of_len(int len, int block_n) {
-  return len > 0 ? (len + block_n - 1) / block_n : 0;
+__device__ __forceinline__ int blocks_of_len(int len) {
+  return len > 0 ? (len + FA_MLA_BLOCK_N - 1) / FA_MLA_BLOCK_N : 0;
 }
 
-// The block stages the per-entry block counts in shared memory (when the
-// entries fit), then one thread walks them (O(entries + parts) work).  An
-// entry's prefix value is written when its last piece is placed.  A decode
-// kernel launched behind this one as a programmatic dependent may start its
-// prologue at once; it waits for this grid before reading the metadata.
+// The block stages the per-sequence block counts in shared memory (when the
+// batch fits), then one thread walks the batch (O(batch + parts) work).
+// A sequence's prefix entry is written when its last piece is placed.
 __global__ void __launch_bounds__(kSchedThreads)
-    mla_metadata_kernel(const int32_t *__restrict__ seq_lens, int batch, int rep, int block_n,
-                        int fixed, int topk, int num_parts, int32_t *__restrict__ meta,
-                        int32_t *__restrict__ num_splits) {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    mla_metadata_kernel(const int32_t *__restrict__ seq_lens, int batch, int topk, int num_parts,
+                        int32_t *__restrict__ meta, int32_t *__restrict__ num_splits) {
   __shared__ int nb_s[kSchedSmemSeqs];
   __shared__ long long part_sum[kSchedThreads];
   const bool staged = batch <= kSchedSmemSeqs;
   long long local = 0;
   for (int b = threadIdx.x; b < batch; b += kSchedThreads) {
-    const int nb = blocks_of_len(topk > 0 ? topk : seq_lens[b / rep], block_n);
+    const int nb = blocks_of_len(topk > 0 ? topk : seq_lens[b]);
     if (staged) nb_s[b] = nb;
     local += nb;
   }
   part_sum[threadIdx.x] = local;
   __syncthreads();
   if (threadIdx.x != 0) return;
-  auto nblk = [&](int b) {
-    return staged ? nb_s[b] : blocks_of_len(topk > 0 ? topk : seq_lens[b / rep], block_n);
-  };
+  auto nblk = [&](int b) { return staged ? nb_s[b] : blocks_of_len(topk > 0 ? topk : seq_lens[b]); };
+  const int fixed = FA_MLA_FIXED_COST;
   long long total = static_cast<long long>(fixed) * batch;
   for (int i = 0; i < kSchedThreads; ++i) total += part_sum[i];
   num_splits[0] = 0;
@@ -97,19 +90,7 @@ __global__ void __launch_bounds__(kSchedThreads)
 
 void launch_mla_metadata(const int32_t *seq_lens, int batch, int topk, int num_parts,
                          int32_t *meta, int32_t *num_splits, cudaStream_t stream) {
-  mla_metadata_kernel<<<1, kSchedThreads, 0, stream>>>(seq_lens, batch, 1, FA_MLA_BLOCK_N,
-                                                       FA_MLA_FIXED_COST, topk, num_parts, meta,
-                                                       num_splits);
-}
-
-// Entries e = 0 .. entries-1 of length seq_lens[e / rep] (uniform_len when
-// uniform_len > 0), blocks of block_n tokens (the grouped-query decode:
-// entry = sequence * kv_heads + kv head).
-void launch_entry_metadata(const int32_t *seq_lens, int uniform_len, int entries, int rep,
-                           int block_n, int fixed, int num_parts, int32_t *meta,
-                           int32_t *num_splits, cudaStream_t stream) {
-  mla_metadata_kernel<<<1, kSchedThreads, 0, stream>>>(seq_lens, entries, rep, block_n, fixed,
-                                                       uniform_len, num_parts, meta, num_splits);
+  mla_metadata_kernel<<<1, kSchedThreads, 0, stream>>>(seq_lens, batch, topk, num_parts, meta, num_splits);
 }
 
 }  // namespace fa

@@ -22,8 +22,6 @@
  *   fa_mla_get_metadata       no reference function: the FlashMLA-style
  *                             metadata call (get_mla_metadata) that the MLA
  *                             decode path needs; format defined in this file
- *                             (fa_schedule_entries: the same scheduler for the
- *                             grouped-query decode's balanced schedule)
  *   fa_mla_decode             paged.py:208-363 generalised to the MLA shape
  *                             (576-dim latent+rope keys, values = first 512
  *                             dims of the same rows, 128 query heads sharing
@@ -226,17 +224,6 @@ int fa_mla_workspace_size(int batch, int s_q, int h_q, int d_v,
 int fa_mla_get_metadata(const int32_t *seq_lens, int batch, int topk,
                         int num_sm_parts, int32_t *tile_meta,
                         int32_t *num_splits, void *stream);
-/* The same device scheduler over generic entries: entry e has
- * seq_lens[e / rep] tokens (uniform_len tokens when seq_lens is NULL),
- * counted in blocks of block_n tokens plus fixed_cost blocks per piece.
- * meta is int32 [num_parts][FA_MLA_META_INTS] in the format above with
- * blocks of block_n tokens, prefix int32 [entries + 1].  The grouped-query
- * decode's balanced schedule is this call with entries = batch *
- * num_kv_heads, rep = num_kv_heads, block_n = 128 (its sched scratch holds
- * meta, then prefix). */
-int fa_schedule_entries(const int32_t *seq_lens, int uniform_len, int entries,
-                        int rep, int block_n, int fixed_cost, int num_parts,
-                        int32_t *meta, int32_t *prefix, void *stream);
 /* Decode kernel, then the combine kernel (queued as a programmatic
  * dependent of the decode: its launch overlaps the decode, and its blocks for
  * sequences that were not split exit before the decode ends). */

@@ -3,8 +3,9 @@
 This package restates, in numpy, the algorithms of FlagAttention's PyTorch
 reference (``src/flag_attn/testing/paged.py``, ``testing/flash.py``), its split
 merge math (``split_kv.py:198-228``, ``paged.py:416-442``), its host split
-heuristics (``paged.py:54-67``, ``split_kv.py:247-276``) and the MLA
-tile-scheduler specification the device scheduler must reproduce bit-exactly.
+heuristics (``paged.py:54-67``, ``split_kv.py:247-276``) and the MLA and
+grouped-query schedule specifications the device code must reproduce
+bit-exactly.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU legs of ``bench.py``
 may import it, and only as the checker or as the timed CPU baseline.  The
@@ -26,6 +27,7 @@ from oracle.attention import (  # noqa: F401
     paged_v2_reduce,
 )
 from oracle.sched import (  # noqa: F401
+    gqa_schedule,
     mla_schedule,
     num_splits_heuristic,
     paged_num_splits,

@@ -117,3 +117,58 @@ def mla_schedule(lens, num_parts, block_n=64, fixed=5):
     for i in range(B):
         prefix[i + 1] = prefix[i] + cnt[i]
     return meta, prefix
+
+
+def gqa_schedule(lens, hkv, parts, block_n=128):
+    """Spec of the grouped-query decode's balanced schedule (the tensor-core
+    kernel's per-CTA share; the reference has no counterpart, its split is
+    the fixed partition rule of ``paged.py:54-67``).
+
+    Entries e = b * hkv + h (sequence b, kv head h) lie on one cost line in
+    order; entry e costs 1 + blocks(len_b) units (block_n tokens per block,
+    the leading unit standing for the per-piece overhead), so its blocks sit
+    at units X(e) + 1 + j.  With T units in all and P = min(parts, T), CTA p
+    takes units [p T // P, (p + 1) T // P): the blocks there, and an empty
+    entry whose leading unit is there.  A split entry's first piece (in CTA
+    p_lo) goes to slot P + p_lo, its later pieces (CTA p) to slot p.
+
+    Returns (pieces, merge): pieces[p] lists (entry, tok0, tok_end, final,
+    slot) of CTA p; merge[e] = (first slot or -1 when unsplit, first later
+    slot, number of later pieces), as the kernel writes it.  Integer-only.
+    """
+    lens = [int(x) for x in lens]
+    B = len(lens)
+    nb = [_cdiv(x, block_n) if x > 0 else 0 for x in lens]
+    scan = [0]
+    for b in range(B):
+        scan.append(scan[-1] + 1 + nb[b])
+    T = hkv * scan[B]
+    P = min(parts, T)
+    E = B * hkv
+
+    def X(e):
+        b, h = divmod(e, hkv)
+        return hkv * scan[b] + h * (1 + nb[b])
+
+    def part_of(u):
+        return min(P - 1, ((u + 1) * P + T - 1) // T - 1)
+
+    pieces = [[] for _ in range(parts)]
+    merge = [None] * E
+    for p in range(P):
+        a0, a1 = p * T // P, (p + 1) * T // P
+        for e in range(E):
+            x, b = X(e), e // hkv
+            n = nb[b]
+            j0 = min(max(a0 - x - 1, 0), n)
+            j1 = min(max(a1 - x - 1, 0), n)
+            if not (j1 > j0 if n > 0 else a0 <= x < a1):
+                continue
+            p_lo = part_of(x + 1) if n else p
+            p_hi = part_of(x + n) if n else p
+            final = p_lo == p_hi
+            slot = -1 if final else (P + p if j0 == 0 else p)
+            pieces[p].append((e, j0 * block_n, min(j1 * block_n, max(lens[b], 0)), final, slot))
+            if j0 == 0:
+                merge[e] = (-1 if final else P + p_lo, p_lo + 1, p_hi - p_lo)
+    return pieces, merge

@@ -2,7 +2,7 @@
 
 The reference's paged test grid runs through the same kernel in
 test_gpu_generic.py; these cases pin what is specific to the tensor-core
-path: that it is the path taken, the device scheduler for (sequence, kv head)
+path: that it is the path taken, the balanced schedule of (sequence, kv head)
 entries bit-for-bit against its host specification, the copy layouts for
 1..128 query rows per kv head, value rows past a sequence end holding NaN,
 explicit and automatic split counts, causal multi-token rows on contiguous
@@ -84,28 +84,41 @@ def test_tensor_core_path_selection(d, group, block, dtype, want):
     assert _lib.lib().fa_decode_uses_tensor_cores(ctypes.byref(a)) == want
 
 
-def test_schedule_entries_bit_exact():
-    """fa_schedule_entries == oracle.mla_schedule over the repeated lengths."""
+def test_balanced_schedule_bit_exact():
+    """The merge records the kernel writes for every entry equal the host
+    specification (oracle.gqa_schedule), and the outputs match the oracle."""
     rs = np.random.RandomState(7)
     lib = _lib.lib()
-    for trial in range(30):
-        B = int(rs.randint(1, 120))
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    for trial in range(12):
+        B = int(rs.randint(1, 60))
+        group = int(rs.choice([1, 4, 8]))
         hkv = int(rs.choice([1, 2, 8]))
-        lens = rs.randint(0 if trial % 4 == 0 else 1, 9000, size=B).astype(np.int32)
-        parts = int(rs.randint(1, 150))
-        entries = B * hkv
-        meta = torch.empty((parts, 8), dtype=torch.int32, device="cuda")
-        prefix = torch.empty(entries + 1, dtype=torch.int32, device="cuda")
-        lens_d = torch.from_numpy(lens).cuda()
-        st = lib.fa_schedule_entries(ctypes.c_void_p(lens_d.data_ptr()), 0, entries, hkv, 128, 1,
-                                     parts, ctypes.c_void_p(meta.data_ptr()),
-                                     ctypes.c_void_p(prefix.data_ptr()),
-                                     ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        lens = rs.randint(0 if trial % 4 == 0 else 1, 3000, size=B).astype(np.int32)
+        lens[0] = max(int(lens[0]), 1)
+        q, k, v, lens_t, bt, scale = _paged_inputs(B, hkv * group, group, 64, 16, 3000,
+                                                   torch.float16, trial, nblocks=400,
+                                                   lens=lens.tolist())
+        out = torch.empty_like(q)
+        a = _args_for(q, k, lens_t, bt, out)
+        a.v = v.data_ptr()
+        a.num_splits = 0
+        po, pl, sc = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+        assert lib.fa_decode_workspace_size(ctypes.byref(a), ctypes.byref(po), ctypes.byref(pl),
+                                            ctypes.byref(sc)) == 0
+        assert sc.value == B * hkv * 16
+        ws = torch.empty(po.value + pl.value + sc.value, dtype=torch.uint8, device="cuda")
+        a.part_o, a.part_lse = ws.data_ptr(), ws.data_ptr() + po.value
+        a.sched = ws.data_ptr() + po.value + pl.value
+        st = lib.fa_paged_attention(ctypes.byref(a),
+                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         assert st == 0
-        want_meta, want_prefix = oracle.mla_schedule(np.repeat(lens, hkv), parts, block_n=128,
-                                                     fixed=1)
-        assert np.array_equal(meta.cpu().numpy(), np.asarray(want_meta, np.int32)), trial
-        assert np.array_equal(prefix.cpu().numpy(), np.asarray(want_prefix, np.int32)), trial
+        torch.cuda.synchronize()
+        got = ws[po.value + pl.value:].view(torch.int32).view(-1, 4)[:, :3].cpu().numpy()
+        _, merge = oracle.gqa_schedule(lens, hkv, sms)
+        assert np.array_equal(got, np.asarray(merge, np.int32)), trial
+        ref = _oracle(q, k, v, bt, lens_t, scale).to(torch.float16).float()
+        assert torch.allclose(out.float().cpu(), ref, atol=2e-3, rtol=1e-5), trial
 
 
 @pytest.mark.parametrize("hq, group", [(64, 1), (64, 8), (16, 16), (64, 32), (64, 64), (96, 96),
