@@ -28,7 +28,8 @@ __global__ void __launch_bounds__(128, 8) lse_combine_kernel(const float *__rest
 }
 
 // MLA: sequence b owns slots num_splits[b] .. num_splits[b+1]-1 of
-// part_o [slot][s_q*h_q][d_v]; a sequence of one piece was written straight to
+// part_o [slot][s_q*h_q][d_v] (partial rows in the output type T, as the decode
+// writes them); a sequence of one piece was written straight to
 // the output.  Narrow form: 128-thread blocks, one warp per row (four rows),
 // partials loaded four at a time (one round trip per four partials).  Wide
 // form (few sequences each split over many parts): 256-thread blocks, two rows,
@@ -38,7 +39,7 @@ __global__ void __launch_bounds__(128, 8) lse_combine_kernel(const float *__rest
 // decode grid to complete (griddepcontrol.wait) before reading partials.
 template <typename T, bool kWide>
 __global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
-    mla_combine_kernel(const float *__restrict__ part_o, const float *__restrict__ part_lse,
+    mla_combine_kernel(const T *__restrict__ part_o, const float *__restrict__ part_lse,
                        const int32_t *__restrict__ num_splits, int s_q, int h_q, int d_v,
                        T *__restrict__ out, int64_t o_sb, int64_t o_ss, int64_t o_sh,
                        float *__restrict__ lse) {
@@ -53,15 +54,16 @@ __global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
   const int flat = kWide ? blockIdx.x * 2 + (warp >> 2) : blockIdx.x * 4 + warp;
   const int j = kWide ? (warp & 3) : 0;
   MergeState st;
-  mla_row_state<kWide>(st, part_o, part_lse, first, n, rows, flat, d_v, lane, j, warp, states);
+  mla_row_state<kWide, T>(st, part_o, part_lse, first, n, rows, flat, d_v, lane, j, warp, states);
   if (j != 0 || flat >= rows) return;
   const int s = flat / h_q, h = flat % h_q;
-  const float l = finish_row<T>(st, d_v, out + b * o_sb + s * o_ss + h * o_sh, lane);
+  const float l = finish_row<T, T>(st, d_v, out + b * o_sb + s * o_ss + h * o_sh, lane);
   if (lane == 0) lse[(static_cast<int64_t>(b) * h_q + h) * s_q + s] = l;
 }
 
 // Grouped-query entries (entry e = sequence * kv_heads + kv head, rows r =
-// head-in-group * m_q + query token), partials part_o [slot][rows][d_v].
+// head-in-group * m_q + query token), partials part_o [slot][rows][d_v] in the
+// output type T.
 // Balanced schedule: merge[e] = {slot of the entry's first piece (-1: not
 // split, written straight to the output), first slot of its later pieces,
 // number of later pieces}, written by the decode.  Fixed partitions (merge
@@ -69,7 +71,7 @@ __global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
 // dependent of the decode; everything it reads comes from the decode.
 template <typename T, bool kWide>
 __global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
-    gqa_combine_kernel(const float *__restrict__ part_o, const float *__restrict__ part_lse,
+    gqa_combine_kernel(const T *__restrict__ part_o, const float *__restrict__ part_lse,
                        const int4 *__restrict__ merge, int splits, int rows, int m_q, int group,
                        int hkv, int hq, int d_v, T *__restrict__ out, int64_t o_sb, int64_t o_sh,
                        int64_t o_sm, float *__restrict__ lse) {
@@ -95,9 +97,9 @@ __global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
   st.init();
   if (flat < rows) {
     if (head >= 0 && j == 0)
-      fold_parts<false, 1>(st, part_o, part_lse, head, 0, 1, 1, os, rows,
+      fold_parts<false, 1, T>(st, part_o, part_lse, head, 0, 1, 1, os, rows,
                            static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
-    fold_parts<false, 4>(st, part_o, part_lse, first, j, kWide ? 4 : 1, n, os, rows,
+    fold_parts<false, 4, T>(st, part_o, part_lse, first, j, kWide ? 4 : 1, n, os, rows,
                          static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
   }
   if (kWide) {
@@ -110,7 +112,7 @@ __global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
   }
   if (j != 0 || flat >= rows) return;
   const int b = e / hkv, h = (e % hkv) * group + flat / m_q, m = flat % m_q;
-  const float l = finish_row<T>(st, d_v, out + b * o_sb + h * o_sh + m * o_sm, lane);
+  const float l = finish_row<T, T>(st, d_v, out + b * o_sb + h * o_sh + m * o_sm, lane);
   if (lse != nullptr && lane == 0) lse[(static_cast<int64_t>(b) * hq + h) * m_q + m] = l;
 }
 
@@ -133,10 +135,11 @@ cudaError_t launch_gqa_combine_t(const float *part_o, const float *part_lse,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   T *o = static_cast<T *>(out);
+  const T *po = reinterpret_cast<const T *>(part_o);
   if (wide)
-    return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<T, true>, part_o, part_lse, merge, splits,
+    return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<T, true>, po, part_lse, merge, splits,
                               rows, m_q, group, hkv, hq, d_v, o, o_sb, o_sh, o_sm, lse);
-  return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<T, false>, part_o, part_lse, merge, splits,
+  return cudaLaunchKernelEx(&cfg, gqa_combine_kernel<T, false>, po, part_lse, merge, splits,
                             rows, m_q, group, hkv, hq, d_v, o, o_sb, o_sh, o_sm, lse);
 }
 
@@ -198,10 +201,11 @@ cudaError_t launch_mla_combine_t(const float *part_o, const float *part_lse,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  const T *po = reinterpret_cast<const T *>(part_o);
   if (wide)
-    return cudaLaunchKernelEx(&cfg, mla_combine_kernel<T, true>, part_o, part_lse, num_splits, s_q,
+    return cudaLaunchKernelEx(&cfg, mla_combine_kernel<T, true>, po, part_lse, num_splits, s_q,
                               h_q, d_v, static_cast<T *>(out), o_sb, o_ss, o_sh, lse);
-  return cudaLaunchKernelEx(&cfg, mla_combine_kernel<T, false>, part_o, part_lse, num_splits, s_q,
+  return cudaLaunchKernelEx(&cfg, mla_combine_kernel<T, false>, po, part_lse, num_splits, s_q,
                             h_q, d_v, static_cast<T *>(out), o_sb, o_ss, o_sh, lse);
 }
 

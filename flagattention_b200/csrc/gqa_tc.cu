@@ -121,7 +121,7 @@ struct Params {
   void *o;
   int64_t o_sb, o_sh, o_sm;
   float *lse;       // nullable, [batch][hq][m_q]
-  float *part_o;    // [slot][rows][d]
+  void *part_o;     // [slot][rows][d], element type T
   float *part_lse;  // [slot][rows]
   int *status;
 };
@@ -366,8 +366,10 @@ __device__ __forceinline__ bool epilogue(const Params &p, const Piece &pc, bool 
     lse = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
   }
   const int h = pc.kvh * p.group + g_idx;
-  T *orow = static_cast<T *>(p.o) + pc.b * p.o_sb + h * p.o_sh + m_idx * p.o_sm;
-  float *prow = p.part_o + (static_cast<int64_t>(pc.slot) * p.rows + r) * kD;
+  // final rows go to the output, split rows to their slot; both in T
+  T *orow = pc.final_out
+                ? static_cast<T *>(p.o) + pc.b * p.o_sb + h * p.o_sh + m_idx * p.o_sm
+                : static_cast<T *>(p.part_o) + (static_cast<int64_t>(pc.slot) * p.rows + r) * kD;
 #pragma unroll 1
   for (int j = 0; j < kD / 32; ++j) {
     float v[32];
@@ -382,22 +384,15 @@ __device__ __forceinline__ bool epilogue(const Params &p, const Piece &pc, bool 
     for (int i = 0; i < 32; ++i) v[i] *= f;
     if (kC == 1) {
       if (live) {
-        if (pc.final_out) {
-          uint4 *dst = reinterpret_cast<uint4 *>(orow + 32 * j);
+        uint4 *dst = reinterpret_cast<uint4 *>(orow + 32 * j);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint4 u;
-            u.x = Elem<T>::pack2(v[8 * i], v[8 * i + 1]);
-            u.y = Elem<T>::pack2(v[8 * i + 2], v[8 * i + 3]);
-            u.z = Elem<T>::pack2(v[8 * i + 4], v[8 * i + 5]);
-            u.w = Elem<T>::pack2(v[8 * i + 6], v[8 * i + 7]);
-            dst[i] = u;
-          }
-        } else {
-          float4 *dst = reinterpret_cast<float4 *>(prow + 32 * j);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        for (int i = 0; i < 4; ++i) {
+          uint4 u;
+          u.x = Elem<T>::pack2(v[8 * i], v[8 * i + 1]);
+          u.y = Elem<T>::pack2(v[8 * i + 2], v[8 * i + 3]);
+          u.z = Elem<T>::pack2(v[8 * i + 4], v[8 * i + 5]);
+          u.w = Elem<T>::pack2(v[8 * i + 6], v[8 * i + 7]);
+          dst[i] = u;
         }
       }
     } else {
@@ -411,13 +406,11 @@ __device__ __forceinline__ bool epilogue(const Params &p, const Piece &pc, bool 
 #pragma unroll
         for (int c = 0; c < kC; ++c) sum += stage[((c * quads + q) * 32 + i) * 33 + lane];
         const int g2 = rr / p.m_q, m2 = rr % p.m_q;
-        if (pc.final_out) {
-          T *o2 = static_cast<T *>(p.o) + pc.b * p.o_sb + (pc.kvh * p.group + g2) * p.o_sh +
-                  m2 * p.o_sm;
-          o2[32 * j + lane] = Elem<T>::from_f(sum);
-        } else {
-          p.part_o[(static_cast<int64_t>(pc.slot) * p.rows + rr) * kD + 32 * j + lane] = sum;
-        }
+        T *o2 = pc.final_out
+                    ? static_cast<T *>(p.o) + pc.b * p.o_sb + (pc.kvh * p.group + g2) * p.o_sh +
+                          m2 * p.o_sm
+                    : static_cast<T *>(p.part_o) + (static_cast<int64_t>(pc.slot) * p.rows + rr) * kD;
+        o2[32 * j + lane] = Elem<T>::from_f(sum);
       }
       if (!rs.sync(abort_flag, p.status)) return false;
     }

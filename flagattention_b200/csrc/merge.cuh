@@ -1,10 +1,13 @@
 // merge.cuh -- log-sum-exp merge of one row's split partials, shared by the
-// combine kernels (combine.cu) and the in-kernel merge of the MLA decode
-// (mla_sv.cu).  Same algebra as the reference's _fwd_combine_kv_splits
-// (split_kv.py:198-228):
+// combine kernels (combine.cu) and the cross-GPU merges (exchange.cu).  Same
+// algebra as the reference's _fwd_combine_kv_splits (split_kv.py:198-228):
 //   lse = m + log(sum_s exp(lse_s - m)),  o = sum_s exp(lse_s - lse) * o_s
-// with f32 partials.  One warp per row (d_v <= 512): lane l owns the float4
-// columns 4 l + 128 k, k < 4.
+// with f32 LSEs, f32 accumulation and partial rows o_s stored as f32 or in the
+// output's 16-bit type (the decode kernels keep split rows in the output
+// type, as the reference keeps its partial O in out.dtype, paged.py:103-113,
+// or fp16, split_kv.py:311).  One warp per row (d_v <= 512).  Lane l owns
+// the columns 4 l + 128 k .. + 3 (k < 4) of f32 partials, and 8 l + 256 k ..
+// + 7 (k < 2) of 16-bit partials, so that every load is 16 bytes.
 #pragma once
 
 #include "common.cuh"
@@ -35,6 +38,24 @@ __device__ __forceinline__ float4 load_part4(const float *p) {
   return kCoherent ? __ldcg(reinterpret_cast<const float4 *>(p))
                    : __ldg(reinterpret_cast<const float4 *>(p));
 }
+// Eight 16-bit partial values (16 bytes) widened to f32.
+template <bool kCoherent, typename TP>
+__device__ __forceinline__ void load_part8(const TP *p, float4 &lo, float4 &hi) {
+  static_assert(sizeof(TP) == 2, "16-bit partials");
+  const uint4 u = kCoherent ? __ldcg(reinterpret_cast<const uint4 *>(p))
+                            : __ldg(reinterpret_cast<const uint4 *>(p));
+  const TP *h = reinterpret_cast<const TP *>(&u);
+  lo = make_float4(Elem<TP>::to_f(h[0]), Elem<TP>::to_f(h[1]), Elem<TP>::to_f(h[2]),
+                   Elem<TP>::to_f(h[3]));
+  hi = make_float4(Elem<TP>::to_f(h[4]), Elem<TP>::to_f(h[5]), Elem<TP>::to_f(h[6]),
+                   Elem<TP>::to_f(h[7]));
+}
+
+// Column of the calling lane's accumulator k (0..3), for partials of type TP.
+template <typename TP>
+__device__ __forceinline__ int acc_col(int lane, int k) {
+  return sizeof(TP) == 4 ? lane * 4 + k * 128 : lane * 8 + (k >> 1) * 256 + (k & 1) * 4;
+}
 
 // Running state of a row's merge: maximum m of the LSEs folded so far, sum z
 // of exp(lse_s - m), and sum of exp(lse_s - m) * o_s (lane l's four float4
@@ -56,8 +77,8 @@ struct MergeState {
 // group's LSEs and value rows are all loaded before any is used, and the
 // groups are folded with a running maximum, so a warp waits for one memory
 // round trip per group instead of one for the LSEs and then one per partial.
-template <bool kCoherent, int kGroup = 2>
-__device__ __forceinline__ void fold_parts(MergeState &st, const float *__restrict__ part_o,
+template <bool kCoherent, int kGroup = 2, typename TP = float>
+__device__ __forceinline__ void fold_parts(MergeState &st, const TP *__restrict__ part_o,
                                            const float *__restrict__ part_lse, int first_slot,
                                            int s0, int step, int n, int64_t o_slot_stride,
                                            int64_t lse_slot_stride, int64_t o_row_off,
@@ -70,12 +91,21 @@ __device__ __forceinline__ void fold_parts(MergeState &st, const float *__restri
       const bool live = s + g * step < n;
       const int64_t slot = first_slot + s + g * step;
       ls[g] = live ? load_part<kCoherent>(part_lse + slot * lse_slot_stride + lse_row) : -INFINITY;
-      const float *src = part_o + slot * o_slot_stride + o_row_off;
+      const TP *src = part_o + slot * o_slot_stride + o_row_off;
+      if constexpr (sizeof(TP) == 4) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int d = lane * 4 + k * 128;
-        v[g][k] = (live && d < d_v) ? load_part4<kCoherent>(src + d)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < 4; ++k) {
+          const int d = lane * 4 + k * 128;
+          v[g][k] = (live && d < d_v) ? load_part4<kCoherent>(src + d)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int d = lane * 8 + k * 256;
+          v[g][2 * k] = v[g][2 * k + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (live && d < d_v) load_part8<kCoherent>(src + d, v[g][2 * k], v[g][2 * k + 1]);
+        }
       }
     }
     float mg = st.m;
@@ -133,21 +163,21 @@ __device__ __forceinline__ void fold_state(MergeState &a, const MergeState &b) {
 //     in warp w0.  Wide spreads one row's partials over four warps: for a few
 //     sequences split over many parts (one long sequence over 37 parts) the
 //     GPU has few rows but many partials per row.
-template <bool kWide>
-__device__ __forceinline__ void mla_row_state(MergeState &st, const float *__restrict__ part_o,
+template <bool kWide, typename TP = float>
+__device__ __forceinline__ void mla_row_state(MergeState &st, const TP *__restrict__ part_o,
                                               const float *__restrict__ part_lse, int first, int n,
                                               int rows, int flat, int d_v, int lane, int j,
                                               int warp, MergeState (*states)[32]) {
   st.init();
   if (!kWide) {
     if (flat < rows)
-      fold_parts<false, 4>(st, part_o, part_lse, first, 0, 1, n,
+      fold_parts<false, 4, TP>(st, part_o, part_lse, first, 0, 1, n,
                            static_cast<int64_t>(rows) * d_v, rows,
                            static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
     return;
   }
   if (flat < rows && j < n)
-    fold_parts<false, 4>(st, part_o, part_lse, first, j, 4, n, static_cast<int64_t>(rows) * d_v,
+    fold_parts<false, 4, TP>(st, part_o, part_lse, first, j, 4, n, static_cast<int64_t>(rows) * d_v,
                          rows, static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
   states[warp][lane] = st;
   __syncthreads();
@@ -157,14 +187,15 @@ __device__ __forceinline__ void mla_row_state(MergeState &st, const float *__res
   }
 }
 
-// Normalised output row and merged LSE of a state.
-template <typename T>
+// Normalised output row and merged LSE of a state whose partials had type TP
+// (which fixes the lane's columns, acc_col).
+template <typename T, typename TP = float>
 __device__ __forceinline__ float finish_row(const MergeState &st, int d_v, T *out, int lane) {
   const float lse = (st.z > 0.f) ? st.m + __logf(st.z) : -INFINITY;
   const float inv = (st.z > 0.f) ? 1.f / st.z : 0.f;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int d = lane * 4 + k * 128;
+    const int d = acc_col<TP>(lane, k);
     const float4 o = make_float4(st.acc[k].x * inv, st.acc[k].y * inv, st.acc[k].z * inv,
                                  st.acc[k].w * inv);
     if (d < d_v) store4<T>(out + d, o);

@@ -291,8 +291,8 @@ struct OutRows {
   uint8_t *base;
   int64_t sb, ss, sh;  // final output strides (elements); split: row stride
   int b, h_q, row0, n_rows;
-  int esz;             // bytes per output element
-  bool split;          // f32 split workspace row (slot * rows_total + flat) * d_v
+  int esz;             // bytes per element (output type; split rows use it too)
+  bool split;          // split workspace row (slot * rows_total + flat) * d_v
   int64_t split_row0;  // slot * rows_total
   int d_v;
 };
@@ -311,7 +311,7 @@ __device__ __noinline__ void write_o_half(uint32_t trow, int ch, int q4, int lan
       const int st_ = fl / o.h_q, hh = fl % o.h_q;
       row_off[k] = (o.b * o.sb + st_ * o.ss + hh * o.sh) * o.esz;
     } else {
-      row_off[k] = (o.split_row0 + fl) * o.d_v * 4;
+      row_off[k] = (o.split_row0 + fl) * o.d_v * o.esz;
     }
   }
   const int cols_it = 128 / o.esz;  // output dims per 128-byte row segment
@@ -1128,7 +1128,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (!ok) break;
           tc_fence_after();
         }
-        // O / l -> out (final) or the f32 split workspace
+        // O / l -> out (final) or the split workspace, in the output type:
+        // half the bytes of f32 partials for a bf16 / f16 output, the same
+        // rounding the reference applies to its partial O (out.dtype,
+        // paged.py:103-113)
         const bool final_out = n_split == 1;
         OutRows o;
         o.base = final_out ? static_cast<uint8_t *>(p.out) : reinterpret_cast<uint8_t *>(p.part_o);
@@ -1139,7 +1142,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         o.h_q = p.h_q;
         o.row0 = row0;
         o.n_rows = n_rows;
-        o.esz = (!final_out || p.out_f32) ? 4 : 2;
+        o.esz = p.out_f32 ? 4 : 2;
         o.split = !final_out;
         o.split_row0 = static_cast<int64_t>(slot_o) * rows_total;
         o.d_v = p.d_v;

@@ -113,7 +113,9 @@ int fa_split_kv_num_splits(int batch, int heads, int m, int n, int block_m,
  *    gets the same work; needs `sched`); num_splits >= 1 keeps the
  *    reference's fixed partitions of partition_size tokens.
  *  - the CUDA-core kernel for every other shape (num_splits >= 1).
- * With splits, partials go to part_o / part_lse and are merged in place.
+ * With splits, partials go to part_o / part_lse and are merged in place
+ * (part_lse f32; part_o f32 for the CUDA-core kernel, rows in the input type
+ * for the tensor-core kernel).
  * fa_decode_workspace_size gives the bytes of part_o, part_lse and sched for
  * the kernel the arguments select (zero when nothing is split). */
 typedef struct fa_decode_args {
@@ -200,7 +202,9 @@ typedef struct fa_mla_args {
   void *out;
   int64_t o_stride_b, o_stride_s, o_stride_h;
   float *lse;
-  float *part_o;   /* f32 [batch + num_sm_parts][s_q*h_q][d_v] */
+  float *part_o;   /* [batch + num_sm_parts][s_q*h_q][d_v] in the output
+                      type (bf16 / f16 / f32); sized for f32 by
+                      fa_mla_workspace_size                       */
   float *part_lse; /* f32 [batch + num_sm_parts][s_q*h_q]      */
   int32_t batch, s_q, h_q, d_qk, d_v;
   int32_t causal;
