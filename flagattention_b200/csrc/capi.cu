@@ -102,19 +102,22 @@ int encode_map(CUtensorMap *map, const void *base, int dtype, uint64_t d, uint64
   return FA_OK;
 }
 
-// 4-D map {d, rows, heads, groups} with a {64, box_rows, 1, 1} box and the
-// 128-byte swizzle: a grouped-query cache, paged ([pages][kv heads][page][d]
-// or any strides) or contiguous ([batch][kv heads][n][d] or any strides).
+// 4-D map {d, rows, heads, groups} with a {64, box_rows, box_heads, 1} box
+// and the 128-byte swizzle: a grouped-query cache, paged ([pages][kv heads]
+// [page][d] or any strides) or contiguous ([batch][kv heads][n][d] or any
+// strides); also the MLA value view, where "heads" are the 64-dim chunks of a
+// latent row (stride 64 elements) so that one box brings rows x 512 dims laid
+// out chunk by chunk.
 int encode_map4(CUtensorMap *map, const void *base, int dtype, uint64_t d, uint64_t rows,
                 uint64_t heads, uint64_t groups, int64_t row_stride, int64_t head_stride,
-                int64_t group_stride, uint32_t box_rows) {
+                int64_t group_stride, uint32_t box_rows, uint32_t box_heads = 1) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[4] = {d, rows, heads, groups};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(row_stride) * 2,
                            static_cast<cuuint64_t>(head_stride) * 2,
                            static_cast<cuuint64_t>(group_stride) * 2};
-  cuuint32_t box[4] = {64, box_rows, 1, 1};
+  cuuint32_t box[4] = {64, box_rows, box_heads, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   CUresult r = enc(map, dtype == FA_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                               : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
@@ -577,8 +580,10 @@ int fa_mla_decode_partial(const fa_mla_args *a, void *stream) {
   st = encode_map(&km, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
                   a->kv_stride_page, bn, 64);
   if (st != FA_OK) return st;
-  st = encode_map(&vm, a->kcache, a->dtype, 576, kv_rows, kv_groups, a->kv_stride_tok,
-                  a->kv_stride_page, 32, 64);
+  // values: {64 dims, rows, 9 chunks of 64 dims, pages}; one 32-row x 8-chunk
+  // box (32 KB) fills a whole value stage, [chunk][row][64 dims]
+  st = encode_map4(&vm, a->kcache, a->dtype, 64, kv_rows, 576 / 64, kv_groups, a->kv_stride_tok,
+                   64, a->kv_stride_page, 32, 8);
   if (st != FA_OK) return st;
   if (sparse) {
     const bool uniform_rows =

@@ -26,7 +26,7 @@
 // tcgen05.cp), warps 4-11 softmax (two warps per 32 query rows, one per
 // 64-token block of the tile).
 // Value CTA (512 threads): warp 0 TMA producer (V in 32-token stages of
-// 8 x 4 KB), warp 1 MMA issuer, warps 4-11 O rescaling, tail clearing and the
+// 8 chunks x 4 KB, one TMA box per stage), warp 1 MMA issuer, warps 4-11 O rescaling, tail clearing and the
 // epilogue (two warps per 32 rows, one per 256 output dims; stores staged
 // through shared memory so that each store instruction writes whole rows).
 // Top-k instance (kSparse): rows come from index lists with tile::gather4,
@@ -972,10 +972,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               if (!ok) break;
               const uint32_t full = smem_u32(&bars->v_full[st]);
               mbar_arrive_expect_tx(full, kVStageBytes);
-#pragma unroll
-              for (int d = 0; d < 8; ++d)
-                tma_load_3d(vbase + st * kVStageBytes + d * kVChunkBytes, &v_map, full, 64 * d,
-                            c1 + kVRows * j, c2);
+              // one box: 32 rows x the 8 value chunks, laid out chunk by chunk
+              tma_load_4d(vbase + st * kVStageBytes, &v_map, full, 0, c1 + kVRows * j, 0, c2);
             }
           }
         }
@@ -1177,8 +1175,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 
 // q_map: query (box 64 dims x 128 rows), kv_map: key rows (box 64 x 64),
-// v_map: value rows (box 64 x 32); all 128-byte swizzle over the same layouts
-// as the reference's caches ([pages, page, 1, 576]).
+// v_map: value rows ({64 dims, rows, 64-dim chunks, pages} with a box of 32
+// rows x 8 chunks); all 128-byte swizzle over the same layouts as the
+// reference's caches ([pages, page, 1, 576]).
 namespace {
 template <typename T, bool kSparse>
 cudaError_t launch_sv_t(const CUtensorMap &qm, const CUtensorMap &km, const CUtensorMap &vm,
