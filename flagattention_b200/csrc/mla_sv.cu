@@ -69,8 +69,8 @@ constexpr int kOffData = 1024;
 constexpr int kOffQRope = kOffData;                         // 2 x 16 KB
 constexpr int kOffRing = kOffQRope + 2 * kChunkBytes;       // 9 x 16 KB
 constexpr int kOffRed = kOffRing + kRing * kChunkBytes;     // 2 KB row maxima / sums
-constexpr int kOffStgP = kOffRed + 2048;                    // 2 x 16 KB P staging
-constexpr int kSmemScore = kOffStgP + 2 * kPBytes;
+constexpr int kOffStgP = kOffRed + 2048;                    // 2 x 18 KB P + metadata staging
+constexpr int kSmemScore = kOffStgP + 2 * kPSlotBytes;
 // value CTA
 constexpr int kOffV = kOffData;                             // 3 x 32 KB
 constexpr int kOffP = kOffV + kVStages * kVStageBytes;      // 4 x 18 KB
@@ -104,6 +104,13 @@ struct Bars {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
+  // teardown accounting of the P transfers (see the teardown): score CTA, the
+  // last block sent into each value slot (-1: none); value CTA, the same
+  // numbers received from the score CTA, and the blocks its PV issuer armed /
+  // saw land
+  int sent_seq[kPSlots];
+  int peer_sent[kPSlots];
+  int armed_upto, done_upto;
   // sparse: per tile (g % 4), one byte per 4-row group with the invalid-index
   // bits of its key rows (row 4 group + j: bit j)
   alignas(16) uint8_t inval[4][32];
@@ -429,6 +436,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(&bars->o_empty), 256);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort_flag = 0;
+    for (int i = 0; i < kPSlots; ++i) bars->sent_seq[i] = bars->peer_sent[i] = -1;
+    bars->armed_upto = bars->done_upto = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -824,20 +833,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           f32x2_split(ps2[0], s0, s1);
           f32x2_split(ps2[1], s2, s3);
           l_half = l_half * alpha + ((s0 + s1) + (s2 + s3));
+          // A piece's last tile: the row sum of both blocks (through this
+          // tile's parity slot, once the partner has read the tile maximum);
+          // 1 / row sum and the piece's LSE (natural log of the scaled row sum)
+          // travel with the piece's last block, so that the value CTA writes
+          // the piece's output and LSE together.
+          float inv_l = 0.f, lse_piece = -INFINITY;
+          if (last) {
+            if (!(ok = pair_sync())) break;
+            rslot[ch * kRows + t] = l_half;
+            if (!(ok = pair_sync())) break;
+            l_run = l_half + rslot[(ch ^ 1) * kRows + t];
+            const float msr = (m_run == -INFINITY) ? 0.f : m_run;
+            lse_piece = l_run > 0.f ? msr * 0.69314718055994531f + logf(l_run) : -INFINITY;
+            inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+          }
           // P of this warp's block -> the value CTA's slot (gb + ch) % kPSlots
           const uint32_t pb = gb + ch;
           const uint32_t pslot = pb % kPSlots;
           const uint32_t pdst = p_remote + pslot * kPSlotBytes;
           const uint32_t pbar = pfull_remote + pslot * 8;
           if (ch < n_blk) {
-            // The block's 16 KB of P is staged in local shared memory (buffer
-            // pb & 1) and sent with one bulk copy: 1024 separate 16-byte
-            // remote stores per block crowd the memory-instruction queues
-            // that the producer's and MMA warp's instructions also use.
-            // The staging buffer was last sent for block pb - 2, whose PV has
-            // finished once p_free of its slot has (its copy had landed).
-            // (Relaying the copy's arrival back from the value CTA instead
-            // measured no faster: this wait is not what paces the pair.)
+            // The block's P (16 KB) and its metadata (O rescale factors and
+            // flags with a tile's first block, 1 / row sum and LSE with a
+            // piece's last block) are staged in local shared memory (buffer
+            // pb & 1, laid out like the value CTA's slot) and sent as ONE bulk
+            // copy of the whole slot (kPSlotBytes): one transfer per block,
+            // issued by one thread, which the teardown can account for
+            // exactly.  Separate 16-byte remote stores per row crowd the
+            // memory-instruction queues that the producer's and MMA warp's
+            // instructions also use.  The staging buffer was last sent for
+            // block pb - 2, whose PV has finished once p_free of its slot has
+            // (its copy had landed).  (Relaying the copy's arrival back from
+            // the value CTA instead measured no faster: this wait is not what
+            // paces the pair.)
             ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->p_free[pslot]),
                                                    ((pb / kPSlots) & 1) ^ 1, abort_flag, p.status,
                                                    kDevTimeoutSoftmax));
@@ -846,47 +875,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                                      ((pb - 2) / kPSlots) & 1, abort_flag,
                                                      p.status, kDevTimeoutSoftmax));
             if (!ok) break;
-            const uint32_t stg = s_base + kOffStgP + (pb & 1) * kPBytes;
+            const uint32_t stg = s_base + kOffStgP + (pb & 1) * kPSlotBytes;
 #pragma unroll
             for (int u = 0; u < 8; ++u)
               asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
                                stg + t * kRowBytes + ((u ^ (t & 7)) << 4)),
                            "r"(pk[4 * u]), "r"(pk[4 * u + 1]), "r"(pk[4 * u + 2]), "r"(pk[4 * u + 3])
                            : "memory");
+            if (ch == 0) {
+              const bool any = __any_sync(0xffffffffu, rescale);
+              asm volatile("st.shared.f32 [%0], %1;" ::"r"(stg + kMetaAlpha + 4 * t),
+                           "f"(rescale ? alpha : 1.f)
+                           : "memory");
+              if (lane == 0)
+                asm volatile("st.shared.u32 [%0], %1;" ::"r"(stg + kMetaFlags + 4 * q4),
+                             "r"(any ? 1u : 0u)
+                             : "memory");
+            }
+            if (last && ch == n_blk - 1) {
+              asm volatile("st.shared.f32 [%0], %1;" ::"r"(stg + kMetaInvL + 4 * t), "f"(inv_l)
+                           : "memory");
+              asm volatile("st.shared.f32 [%0], %1;" ::"r"(stg + kMetaLse + 4 * t), "f"(lse_piece)
+                           : "memory");
+            }
             fence_proxy_async_smem();  // generic-proxy writes -> the bulk copy's reads
             mbar_arrive(smem_u32(&bars->stg_ready[ch]));
             if (t == 0) {
               if (!mbar_wait(smem_u32(&bars->stg_ready[ch]), stg_uses[ch] & 1, abort_flag,
-                             p.status, kDevTimeoutSoftmax))
+                             p.status, kDevTimeoutSoftmax)) {
                 ok = false;
-              else
-                bulk_copy_to_peer(pdst, stg, kPBytes, pbar);
+              } else {
+                bulk_copy_to_peer(pdst, stg, kPSlotBytes, pbar);
+                *reinterpret_cast<volatile int *>(&bars->sent_seq[pslot]) = static_cast<int>(pb);
+              }
             }
             ++stg_uses[ch];
             if (!(ok = __all_sync(0xffffffffu, ok))) break;
-            if (ch == 0) {
-              st_async_u32(pdst + kMetaAlpha + 4 * t, __float_as_uint(rescale ? alpha : 1.f), pbar);
-              const bool any = __any_sync(0xffffffffu, rescale);
-              if (lane == 0) st_async_u32(pdst + kMetaFlags + 4 * q4, any ? 1u : 0u, pbar);
-            }
-          }
-          if (last) {
-            // row sum = both blocks' sums (through this tile's parity slot,
-            // once the partner has read the tile maximum)
-            if (!(ok = pair_sync())) break;
-            rslot[ch * kRows + t] = l_half;
-            if (!(ok = pair_sync())) break;
-            l_run = l_half + rslot[(ch ^ 1) * kRows + t];
-            if (ch == n_blk - 1) {
-              // 1 / row sum and the piece's LSE (natural log of the scaled
-              // row sum) travel with the piece's last block: the value CTA
-              // writes the piece's output and LSE together
-              const float ms = (m_run == -INFINITY) ? 0.f : m_run;
-              const float lse = l_run > 0.f ? ms * 0.69314718055994531f + logf(l_run) : -INFINITY;
-              st_async_u32(pdst + kMetaInvL + 4 * t, __float_as_uint(l_run > 0.f ? 1.f / l_run : 0.f),
-                           pbar);
-              st_async_u32(pdst + kMetaLse + 4 * t, __float_as_uint(lse), pbar);
-            }
           }
           gb += n_blk;
         }
@@ -1000,6 +1024,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, p.status, kDevTimeoutMma)) != 0;
       };
       uint32_t vs = 0, gb = 0;
+      uint32_t armed = 0, landed = 0;  // P blocks armed / seen complete (teardown accounting)
       int pi = 0;
       bool ok = true;
       for (int i = 0; i < n_pieces && ok; ++i) {
@@ -1009,18 +1034,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int bt = pc.tok0; bt < pc.tok_end && ok; bt += kBlk, ++gb) {
           const int vb = min(kBlk, pc.tok_end - bt);
           const int n_sub = vb > kVRows ? 2 : 1;
-          const bool tile_first = ((bt - pc.tok0) & (2 * kBlk - 1)) == 0;
-          const bool piece_last = bt + kBlk >= pc.tok_end;
           const uint32_t ps = gb % kPSlots;
           const uint32_t ph = (gb / kPSlots) & 1;
-          if (lane == 0)
-            mbar_arrive_expect_tx(smem_u32(&bars->p_full[ps]),
-                                  kPBytes + (tile_first ? 512 + 16 : 0) + (piece_last ? 1024 : 0));
+          // every block arrives as one copy of the whole slot (P + metadata)
+          if (lane == 0) mbar_arrive_expect_tx(smem_u32(&bars->p_full[ps]), kPSlotBytes);
+          armed = gb + 1;
           ok = wait(smem_u32(&bars->p_full[ps]), ph);
+          if (ok) landed = gb + 1;
           ok = ok && wait(smem_u32(&bars->m_read[ps]), ph);
           if (ok && first_blk) ok = wait(smem_u32(&bars->o_empty), (pi & 1) ^ 1);
           if (!ok) break;
-          fence_proxy_async_smem();  // st.async / cleared rows -> tensor-core reads
+          fence_proxy_async_smem();  // cleared value rows -> tensor-core reads
           tc_fence_after();
           const uint64_t pa = p_desc + static_cast<uint64_t>((ps * kPSlotBytes) >> 4);
           for (int j = 0; j < n_sub; ++j, ++vs) {
@@ -1045,6 +1069,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           first_blk = false;
         }
         ++pi;
+      }
+      if (lane == 0) {
+        bars->armed_upto = static_cast<int>(armed);
+        bars->done_upto = static_cast<int>(landed);
       }
       tc_commit_warp(smem_u32(&bars->drain));
       volatile int never = 0;
@@ -1162,8 +1190,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 
   // -------------------------------------------------------------- teardown
+  // No P transfer may still be in flight when either CTA exits (after a
+  // bounded wait gave up, the roles unwind at different points).  The score
+  // CTA sends block b into slot b % kPSlots only after block b - kPSlots was
+  // consumed, so per slot at most one sent block can be unconsumed: the last
+  // one sent (sent_seq).  The score CTA hands those numbers over; the value
+  // CTA arms (when its PV issuer had not) and waits for each of them, so every
+  // copy issued has landed -- and has finished reading the score CTA's
+  // staging buffer -- before the second cluster barrier lets the pair go.
+  // Without a time-out every sent block was consumed and nothing is waited.
   tc_fence_before();
   __syncthreads();
+  if (rank == 0 && threadIdx.x == 0) {
+    for (int i = 0; i < kPSlots; ++i)
+      asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(
+                       map_to_rank(smem_u32(&bars->peer_sent[i]), 1)),
+                   "r"(static_cast<uint32_t>(
+                       *reinterpret_cast<volatile int *>(&bars->sent_seq[i])))
+                   : "memory");
+  }
+  cluster_sync();
+  if (rank == 1 && threadIdx.x == 0) {
+    volatile int never = 0;
+    const int done = bars->done_upto, armed = bars->armed_upto;
+    for (int i = 0; i < kPSlots; ++i) {
+      const int b = *reinterpret_cast<volatile int *>(&bars->peer_sent[i]);
+      if (b < done) continue;  // consumed (or nothing sent into this slot)
+      const uint32_t bar = smem_u32(&bars->p_full[i]);
+      if (b >= armed) mbar_arrive_expect_tx(bar, kPSlotBytes);
+      mbar_wait(bar, (static_cast<uint32_t>(b) / kPSlots) & 1u, &never, p.status, kDevTimeoutDrain);
+    }
+  }
   cluster_sync();  // the peer no longer touches this CTA's shared memory
   if (warp == 1) {
     tc_fence_after();
