@@ -19,6 +19,10 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 OBJDIR = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libflagattn_b200.so")
+# The abort-path test library: the same objects except the MLA decode, built
+# with FA_DEBUG_ABORT_TEST (short wait limit, one lost barrier arrival).  Only
+# tests/test_gpu_abort.py loads it, in a child process.
+ABORT_TEST_LIB = os.path.join(PKG, "libflagattn_b200_aborttest.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
@@ -42,15 +46,18 @@ def _deps():
 
 
 def up_to_date():
-    if not os.path.exists(LIB):
-        return False
-    t = os.path.getmtime(LIB)
-    return all(os.path.getmtime(d) <= t for d in _deps())
+    for lib in (LIB, ABORT_TEST_LIB):
+        if not os.path.exists(lib):
+            return False
+        t = os.path.getmtime(lib)
+        if not all(os.path.getmtime(d) <= t for d in _deps()):
+            return False
+    return True
 
 
-def _compile(src, verbose_ptxas):
-    obj = os.path.join(OBJDIR, os.path.basename(src) + ".o")
-    cmd = [_nvcc(), *ARCH, *FLAGS, "-c", src, "-o", obj]
+def _compile(src, verbose_ptxas, defines=(), suffix=""):
+    obj = os.path.join(OBJDIR, os.path.basename(src) + suffix + ".o")
+    cmd = [_nvcc(), *ARCH, *FLAGS, *[f"-D{d}" for d in defines], "-c", src, "-o", obj]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -65,17 +72,22 @@ def build(force=False, verbose_ptxas=False):
         return LIB
     os.makedirs(OBJDIR, exist_ok=True)
     srcs = _sources()
-    with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
-        results = list(ex.map(lambda s: _compile(s, verbose_ptxas), srcs))
+    mla = os.path.join(CSRC, "mla_sv.cu")
+    jobs = [(s, (), "") for s in srcs] + [(mla, ("FA_DEBUG_ABORT_TEST",), ".aborttest")]
+    with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, len(jobs))) as ex:
+        results = list(ex.map(lambda j: _compile(j[0], verbose_ptxas, j[1], j[2]), jobs))
     if verbose_ptxas:
-        for _, log in results:
+        for _, log in results[:len(srcs)]:
             sys.stderr.write(log)
-    tmp = LIB + ".tmp"
-    cmd = [_nvcc(), *ARCH, "-shared", "-o", tmp, *[o for o, _ in results], "-lcuda"]
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if r.returncode != 0:
-        raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    os.replace(tmp, LIB)
+    objs = [o for o, _ in results[:len(srcs)]]
+    test_objs = [results[-1][0] if o.endswith("mla_sv.cu.o") else o for o in objs]
+    for lib, parts in ((LIB, objs), (ABORT_TEST_LIB, test_objs)):
+        tmp = lib + ".tmp"
+        cmd = [_nvcc(), *ARCH, "-shared", "-o", tmp, *parts, "-lcuda"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+        os.replace(tmp, lib)
     return LIB
 
 

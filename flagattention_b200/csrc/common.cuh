@@ -30,7 +30,13 @@ enum DeviceStatus : int {
 // the CTA's abort flag and the device status word, and the kernel unwinds.
 // The SM-local cycle counter is read instead of %globaltimer because it costs
 // a few cycles where the global timer costs hundreds, on every slow wait.
+#ifdef FA_DEBUG_ABORT_TEST
+// The abort-path test build (never the shipped library): waits give up after
+// about 10 ms so that the test's lost arrival unwinds quickly.
+constexpr long long kWaitLimitCycles = 20000000ll;
+#else
 constexpr long long kWaitLimitCycles = 4000000000ll;
+#endif
 
 template <typename T> struct Elem;
 template <> struct Elem<__nv_bfloat16> {

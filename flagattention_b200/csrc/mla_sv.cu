@@ -62,6 +62,9 @@ constexpr int kPSlotBytes = kPBytes + 2048;         // 18 KB
 constexpr int kPSlots = 4;
 constexpr uint32_t kColQ = 0, kColS = 256, kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;           // log2 units (factor 256)
+#ifdef FA_DEBUG_ABORT_TEST
+constexpr uint32_t kAbortTestBlock = 6;             // P block whose m_read arrival is lost
+#endif
 
 constexpr int kOffBar = 0;
 constexpr int kOffData = 1024;
@@ -1142,6 +1145,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             fence_proxy_async_smem();
           }
           tc_fence_before();
+#ifdef FA_DEBUG_ABORT_TEST
+          // the abort-path test build: block kAbortTestBlock's metadata-read
+          // arrival is lost, so the PV issuer's wait for it runs out while
+          // the score CTA still has later blocks in flight (teardown drain)
+          if (gb != kAbortTestBlock)
+#endif
           mbar_arrive(smem_u32(&bars->m_read[ps]));
           vs += n_sub;
         }
