@@ -31,14 +31,15 @@ __global__ void __launch_bounds__(128, 8) lse_combine_kernel(const float *__rest
 // part_o [slot][s_q*h_q][d_v] (partial rows in the output type T, as the decode
 // writes them); a sequence of one piece was written straight to
 // the output.  Narrow form: 128-thread blocks, one warp per row (four rows),
-// partials loaded four at a time (one round trip per four partials).  Wide
+// partials loaded two at a time (one round trip per two partials; most rows
+// have two, and the smaller register footprint keeps eight blocks per SM).  Wide
 // form (few sequences each split over many parts): 256-thread blocks, two rows,
 // four warps per row (mla_row_state).  Launched as a programmatic dependent of
 // the decode kernel: its launch overlaps the decode, blocks of unsplit
 // sequences exit while the decode still runs, and the others wait for the
 // decode grid to complete (griddepcontrol.wait) before reading partials.
 template <typename T, bool kWide>
-__global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
+__global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 8)
     mla_combine_kernel(const T *__restrict__ part_o, const float *__restrict__ part_lse,
                        const int32_t *__restrict__ num_splits, int s_q, int h_q, int d_v,
                        T *__restrict__ out, int64_t o_sb, int64_t o_ss, int64_t o_sh,
@@ -99,7 +100,7 @@ __global__ void __launch_bounds__(kWide ? 256 : 128, kWide ? 2 : 4)
     if (head >= 0 && j == 0)
       fold_parts<false, 1, T>(st, part_o, part_lse, head, 0, 1, 1, os, rows,
                            static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
-    fold_parts<false, 4, T>(st, part_o, part_lse, first, j, kWide ? 4 : 1, n, os, rows,
+    fold_parts<false, 2, T>(st, part_o, part_lse, first, j, kWide ? 4 : 1, n, os, rows,
                          static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
   }
   if (kWide) {

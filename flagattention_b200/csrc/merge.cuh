@@ -171,7 +171,7 @@ __device__ __forceinline__ void mla_row_state(MergeState &st, const TP *__restri
   st.init();
   if (!kWide) {
     if (flat < rows)
-      fold_parts<false, 4, TP>(st, part_o, part_lse, first, 0, 1, n,
+      fold_parts<false, 2, TP>(st, part_o, part_lse, first, 0, 1, n,
                            static_cast<int64_t>(rows) * d_v, rows,
                            static_cast<int64_t>(flat) * d_v, flat, d_v, lane);
     return;
