@@ -8,9 +8,9 @@
 //
 //   * one persistent CTA per SM walks "pieces": a token range of one entry
 //     (entry = sequence * kv_heads + kv head); with the balanced schedule a
-//     CTA owns one part of the device scheduler's metadata (sched.cu), with
-//     an explicit split count it takes the reference's fixed partitions
-//     round-robin;
+//     CTA cuts its own equal share of all entries' key blocks out of the
+//     sequence lengths (compute_share), with an explicit split count it
+//     takes the reference's fixed partitions round-robin;
 //   * K and V tiles of 128 tokens arrive by TMA, one box per page (64 dims x
 //     min(page, 128) rows, 128-byte swizzle), each into its own ring; boxes
 //     outside the piece or past the sequence end are requested at an
@@ -695,22 +695,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   pc.p_hi - pc.p_lo, 0);
       const int n_tiles = pc.tiles();
       int n0 = pc.tok0 & ~(kTileN - 1);
-      for (int t = 0; t < n_tiles; ++t, ++g, n0 += kTileN) {
-        // box of lane j: tokens [n0 + j * box_rows, + box_rows); boxes that
-        // miss the piece read an out-of-range page (zero fill, no traffic)
-        int y = 0, page = p.block_table ? p.num_pages : p.batch;
+      // box of lane j: tokens [n0 + j * box_rows, + box_rows); boxes that
+      // miss the piece read an out-of-range page (zero fill, no traffic).
+      // The page numbers of the next tile are read one tile ahead, so the
+      // block-table load's latency overlaps this tile's waits and copies.
+      auto box_coord = [&](int base, int &y_out, int &page_out) {
+        y_out = 0;
+        page_out = p.block_table ? p.num_pages : p.batch;
         if (lane < nbox) {
-          const int tok = n0 + lane * p.box_rows;
+          const int tok = base + lane * p.box_rows;
           if (tok < pc.tok_end && tok + p.box_rows > pc.tok0) {
             if (p.block_table) {
-              page = __ldg(p.block_table + pc.b * p.bt_stride + tok / p.page_size);
-              y = tok % p.page_size;
+              page_out = __ldg(p.block_table + pc.b * p.bt_stride + tok / p.page_size);
+              y_out = tok % p.page_size;
             } else {
-              page = pc.b;
-              y = tok;
+              page_out = pc.b;
+              y_out = tok;
             }
           }
         }
+      };
+      int ny, npage;
+      box_coord(n0, ny, npage);
+      for (int t = 0; t < n_tiles; ++t, ++g, n0 += kTileN) {
+        const int y = ny, page = npage;
+        if (t + 1 < n_tiles) box_coord(n0 + kTileN, ny, npage);
         const uint32_t st = g % PL::kStages, ph = ((g / PL::kStages) & 1u) ^ 1u;
         if (!(ok = warp_wait(smem_u32(&bars->k_empty[st]), ph, abort_flag, p.status,
                              kDevTimeoutProducer)))
