@@ -30,6 +30,7 @@ cudaError_t launch_gqa_combine(const float *, const float *, const int4 *, int, 
                                int, int, int, int, bool, void *, int, int64_t, int64_t, int64_t,
                                float *, cudaStream_t);
 int gqa_max_balanced_batch();
+int gqa_tile_tokens(int d);
 cudaError_t launch_mla_sv(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                           const CUtensorMap &, const fa_mla_args *, int, cudaStream_t);
 }  // namespace fa
@@ -157,16 +158,14 @@ int encode_gather_map(CUtensorMap *map, const void *base, int dtype, uint64_t ro
   return FA_OK;
 }
 
-constexpr int kGqaBlockN = 128;   // tokens per tile (page boxes hold at most this many rows)
-
 // K and V tensor maps of the grouped-query kernel: boxes of 64 dims x one
-// page (at most 128 rows) over {d, page rows, kv heads, pages}, or 128 rows
-// over {d, n, kv heads, batch} for contiguous caches.
+// page (at most one tile: 128 rows, 64 for head size 256) over {d, page rows,
+// kv heads, pages}, or one tile of rows over {d, n, kv heads, batch} for
+// contiguous caches.
 int encode_kv_maps(const fa_decode_args *a, CUtensorMap *km, CUtensorMap *vm) {
   const bool paged = a->block_table != nullptr;
-  const uint32_t box_rows =
-      paged ? static_cast<uint32_t>(a->page_size < kGqaBlockN ? a->page_size : kGqaBlockN)
-            : kGqaBlockN;
+  const int tile = fa::gqa_tile_tokens(a->d_qk);
+  const uint32_t box_rows = static_cast<uint32_t>(paged && a->page_size < tile ? a->page_size : tile);
   const uint64_t rows = paged ? a->page_size : static_cast<uint64_t>(a->n_ctx > 0 ? a->n_ctx : 1);
   const uint64_t groups = paged ? a->num_pages : a->batch;
   int st = encode_map4(km, a->k, a->dtype, a->d_qk, rows, a->num_kv_heads, groups,

@@ -39,20 +39,25 @@
 namespace fa {
 namespace gqa {
 
-constexpr int kTileN = 128;                  // tokens per tile: QK N, PV K
 constexpr int kThreads = 192;                // warps 0-3 rows, 4 producer, 5 MMA
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
-constexpr int kChunkBytes = kTileN * 128;    // 128 token rows x 64 dims
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;    // log2 units (factor 256)
 constexpr int kMaxStages = 6;
 
+// Tokens per tile (QK N, PV K): 128, or 64 for head size 256, where O (256
+// TMEM columns), two S / P buffers and one Q buffer fill the 512 columns.
+__host__ __device__ constexpr int tile_tokens(int d) { return d == 256 ? 64 : 128; }
+
 template <int kD>
 struct Plan {
+  static constexpr int kTile = tile_tokens(kD);
   static constexpr int kChunks = kD / 64;
-  static constexpr int kTileBytes = kChunks * kChunkBytes;     // 16 or 32 KB
-  static constexpr int kStages = kD == 64 ? 6 : 3;             // per ring
+  static constexpr int kChunkBytes = kTile * 128;                // tile rows x 64 dims
+  static constexpr int kTileBytes = kChunks * kChunkBytes;       // 16 or 32 KB
+  static constexpr int kStages = kD == 64 ? 6 : 3;               // per ring
+  static constexpr int kQBufs = kD == 256 ? 1 : 2;               // Q buffers in TMEM
   static constexpr int kOffK = 1024;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
   static constexpr int kOffStage = kOffV + kStages * kTileBytes;  // copy merge: [warp][lane][33] f32
@@ -60,11 +65,11 @@ struct Plan {
   static constexpr int kOffStats = kOffStage + kStageBytes;      // [2][warp][lane] f32
   static constexpr int kSmemUsed = kOffStats + 2 * 4 * 32 * 4;
   static constexpr int kSmemBytes = kSmemUsed + 1024;            // base alignment slack
-  // TMEM columns: O, two S / P buffers, two Q buffers (bf16 / f16 pairs)
+  // TMEM columns: O, two S / P buffers, Q buffers (bf16 / f16 pairs)
   static constexpr uint32_t kColO = 0;
   static constexpr uint32_t kColS = kD;
-  static constexpr uint32_t kColQ = kD + 2 * kTileN;
-  static_assert(kColQ + kD <= kTmemCols, "TMEM plan");
+  static constexpr uint32_t kColQ = kD + 2 * kTile;
+  static_assert(kColQ + kQBufs * kD / 2 <= kTmemCols, "TMEM plan");
   static_assert(kStages <= kMaxStages, "ring");
   static_assert(kSmemBytes <= 232448, "shared memory plan exceeds 227 KB");
   static_assert(kOffK % 1024 == 0 && kOffV % 1024 == 0 && kTileBytes % 1024 == 0,
@@ -108,6 +113,7 @@ struct Params {
   const int32_t *seq_lens;     // nullptr: every sequence has n_ctx tokens
   int32_t n_ctx;
   int32_t batch, hq, hkv, group, m_q, rows, causal;
+  int32_t tile_n;              // tokens per tile (tile_tokens(d)): the schedule's block
   float scale_log2;
   // num_splits == 0: the balanced schedule (Share); a split entry's pieces
   // go to slot parts + p (its first piece, in CTA p) and slots p (every
@@ -132,16 +138,16 @@ struct Piece {
   bool final_out;   // written straight to the output
   bool entry_first; // holds the entry's first block (or the entry is empty)
   int p_lo, p_hi;   // CTAs holding the entry's first / last block (balanced)
-  __device__ __forceinline__ int tiles() const {
-    return tok_end > tok0 ? (tok_end - (tok0 & ~(kTileN - 1)) + kTileN - 1) / kTileN : 0;
+  __device__ __forceinline__ int tiles(int tile) const {
+    return tok_end > tok0 ? (tok_end - (tok0 & ~(tile - 1)) + tile - 1) / tile : 0;
   }
 };
 
 __device__ __forceinline__ int seq_len_of(const Params &p, int b) {
   return p.seq_lens ? __ldg(p.seq_lens + b) : p.n_ctx;
 }
-__device__ __forceinline__ int blocks_of(int len) {
-  return len > 0 ? (len + kTileN - 1) / kTileN : 0;
+__device__ __forceinline__ int blocks_of(int len, int tile) {
+  return len > 0 ? (len + tile - 1) / tile : 0;
 }
 
 // The CTA's share of the balanced schedule.  All threads take part: a block
@@ -153,7 +159,7 @@ __device__ __noinline__ void compute_share(const Params &p, long long *scan, Bar
   const int per = (B + kThreads - 1) / kThreads;
   const int b0 = min(B, tid * per), b1 = min(B, b0 + per);
   long long local = 0;
-  for (int b = b0; b < b1; ++b) local += 1 + blocks_of(seq_len_of(p, b));
+  for (int b = b0; b < b1; ++b) local += 1 + blocks_of(seq_len_of(p, b), p.tile_n);
   long long incl = local;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -166,7 +172,7 @@ __device__ __noinline__ void compute_share(const Params &p, long long *scan, Bar
   for (int w = 0; w < warp; ++w) run += bars->warp_sum[w];
   for (int b = b0; b < b1; ++b) {
     scan[b] = run;
-    run += 1 + blocks_of(seq_len_of(p, b));
+    run += 1 + blocks_of(seq_len_of(p, b), p.tile_n);
   }
   if (b1 == B && b0 < b1) scan[B] = run;
   if (B == 0 && tid == 0) scan[0] = 0;
@@ -221,7 +227,7 @@ __device__ __forceinline__ bool valid(const Params &p, const Share *sh, const Cu
 }
 __device__ __forceinline__ void advance(const Params &p, Cursor &c) {
   if (p.num_splits == 0) {
-    c.x += 1 + blocks_of(seq_len_of(p, c.e / p.hkv));
+    c.x += 1 + blocks_of(seq_len_of(p, c.e / p.hkv), p.tile_n);
     ++c.e;
   } else {
     c.part += gridDim.x;
@@ -234,13 +240,13 @@ __device__ __noinline__ Piece get_piece(const Params &p, const Share *sh, Cursor
     pc.e = c.e;
     pc.b = c.e / p.hkv;
     pc.len = max(seq_len_of(p, pc.b), 0);
-    const int nb = blocks_of(pc.len);
+    const int nb = blocks_of(pc.len, p.tile_n);
     // blocks of this entry inside [a0, a1): block j sits at unit x + 1 + j
     const long long j0 = min(max(sh->a0 - c.x - 1, 0ll), static_cast<long long>(nb));
     const long long j1 = min(max(sh->a1 - c.x - 1, 0ll), static_cast<long long>(nb));
     pc.present = nb > 0 ? j1 > j0 : c.x >= sh->a0;
-    pc.tok0 = static_cast<int>(j0) * kTileN;
-    pc.tok_end = min(static_cast<int>(j1) * kTileN, pc.len);
+    pc.tok0 = static_cast<int>(j0) * p.tile_n;
+    pc.tok_end = min(static_cast<int>(j1) * p.tile_n, pc.len);
     auto part_of = [&](long long u) {
       return static_cast<int>(min(static_cast<long long>(sh->parts - 1),
                                   ((u + 1) * sh->parts + sh->total - 1) / sh->total - 1));
@@ -276,7 +282,7 @@ __device__ __noinline__ Piece get_piece(const Params &p, const Share *sh, Cursor
 __device__ __forceinline__ void next_with_tiles(const Params &p, const Share *sh, Cursor &c) {
   while (valid(p, sh, c)) {
     const Piece pc = get_piece(p, sh, c);
-    if (pc.present && pc.tiles() > 0) return;
+    if (pc.present && pc.tiles(p.tile_n) > 0) return;
     advance(p, c);
   }
 }
@@ -293,25 +299,24 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
 template <typename T, int kD>
 __device__ __forceinline__ void write_q(const Params &p, const Piece &pc, bool live, int g_idx,
                                         int m_idx, uint32_t t_q, uint32_t bar, int lane) {
-  uint32_t w[kD / 2];
-  if (live) {
-    const int h = pc.kvh * p.group + g_idx;
-    const uint4 *src = reinterpret_cast<const uint4 *>(
-        static_cast<const T *>(p.q) + pc.b * p.q_sb + h * p.q_sh + m_idx * p.q_sm);
+  const int h = pc.kvh * p.group + g_idx;
+  const uint4 *src = reinterpret_cast<const uint4 *>(
+      static_cast<const T *>(p.q) + pc.b * p.q_sb + h * p.q_sh + m_idx * p.q_sm);
+  // 64 dims (32 packed words) at a time: a 256-wide row would hold 128
+  // registers at once
 #pragma unroll
-    for (int i = 0; i < kD / 8; ++i) {
-      const uint4 v = __ldg(src + i);
+  for (int j = 0; j < kD / 64; ++j) {
+    uint32_t w[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 v = live ? __ldg(src + 8 * j + i) : make_uint4(0u, 0u, 0u, 0u);
       w[4 * i] = v.x;
       w[4 * i + 1] = v.y;
       w[4 * i + 2] = v.z;
       w[4 * i + 3] = v.w;
     }
-  } else {
-#pragma unroll
-    for (int i = 0; i < kD / 2; ++i) w[i] = 0u;
+    tmem_st32(t_q + 32 * j, w);
   }
-#pragma unroll
-  for (int j = 0; j < kD / 64; ++j) tmem_st32(t_q + 32 * j, w + 32 * j);
   tmem_wait_st();
   tc_fence_before();
   __syncwarp();
@@ -431,7 +436,7 @@ template <typename T, int kD, int kC>
 __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *smem,
                                          uint32_t tmem, int warp, int lane) {
   using PL = Plan<kD>;
-  constexpr int kCols = kTileN / kC;   // tile columns of one copy
+  constexpr int kCols = PL::kTile / kC;  // tile columns of one copy
   constexpr int kWords = kCols / 2;    // packed P words of one copy
   volatile int *abort_flag = &bars->abort_flag;
   const int quads = kC == 1 ? (p.rows + 31) / 32 : 4 / kC;
@@ -461,8 +466,8 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
   for (Cursor c = first_cursor(p, sh); valid(p, sh, c) && ok; advance(p, c)) {
     const Piece pc = get_piece(p, sh, c);
     if (!pc.present) continue;
-    const int n_tiles = pc.tiles();
-    if (n_tiles > 0) {
+    const int n_tiles = pc.tiles(p.tile_n);
+    if (PL::kQBufs == 2 && n_tiles > 0) {
       // Q of the next piece with tiles, into the other buffer: its previous
       // user (two pieces back) finished all QKs before this piece started
       Cursor nq = c;
@@ -477,17 +482,21 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
     // m + len - m_q (bottom-right alignment, split_kv.py:88-92)
     const int row_end = p.causal ? min(pc.tok_end, m_idx + pc.len - p.m_q + 1) : pc.tok_end;
     float m_use = -INFINITY, l = 0.f;
-    int n0 = pc.tok0 & ~(kTileN - 1);
-    for (int t = 0; t < n_tiles; ++t, ++g, n0 += kTileN) {
+    int n0 = pc.tok0 & ~(PL::kTile - 1);
+    for (int t = 0; t < n_tiles; ++t, ++g, n0 += PL::kTile) {
       const uint32_t buf = g & 1u;
       if (!(ok = warp_wait(smem_u32(&bars->s_full[buf]), (g >> 1) & 1u, abort_flag, p.status,
                            kDevTimeoutSoftmax)))
         break;
       tc_fence_after();
-      const uint32_t t_s = tmem + lane_off + PL::kColS + buf * kTileN;
+      const uint32_t t_s = tmem + lane_off + PL::kColS + buf * PL::kTile;
       float s[kCols];
+      if constexpr (kCols == 16) {
+        tmem_ld16(t_s + copy * kCols, s);
+      } else {
 #pragma unroll
-      for (int j = 0; j < kCols / 32; ++j) tmem_ld32(t_s + copy * kCols + 32 * j, s + 32 * j);
+        for (int j = 0; j < kCols / 32; ++j) tmem_ld32(t_s + copy * kCols + 32 * j, s + 32 * j);
+      }
       tmem_wait_ld();
       // rows past the group (zero Q, so S = 0) count as fully valid: their
       // P and O rows are never read
@@ -533,22 +542,23 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
       f32x2_split(acc2, a0, a1);
       l += a0 + a1;
       // P over the S buffer: this copy's words, zeros over the other copies'
-      if constexpr (kC == 1) {
-        tmem_st32(t_s, w);
-        tmem_st32(t_s + 32, w + 32);
-      } else if constexpr (kC == 2) {
-        uint32_t z[32];
+      auto st_words = [&](uint32_t addr, const uint32_t *src) {  // kWords words
+        if constexpr (kWords >= 32) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) z[j] = 0u;
-        tmem_st32(t_s + copy * 32, w);
-        tmem_st32(t_s + (copy ^ 1) * 32, z);
-      } else {
-        uint32_t z[16];
+          for (int j = 0; j < kWords / 32; ++j) tmem_st32(addr + 32 * j, src + 32 * j);
+        } else if constexpr (kWords == 16) {
+          tmem_st16p(addr, src);
+        } else {
+          tmem_st8p(addr, src);
+        }
+      };
+      st_words(t_s + copy * kWords, w);
+      if constexpr (kC > 1) {
+        uint32_t z[kWords];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) z[j] = 0u;
-        tmem_st16p(t_s + copy * 16, w);
+        for (int j = 0; j < kWords; ++j) z[j] = 0u;
 #pragma unroll
-        for (int cc = 1; cc < 4; ++cc) tmem_st16p(t_s + ((copy + cc) & 3) * 16, z);
+        for (int cc = 1; cc < kC; ++cc) st_words(t_s + ((copy + cc) % kC) * kWords, z);
       }
       if (t > 0) {
         // PV of the previous tile must be complete before O is rescaled
@@ -574,7 +584,7 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
       // Value rows past the sequence end inside the last loaded page may
       // hold any bits (even NaN); P is 0 there but 0 * NaN is not, so clear
       // them before the PV product.
-      if (warp == 0 && pc.len > n0 && pc.len < n0 + kTileN && pc.len <= pc.tok_end) {
+      if (warp == 0 && pc.len > n0 && pc.len < n0 + PL::kTile && pc.len <= pc.tok_end) {
         const int jb = (pc.len - 1 - n0) / p.box_rows;
         const int r0 = pc.len - n0, r1 = (jb + 1) * p.box_rows;
         const int btok = n0 + jb * p.box_rows;
@@ -587,7 +597,8 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
           const int units = (r1 - r0) * 8;
           for (int u = lane; u < units * PL::kChunks; u += 32) {
             const int ch = u / units, rem = u % units;
-            const uint32_t addr = tile + ch * kChunkBytes + (r0 + rem / 8) * 128 + (rem % 8) * 16;
+            const uint32_t addr =
+                tile + ch * PL::kChunkBytes + (r0 + rem / 8) * 128 + (rem % 8) * 16;
             asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u)
                          : "memory");
           }
@@ -600,6 +611,16 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
       if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[buf]));
     }
     if (!ok) break;
+    if (PL::kQBufs == 1 && n_tiles > 0) {
+      // one Q buffer (head size 256): the next piece's Q goes in once every
+      // score product of this piece has completed (each s_full was waited)
+      Cursor nq = c;
+      advance(p, nq);
+      next_with_tiles(p, sh, nq);
+      if (valid(p, sh, nq))
+        write_q<T, kD>(p, get_piece(p, sh, nq), live, g_idx, m_idx, tmem + lane_off + PL::kColQ,
+                       smem_u32(&bars->q_full[0]), lane);
+    }
     if (n_tiles > 0) {
       if (!(ok = warp_wait(smem_u32(&bars->pv_done), (g - 1) & 1u, abort_flag, p.status,
                            kDevTimeoutSoftmax)))
@@ -683,7 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kProducerWarp) {
     // ------------------------------------------------------- TMA producer
     const uint32_t kbase = smem_u32(smem + PL::kOffK), vbase = smem_u32(smem + PL::kOffV);
-    const int nbox = kTileN / p.box_rows;
+    const int nbox = PL::kTile / p.box_rows;
     uint32_t g = 0, gk = 0, gv = 0;  // tiles begun, K tiles issued, V tiles issued
     bool ok = true;
     const Share *sh = &bars->share;
@@ -693,8 +714,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.num_splits == 0 && pc.entry_first && lane == 0)
         p.merge[pc.e] = make_int4(pc.final_out ? -1 : sh->parts + pc.p_lo, pc.p_lo + 1,
                                   pc.p_hi - pc.p_lo, 0);
-      const int n_tiles = pc.tiles();
-      int n0 = pc.tok0 & ~(kTileN - 1);
+      const int n_tiles = pc.tiles(p.tile_n);
+      int n0 = pc.tok0 & ~(PL::kTile - 1);
       // box of lane j: tokens [n0 + j * box_rows, + box_rows); boxes that
       // miss the piece read an out-of-range page (zero fill, no traffic).
       // The page numbers of the next tile are read one tile ahead, so the
@@ -717,9 +738,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       int ny, npage;
       box_coord(n0, ny, npage);
-      for (int t = 0; t < n_tiles; ++t, ++g, n0 += kTileN) {
+      for (int t = 0; t < n_tiles; ++t, ++g, n0 += PL::kTile) {
         const int y = ny, page = npage;
-        if (t + 1 < n_tiles) box_coord(n0 + kTileN, ny, npage);
+        if (t + 1 < n_tiles) box_coord(n0 + PL::kTile, ny, npage);
         const uint32_t st = g % PL::kStages, ph = ((g / PL::kStages) & 1u) ^ 1u;
         if (!(ok = warp_wait(smem_u32(&bars->k_empty[st]), ph, abort_flag, p.status,
                              kDevTimeoutProducer)))
@@ -730,7 +751,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane < nbox) {
 #pragma unroll
           for (int ch = 0; ch < PL::kChunks; ++ch)
-            tma_load_4d(kbase + st * PL::kTileBytes + ch * kChunkBytes + lane * p.box_rows * 128,
+            tma_load_4d(kbase + st * PL::kTileBytes + ch * PL::kChunkBytes + lane * p.box_rows * 128,
                         &k_map, kf, ch * 64, y, pc.kvh, page);
         }
         ++gk;
@@ -743,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane < nbox) {
 #pragma unroll
           for (int ch = 0; ch < PL::kChunks; ++ch)
-            tma_load_4d(vbase + st * PL::kTileBytes + ch * kChunkBytes + lane * p.box_rows * 128,
+            tma_load_4d(vbase + st * PL::kTileBytes + ch * PL::kChunkBytes + lane * p.box_rows * 128,
                         &v_map, vf, ch * 64, y, pc.kvh, page);
         }
         ++gv;
@@ -763,11 +784,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ---------------------------------------------------------- MMA issuer
-    constexpr uint32_t kIdescQK = umma_idesc_f16(128, kTileN, fmt, 0);
+    constexpr uint32_t kIdescQK = umma_idesc_f16(128, PL::kTile, fmt, 0);
     constexpr uint32_t kIdescPV = umma_idesc_f16(128, kD, fmt, 1);
     const uint32_t kbase = smem_u32(smem + PL::kOffK), vbase = smem_u32(smem + PL::kOffV);
     const uint64_t k_desc = smem_desc_sw128(kbase, 16, 1024);
-    const uint64_t v_desc = smem_desc_sw128(vbase, kChunkBytes, 1024);
+    const uint64_t v_desc = smem_desc_sw128(vbase, PL::kChunkBytes, 1024);
     uint32_t g = 0, k = 0;
     bool ok = true;
     int pend = -1;             // tile whose PV is still to be issued
@@ -783,8 +804,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint64_t vd = v_desc + static_cast<uint64_t>((st * PL::kTileBytes) >> 4);
 #pragma unroll
-      for (int kk = 0; kk < kTileN / 16; ++kk)
-        umma_ts_warp(tmem + PL::kColO, tmem + PL::kColS + buf * kTileN + kk * 8,
+      for (int kk = 0; kk < PL::kTile / 16; ++kk)
+        umma_ts_warp(tmem + PL::kColO, tmem + PL::kColS + buf * PL::kTile + kk * 8,
                      vd + static_cast<uint64_t>((kk * 16 * 128) >> 4), kIdescPV,
                      (first && kk == 0) ? 0u : 1u);
       tc_commit_warp(smem_u32(&bars->v_empty[st]));
@@ -795,26 +816,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (Cursor c = first_cursor(p, sh); valid(p, sh, c) && ok; advance(p, c)) {
       const Piece pc = get_piece(p, sh, c);
       if (!pc.present) continue;
-      const int n_tiles = pc.tiles();
+      const int n_tiles = pc.tiles(p.tile_n);
       if (n_tiles == 0) continue;
-      if (!(ok = warp_wait(smem_u32(&bars->q_full[k & 1u]), (k >> 1) & 1u, abort_flag, p.status,
-                           kDevTimeoutMma)))
+      const uint32_t qb = k % PL::kQBufs;
+      if (!(ok = warp_wait(smem_u32(&bars->q_full[qb]), (k / PL::kQBufs) & 1u, abort_flag,
+                           p.status, kDevTimeoutMma)))
         break;
-      const uint32_t qcol = tmem + PL::kColQ + (k & 1u) * (kD / 2);
+      const uint32_t qcol = tmem + PL::kColQ + qb * (kD / 2);
       for (int t = 0; t < n_tiles && ok; ++t, ++g) {
         const uint32_t st = g % PL::kStages;
         if (!(ok = warp_wait(smem_u32(&bars->k_full[st]), (g / PL::kStages) & 1u, abort_flag,
                              p.status, kDevTimeoutMma)))
           break;
         tc_fence_after();
-        const uint32_t sd = tmem + PL::kColS + (g & 1u) * kTileN;
+        const uint32_t sd = tmem + PL::kColS + (g & 1u) * PL::kTile;
         const uint64_t kd = k_desc + static_cast<uint64_t>((st * PL::kTileBytes) >> 4);
 #pragma unroll
         for (int ch = 0; ch < PL::kChunks; ++ch)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             umma_ts_warp(sd, qcol + ch * 32 + kk * 8,
-                         kd + static_cast<uint64_t>((ch * kChunkBytes + kk * 32) >> 4), kIdescQK,
+                         kd + static_cast<uint64_t>((ch * PL::kChunkBytes + kk * 32) >> 4), kIdescQK,
                          (ch | kk) ? 1u : 0u);
         tc_commit_warp(smem_u32(&bars->k_empty[st]));
         tc_commit_warp(smem_u32(&bars->s_full[g & 1u]));
@@ -874,26 +896,33 @@ cudaError_t launch_d(const CUtensorMap &km, const CUtensorMap &vm, const Params 
 }  // namespace gqa
 
 int gqa_max_balanced_batch() {
-  // the scan holds batch + 1 int64 in the K and V rings (same size for both
-  // head sizes)
+  // the scan holds batch + 1 int64 in the K and V rings (same size for every
+  // head size)
   static_assert(gqa::Plan<64>::kOffStage - gqa::Plan<64>::kOffK ==
-                    gqa::Plan<128>::kOffStage - gqa::Plan<128>::kOffK,
+                        gqa::Plan<128>::kOffStage - gqa::Plan<128>::kOffK &&
+                    gqa::Plan<256>::kOffStage - gqa::Plan<256>::kOffK ==
+                        gqa::Plan<128>::kOffStage - gqa::Plan<128>::kOffK,
                 "ring sizes");
   return (gqa::Plan<128>::kOffStage - gqa::Plan<128>::kOffK) / 8 - 1;
 }
 
 size_t gqa_smem_bytes(int d) {
-  return d == 64 ? gqa::Plan<64>::kSmemBytes : gqa::Plan<128>::kSmemBytes;
+  return d == 64    ? gqa::Plan<64>::kSmemBytes
+         : d == 256 ? gqa::Plan<256>::kSmemBytes
+                    : gqa::Plan<128>::kSmemBytes;
 }
 
-// The tensor-core kernel serves bf16 / f16 with d_qk == d_v in {64, 128},
-// at most 128 query rows per kv head, a positive scale, 16-byte aligned rows
-// and pages of a power-of-two size >= 16 or a multiple of 128 tokens.
+int gqa_tile_tokens(int d) { return gqa::tile_tokens(d); }
+
+// The tensor-core kernel serves bf16 / f16 with d_qk == d_v in {64, 128,
+// 256}, at most 128 query rows per kv head, a positive scale, 16-byte aligned
+// rows and pages of at least 16 tokens that divide the tile (128 tokens; 64
+// for head size 256) or are a multiple of it.
 bool gqa_tc_eligible(const fa_decode_args *a) {
   auto al16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
   auto m8 = [](int64_t x) { return x % 8 == 0; };
   if (a->dtype != FA_DTYPE_BF16 && a->dtype != FA_DTYPE_F16) return false;
-  if (a->d_qk != a->d_v || (a->d_qk != 64 && a->d_qk != 128)) return false;
+  if (a->d_qk != a->d_v || (a->d_qk != 64 && a->d_qk != 128 && a->d_qk != 256)) return false;
   if (a->num_kv_heads <= 0 || a->num_q_heads % a->num_kv_heads) return false;
   const int64_t rows = static_cast<int64_t>(a->num_q_heads / a->num_kv_heads) * a->m_q;
   if (rows < 1 || rows > 128) return false;
@@ -905,7 +934,8 @@ bool gqa_tc_eligible(const fa_decode_args *a) {
   if (a->block_table) {
     const int ps = a->page_size;
     if (ps < 16 || ps % 16) return false;
-    if (ps <= gqa::kTileN ? (gqa::kTileN % ps) : (ps % gqa::kTileN)) return false;
+    const int tile = gqa::tile_tokens(a->d_qk);
+    if (ps <= tile ? (tile % ps) : (ps % tile)) return false;
     if (a->num_pages <= 0) return false;
   }
   return true;
@@ -927,8 +957,8 @@ cudaError_t launch_gqa_tc(const CUtensorMap &km, const CUtensorMap &vm, const fa
   p.bt_stride = a->bt_stride;
   p.page_size = a->page_size;
   p.num_pages = a->num_pages;
-  p.box_rows = a->block_table ? (a->page_size < gqa::kTileN ? a->page_size : gqa::kTileN)
-                              : gqa::kTileN;
+  p.tile_n = gqa::tile_tokens(a->d_qk);
+  p.box_rows = a->block_table && a->page_size < p.tile_n ? a->page_size : p.tile_n;
   p.seq_lens = a->seq_lens;
   p.n_ctx = a->n_ctx;
   p.batch = a->batch;
@@ -955,6 +985,9 @@ cudaError_t launch_gqa_tc(const CUtensorMap &km, const CUtensorMap &vm, const fa
   if (a->d_qk == 64)
     return f16 ? gqa::launch_d<__half, 64>(km, vm, p, grid, pdl, stream)
                : gqa::launch_d<__nv_bfloat16, 64>(km, vm, p, grid, pdl, stream);
+  if (a->d_qk == 256)
+    return f16 ? gqa::launch_d<__half, 256>(km, vm, p, grid, pdl, stream)
+               : gqa::launch_d<__nv_bfloat16, 256>(km, vm, p, grid, pdl, stream);
   return f16 ? gqa::launch_d<__half, 128>(km, vm, p, grid, pdl, stream)
              : gqa::launch_d<__nv_bfloat16, 128>(km, vm, p, grid, pdl, stream);
 }

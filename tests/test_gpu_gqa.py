@@ -4,7 +4,8 @@ The reference's paged test grid runs through the same kernel in
 test_gpu_generic.py; these cases pin what is specific to the tensor-core
 path: that it is the path taken, the balanced schedule of (sequence, kv head)
 entries bit-for-bit against its host specification, the copy layouts for
-1..128 query rows per kv head, value rows past a sequence end holding NaN,
+1..128 query rows per kv head, head sizes 64, 128 and 256 (the last on
+64-token tiles), value rows past a sequence end holding NaN,
 explicit and automatic split counts, causal multi-token rows on contiguous
 caches, and a clean status word.
 """
@@ -75,7 +76,8 @@ def _args_for(q, k, lens, bt, out):
     (128, 8, 16, torch.float16, 1), (64, 1, 256, torch.bfloat16, 1), (128, 128, 128,
                                                                        torch.float16, 1),
     (32, 8, 16, torch.float16, 0), (128, 8, 16, torch.float32, 0), (128, 8, 48, torch.float16, 0),
-    (128, 256, 16, torch.float16, 0)])
+    (128, 256, 16, torch.float16, 0), (256, 8, 16, torch.bfloat16, 1),
+    (256, 4, 128, torch.float16, 1), (256, 8, 32, torch.float16, 1), (256, 8, 96, torch.float16, 0)])
 def test_tensor_core_path_selection(d, group, block, dtype, want):
     q, k, _, lens, bt, _ = _paged_inputs(2, max(group, 8), group, d, block, 64, dtype, 0,
                                          nblocks=8)
@@ -84,10 +86,12 @@ def test_tensor_core_path_selection(d, group, block, dtype, want):
     assert _lib.lib().fa_decode_uses_tensor_cores(ctypes.byref(a)) == want
 
 
-def test_balanced_schedule_bit_exact():
+@pytest.mark.parametrize("d", [64, 256])
+def test_balanced_schedule_bit_exact(d):
     """The merge records the kernel writes for every entry equal the host
-    specification (oracle.gqa_schedule), and the outputs match the oracle."""
-    rs = np.random.RandomState(7)
+    specification (oracle.gqa_schedule; 128-token blocks, 64 for head size
+    256), and the outputs match the oracle."""
+    rs = np.random.RandomState(7 + d)
     lib = _lib.lib()
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     for trial in range(12):
@@ -96,7 +100,7 @@ def test_balanced_schedule_bit_exact():
         hkv = int(rs.choice([1, 2, 8]))
         lens = rs.randint(0 if trial % 4 == 0 else 1, 3000, size=B).astype(np.int32)
         lens[0] = max(int(lens[0]), 1)
-        q, k, v, lens_t, bt, scale = _paged_inputs(B, hkv * group, group, 64, 16, 3000,
+        q, k, v, lens_t, bt, scale = _paged_inputs(B, hkv * group, group, d, 16, 3000,
                                                    torch.float16, trial, nblocks=400,
                                                    lens=lens.tolist())
         out = torch.empty_like(q)
@@ -115,7 +119,7 @@ def test_balanced_schedule_bit_exact():
         assert st == 0
         torch.cuda.synchronize()
         got = ws[po.value + pl.value:].view(torch.int32).view(-1, 4)[:, :3].cpu().numpy()
-        _, merge = oracle.gqa_schedule(lens, hkv, sms)
+        _, merge = oracle.gqa_schedule(lens, hkv, sms, block_n=64 if d == 256 else 128)
         assert np.array_equal(got, np.asarray(merge, np.int32)), trial
         ref = _oracle(q, k, v, bt, lens_t, scale).to(torch.float16).float()
         assert torch.allclose(out.float().cpu(), ref, atol=2e-3, rtol=1e-5), trial
@@ -123,7 +127,7 @@ def test_balanced_schedule_bit_exact():
 
 @pytest.mark.parametrize("hq, group", [(64, 1), (64, 8), (16, 16), (64, 32), (64, 64), (96, 96),
                                        (128, 128)])
-@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("d", [64, 128, 256])
 def test_rows_per_kv_head(hq, group, d):
     """1..128 query rows per kv head: four, two or one copies of each row."""
     q, k, v, lens, bt, scale = _paged_inputs(5, hq, group, d, 16, 700, torch.bfloat16, group + d)
@@ -135,14 +139,15 @@ def test_rows_per_kv_head(hq, group, d):
     assert read_status(q.device) == 0
 
 
-@pytest.mark.parametrize("block", [16, 128, 256])
+@pytest.mark.parametrize("d, block", [(128, 16), (128, 128), (128, 256), (256, 16),
+                                      (256, 128)])
 @pytest.mark.parametrize("num_splits", [0, 1, 3, 8])
-def test_nan_past_sequence_end_and_splits(block, num_splits):
+def test_nan_past_sequence_end_and_splits(d, block, num_splits):
     """Value / key slots past each sequence's end in its last page hold NaN;
     the output stays finite and equal to the oracle's."""
     lens = [1, 17, 129, 300, 1000, 4096, 77]
     width = (max(lens) + block - 1) // block
-    q, k, v, lens_t, bt, scale = _paged_inputs(len(lens), 64, 8, 128, block, 4096,
+    q, k, v, lens_t, bt, scale = _paged_inputs(len(lens), 64, 8, d, block, 4096,
                                                torch.float16, block + num_splits,
                                                nblocks=len(lens) * width, lens=lens)
     # distinct pages per sequence so that poisoning one tail cannot touch
@@ -179,11 +184,12 @@ def test_bench_shape_matches_oracle():
 
 @pytest.mark.parametrize("M", [1, 3, 4])
 @pytest.mark.parametrize("causal", [False, True])
-def test_contiguous_causal_rows(M, causal):
+@pytest.mark.parametrize("D", [128, 256])
+def test_contiguous_causal_rows(M, causal, D):
     """Contiguous caches (split-KV decoding) with several query tokens per
     sequence and bottom-right causal masking, GQA group 4."""
-    g = torch.Generator(device="cuda").manual_seed(M * 2 + causal)
-    B, Hq, Hk, N, D = 3, 16, 4, 3001, 128
+    g = torch.Generator(device="cuda").manual_seed(M * 2 + causal + D)
+    B, Hq, Hk, N = 3, 16, 4, 3001
     q = torch.randn(B, Hq, M, D, generator=g, device="cuda").to(torch.bfloat16)
     k = torch.randn(B, Hk, N, D, generator=g, device="cuda").to(torch.bfloat16)
     v = torch.randn(B, Hk, N, D, generator=g, device="cuda").to(torch.bfloat16)
