@@ -60,6 +60,10 @@ def parse():
                         "GPU for the record (MTP causal, sparse top-k, 1M-token context)")
     p.add_argument("--batch", type=int, default=0,
                    help="configs 3-5: first N sequences only (smaller cases for profiling)")
+    p.add_argument("--gqa", default=None, metavar="KEY=VALUE,...",
+                   help="time only the grouped-query paged_attention record on one GPU, its "
+                        "shape changed by overrides (keys: seqs, heads_q, heads_kv, head, "
+                        "page, ctx, splits); '' keeps the default shape")
     return p.parse_args()
 
 
@@ -583,20 +587,31 @@ def run_mtp_sharded(args, world, rank, dev, flush):
 
 
 # ------------------ the reference's own paged API at a GQA shape (per GPU)
-GQA = dict(seqs=32, heads_q=64, heads_kv=8, head=128, page=16, ctx=4096)
+GQA = dict(seqs=32, heads_q=64, heads_kv=8, head=128, page=16, ctx=4096, splits=0)
 
 
-def run_gqa(args, dev, flush):
-    """`paged_attention` (paged.py:20) at a grouped-query shape: 32 sequences
-    of 4096 tokens, 64 query heads over 8 kv heads (group 8), head size 128,
-    16-token pages in a random permutation, bf16.  Per GPU (each rank runs
-    its own).  Bytes: every K and V row once + Q + O."""
+def gqa_shape(spec):
+    """GQA with the overrides of a `--gqa` value ("head=256,page=128")."""
+    c = dict(GQA)
+    for item in filter(None, (spec or "").split(",")):
+        key, _, val = item.partition("=")
+        if key not in c:
+            raise SystemExit(f"--gqa: unknown key {key!r} (keys: {', '.join(c)})")
+        c[key] = int(val)
+    return c
+
+
+def run_gqa(args, dev, flush, c=GQA):
+    """`paged_attention` (paged.py:20) at a grouped-query shape: by default
+    32 sequences of 4096 tokens, 64 query heads over 8 kv heads (group 8),
+    head size 128, 16-token pages in a random permutation, bf16, the balanced
+    schedule (num_splits 0).  Per GPU (each rank runs its own).  Bytes: every
+    K and V row once + Q + O."""
     import torch
 
     import flagattention_b200 as fa
     from flagattention_b200 import _torch as fat
 
-    c = GQA
     g = torch.Generator(device=dev).manual_seed(SEED + 400)
     pages_per = c["ctx"] // c["page"]
     npages = c["seqs"] * pages_per
@@ -610,7 +625,7 @@ def run_gqa(args, dev, flush):
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        return fa.paged_attention(q, kc, vc, lens, bt, scale, c["ctx"])
+        return fa.paged_attention(q, kc, vc, lens, bt, scale, c["ctx"], c["splits"])
 
     for _ in range(args.warmup):
         step()
@@ -630,7 +645,10 @@ def run_gqa(args, dev, flush):
     ms = a.elapsed_time(b) / steps
     nbytes = 2 * kc.numel() * 2 + 2 * q.numel() * 2
     peak_gbs, _, peak_kind = measured_peaks()
-    return {"workload": "gqa_paged_decode_b32_hq64_hkv8_d128_page16_ctx4096_bf16",
+    name = "gqa_paged_decode_b{seqs}_hq{heads_q}_hkv{heads_kv}_d{head}_page{page}_ctx{ctx}_bf16"
+    if c["splits"]:
+        name += "_splits{splits}"
+    return {"workload": name.format(**c),
             "api": "paged_attention (paged.py:20)", "steps": steps, "ms_per_step": ms,
             "l2": "inputs larger than L2, calls back to back",
             "tokens_per_s": c["seqs"] / (ms * 1e-3),
@@ -836,9 +854,28 @@ def run_other(args):
     print(json.dumps(line))
 
 
+def run_gqa_only(args):
+    """`--gqa`: the grouped-query record alone, one GPU, one JSON line."""
+    import torch
+
+    c = gqa_shape(args.gqa)
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)   # > 126 MB L2
+    rec = run_gqa(args, dev, flush, c)
+    rec["warmup"] = args.warmup
+    print(json.dumps(rec), flush=True)
+
+
 def main():
     args = parse()
-    if args.config != 2:
+    if args.gqa is not None:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference arm is timed on the headline config only"}))
+        else:
+            run_gqa_only(args)
+    elif args.config != 2:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable":
                               "the reference arm is timed on the headline config only"}))
