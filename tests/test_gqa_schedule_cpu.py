@@ -3,12 +3,13 @@ every block of every entry is decoded exactly once, the shares are equal to a
 unit, and the merge records name exactly the slots the pieces use."""
 
 import numpy as np
+import pytest
 
 import oracle
 
 
-def _check(lens, hkv, parts):
-    pieces, merge = oracle.gqa_schedule(lens, hkv, parts)
+def _check(lens, hkv, parts, block_n=128):
+    pieces, merge = oracle.gqa_schedule(lens, hkv, parts, block_n=block_n)
     E = len(lens) * hkv
     covered = {e: [] for e in range(E)}
     slots = {}
@@ -36,13 +37,19 @@ def _check(lens, hkv, parts):
     return pieces
 
 
-def test_schedule_covers_every_block_once():
+@pytest.mark.parametrize("block_n", [128, 64])  # 64: head size 256's tiles
+def test_schedule_covers_every_block_once(block_n):
     rs = np.random.RandomState(3)
     for trial in range(60):
         B = int(rs.randint(1, 40))
         hkv = int(rs.choice([1, 2, 8]))
         lens = rs.randint(0 if trial % 5 == 0 else 1, 3000, size=B)
-        _check(lens, hkv, int(rs.randint(1, 160)))
+        pieces = _check(lens, hkv, int(rs.randint(1, 160)), block_n)
+        # pieces start and end on block boundaries (or the sequence end)
+        for pl in pieces:
+            for e, t0, t1, _, _ in pl:
+                assert t0 % block_n == 0
+                assert t1 % block_n == 0 or t1 == lens[e // hkv]
 
 
 def test_schedule_shares_are_balanced():
