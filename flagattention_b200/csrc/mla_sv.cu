@@ -1092,10 +1092,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t trow = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
       uint32_t vs = 0, gb = 0;
       bool ok = true;
+      // A piece's bounds and split slots are fetched while the previous
+      // piece's last PV runs (before its epilogue), so that after the
+      // epilogue the next piece's first block is released at once: these
+      // dependent global loads would otherwise sit between the two.
+      Piece nxt{};
+      int nxt_first = 0, nxt_n = 1;
+      auto fetch = [&](int i) {
+        nxt = get_piece(p, meta, i);
+        nxt_first = p.num_splits[nxt.b];
+        nxt_n = p.num_splits[nxt.b + 1] - nxt_first;
+      };
+      if (n_pieces > 0) fetch(0);
       for (int i = 0; i < n_pieces && ok; ++i) {
-        const Piece pc = get_piece(p, meta, i);
-        const int first_slot = p.num_splits[pc.b];
-        const int n_split = p.num_splits[pc.b + 1] - first_slot;
+        const Piece pc = nxt;
+        const int first_slot = nxt_first;
+        const int n_split = nxt_n;
         const int slot_o = first_slot + pc.split_idx;
         const bool has_tiles = pc.tok_end > pc.tok0;
         float inv_l = 0.f, lse_row = -INFINITY;
@@ -1155,6 +1167,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           vs += n_sub;
         }
         if (!ok) break;
+        if (i + 1 < n_pieces) fetch(i + 1);
         if (has_tiles) {
           const uint32_t lg = gb - 1;
           ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->pv_done[lg % kPSlots]),

@@ -86,6 +86,26 @@ def test_dense_fp16():
     assert_close("lse", lse, want_l)
 
 
+def test_output_rows_not_32_byte_aligned():
+    """A caller's output view with a padded row stride whose rows start 16
+    bytes past a 32-byte boundary gets the same result as a fresh output, bit
+    for bit (split and unsplit sequences), and nothing outside the view."""
+    d = build_dense(14, [3000, 64, 1201, 5000], heads=128)
+    meta, splits = fa.get_mla_metadata(d["lens"], 128, 1, num_sm_parts_override=9)
+    ref_o, ref_l = fa.flash_mla_with_kvcache(d["q"], d["kc"], d["bt"], d["lens"], D_V, meta,
+                                             splits, softmax_scale=SCALE)
+    big = torch.full((4, 1, 128, D_V + 8), float("nan"), dtype=ref_o.dtype, device="cuda")
+    out = big[..., 8:]  # row stride 520 elements: 16- but not 32-byte aligned rows
+    assert out.data_ptr() % 32 == 16
+    o2, l2 = fa.flash_mla_with_kvcache(d["q"], d["kc"], d["bt"], d["lens"], D_V, meta, splits,
+                                       softmax_scale=SCALE, out=out)
+    torch.cuda.synchronize()
+    _status_ok()
+    assert o2.data_ptr() == out.data_ptr()
+    assert torch.equal(out, ref_o) and torch.equal(l2, ref_l)
+    assert torch.isnan(big[..., :8]).all()  # nothing written outside the view
+
+
 def test_zero_length_sequence():
     d = build_dense(13, [0, 100, 0], heads=128)
     out, lse, _, _ = _decode(d)
