@@ -29,7 +29,7 @@ cudaError_t launch_gqa_tc(const CUtensorMap &, const CUtensorMap &, const fa_dec
 cudaError_t launch_gqa_combine(const float *, const float *, const int4 *, int, int, int, int,
                                int, int, int, int, bool, void *, int, int64_t, int64_t, int64_t,
                                float *, cudaStream_t);
-int gqa_max_balanced_batch();
+int gqa_max_balanced_batch(int d);
 int gqa_tile_tokens(int d);
 cudaError_t launch_mla_sv(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                           const CUtensorMap &, const fa_mla_args *, int, cudaStream_t);
@@ -118,12 +118,18 @@ int encode_map4(CUtensorMap *map, const void *base, int dtype, uint64_t d, uint6
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(row_stride) * 2,
                            static_cast<cuuint64_t>(head_stride) * 2,
                            static_cast<cuuint64_t>(group_stride) * 2};
-  cuuint32_t box[4] = {64, box_rows, box_heads, 1};
+  // boxes of up to 64 dims: one swizzle row of 128 bytes, or of 64 / 32
+  // bytes for head sizes 32 / 16 (the kernel's operand layout follows)
+  const uint32_t inner = d < 64 ? static_cast<uint32_t>(d) : 64u;
+  const CUtensorMapSwizzle swz = inner == 64   ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : inner == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                               : CU_TENSOR_MAP_SWIZZLE_32B;
+  cuuint32_t box[4] = {inner, box_rows, box_heads, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   CUresult r = enc(map, dtype == FA_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                               : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                    4, const_cast<void *>(base), dims, strides, box, es,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(FA_ERR_INVALID_ARGUMENT,
@@ -222,9 +228,9 @@ int validate_decode(const fa_decode_args *a, bool tc) {
                 a->num_splits);
   if (a->num_splits == 0 && !a->sched)
     return fail(FA_ERR_INVALID_ARGUMENT, "the balanced schedule needs the sched scratch");
-  if (a->num_splits == 0 && a->batch > fa::gqa_max_balanced_batch())
+  if (a->num_splits == 0 && a->batch > fa::gqa_max_balanced_batch(a->d_qk))
     return fail(FA_ERR_UNSUPPORTED, "balanced schedule: at most %d sequences per call",
-                fa::gqa_max_balanced_batch());
+                fa::gqa_max_balanced_batch(a->d_qk));
   if (a->num_splits != 1 && (!a->part_o || !a->part_lse || !aligned16(a->part_o)))
     return fail(FA_ERR_INVALID_ARGUMENT, "split decode needs 16-byte aligned f32 workspace");
   if (a->num_splits > 1 && a->partition_size <= 0)
@@ -446,9 +452,9 @@ int fa_decode_workspace_size(const fa_decode_args *a, size_t *part_o_bytes,
     int sms = 0;
     int st = current_sm_count(&sms);
     if (st != FA_OK) return st;
-    if (a->batch > fa::gqa_max_balanced_batch())
+    if (a->batch > fa::gqa_max_balanced_batch(a->d_qk))
       return fail(FA_ERR_UNSUPPORTED, "balanced schedule: at most %d sequences per call",
-                  fa::gqa_max_balanced_batch());
+                  fa::gqa_max_balanced_batch(a->d_qk));
     // two split slots per CTA (its first and its last piece); one int4 merge
     // record per entry
     slots = 2 * static_cast<size_t>(sms);

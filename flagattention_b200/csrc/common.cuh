@@ -525,6 +525,21 @@ __device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr, uint32_t lbo,
   d |= 4ull << 61;  // SWIZZLE_64B
   return d;
 }
+// Operand in the swizzle layout of `row_bytes`-byte rows (128, 64 or 32:
+// layout codes 2, 4, 6), 8-row atoms of 8 * row_bytes bytes.
+__host__ __device__ constexpr uint32_t smem_swizzle_code(int row_bytes) {
+  return row_bytes == 128 ? 2u : (row_bytes == 64 ? 4u : 6u);
+}
+__device__ __forceinline__ uint64_t smem_desc_swz(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                                  uint32_t code) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;  // version
+  d |= static_cast<uint64_t>(code) << 61;
+  return d;
+}
 // Instruction descriptor, kind::f16 with f32 accumulation.
 // fmt: 0 = f16, 1 = bf16; b_mn_major: B operand stored N-contiguous.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, int fmt, int b_mn_major) {

@@ -44,7 +44,7 @@ constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;    // log2 units (factor 256)
-constexpr int kMaxStages = 6;
+constexpr int kMaxStages = 12;
 
 // Tokens per tile (QK N, PV K): 128, or 64 for head size 256, where O (256
 // TMEM columns), two S / P buffers and one Q buffer fill the 512 columns.
@@ -53,10 +53,16 @@ __host__ __device__ constexpr int tile_tokens(int d) { return d == 256 ? 64 : 12
 template <int kD>
 struct Plan {
   static constexpr int kTile = tile_tokens(kD);
-  static constexpr int kChunks = kD / 64;
-  static constexpr int kChunkBytes = kTile * 128;                // tile rows x 64 dims
-  static constexpr int kTileBytes = kChunks * kChunkBytes;       // 16 or 32 KB
-  static constexpr int kStages = kD == 64 ? 6 : 3;               // per ring
+  // a chunk: up to 64 dims of every tile row, one swizzle row of kRowBytes
+  // (128; 64 / 32 for head sizes 32 / 16, with the matching swizzle)
+  static constexpr int kChunkDims = kD < 64 ? kD : 64;
+  static constexpr int kRowBytes = 2 * kChunkDims;
+  static constexpr int kChunks = kD / kChunkDims;
+  static constexpr int kChunkBytes = kTile * kRowBytes;
+  static constexpr int kTileBytes = kChunks * kChunkBytes;       // 4 to 32 KB
+  static constexpr uint32_t kSwizzle = smem_swizzle_code(kRowBytes);
+  static constexpr uint32_t kAtomBytes = 8 * kRowBytes;          // 8-row swizzle atom
+  static constexpr int kStages = kD <= 32 ? 12 : (kD == 64 ? 6 : 3);  // per ring
   static constexpr int kQBufs = kD == 256 ? 1 : 2;               // Q buffers in TMEM
   static constexpr int kOffK = 1024;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
@@ -67,8 +73,8 @@ struct Plan {
   static constexpr int kSmemBytes = kSmemUsed + 1024;            // base alignment slack
   // TMEM columns: O, two S / P buffers, Q buffers (bf16 / f16 pairs)
   static constexpr uint32_t kColO = 0;
-  static constexpr uint32_t kColS = kD;
-  static constexpr uint32_t kColQ = kD + 2 * kTile;
+  static constexpr uint32_t kColS = kD < 64 ? 64 : kD;
+  static constexpr uint32_t kColQ = kColS + 2 * kTile;
   static_assert(kColQ + kQBufs * kD / 2 <= kTmemCols, "TMEM plan");
   static_assert(kStages <= kMaxStages, "ring");
   static_assert(kSmemBytes <= 232448, "shared memory plan exceeds 227 KB");
@@ -302,20 +308,26 @@ __device__ __forceinline__ void write_q(const Params &p, const Piece &pc, bool l
   const int h = pc.kvh * p.group + g_idx;
   const uint4 *src = reinterpret_cast<const uint4 *>(
       static_cast<const T *>(p.q) + pc.b * p.q_sb + h * p.q_sh + m_idx * p.q_sm);
-  // 64 dims (32 packed words) at a time: a 256-wide row would hold 128
-  // registers at once
+  // up to 64 dims (32 packed words) at a time: a 256-wide row would hold
+  // 128 registers at once
+  constexpr int kW = kD >= 64 ? 32 : kD / 2;
 #pragma unroll
-  for (int j = 0; j < kD / 64; ++j) {
-    uint32_t w[32];
+  for (int j = 0; j < kD / 2 / kW; ++j) {
+    uint32_t w[kW];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint4 v = live ? __ldg(src + 8 * j + i) : make_uint4(0u, 0u, 0u, 0u);
+    for (int i = 0; i < kW / 4; ++i) {
+      const uint4 v = live ? __ldg(src + (kW / 4) * j + i) : make_uint4(0u, 0u, 0u, 0u);
       w[4 * i] = v.x;
       w[4 * i + 1] = v.y;
       w[4 * i + 2] = v.z;
       w[4 * i + 3] = v.w;
     }
-    tmem_st32(t_q + 32 * j, w);
+    if constexpr (kW == 32)
+      tmem_st32(t_q + kW * j, w);
+    else if constexpr (kW == 16)
+      tmem_st16p(t_q + kW * j, w);
+    else
+      tmem_st8p(t_q + kW * j, w);
   }
   tmem_wait_st();
   tc_fence_before();
@@ -375,23 +387,27 @@ __device__ __forceinline__ bool epilogue(const Params &p, const Piece &pc, bool 
   T *orow = pc.final_out
                 ? static_cast<T *>(p.o) + pc.b * p.o_sb + h * p.o_sh + m_idx * p.o_sm
                 : static_cast<T *>(p.part_o) + (static_cast<int64_t>(pc.slot) * p.rows + r) * kD;
+  constexpr int kOG = kD < 32 ? kD : 32;  // output columns per TMEM load
 #pragma unroll 1
-  for (int j = 0; j < kD / 32; ++j) {
-    float v[32];
+  for (int j = 0; j < kD / kOG; ++j) {
+    float v[kOG];
     if (has_tiles) {
-      tmem_ld32(t_o + 32 * j, v);
+      if constexpr (kOG == 32)
+        tmem_ld32(t_o + 32 * j, v);
+      else
+        tmem_ld16(t_o + kOG * j, v);
       tmem_wait_ld();
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      for (int i = 0; i < kOG; ++i) v[i] = 0.f;
     }
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] *= f;
+    for (int i = 0; i < kOG; ++i) v[i] *= f;
     if (kC == 1) {
       if (live) {
-        uint4 *dst = reinterpret_cast<uint4 *>(orow + 32 * j);
+        uint4 *dst = reinterpret_cast<uint4 *>(orow + kOG * j);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < kOG / 8; ++i) {
           uint4 u;
           u.x = Elem<T>::pack2(v[8 * i], v[8 * i + 1]);
           u.y = Elem<T>::pack2(v[8 * i + 2], v[8 * i + 3]);
@@ -403,9 +419,9 @@ __device__ __forceinline__ bool epilogue(const Params &p, const Piece &pc, bool 
     } else {
       float *mine = stage + (warp * 32 + lane) * 33;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) mine[i] = v[i];
+      for (int i = 0; i < kOG; ++i) mine[i] = v[i];
       if (!rs.sync(abort_flag, p.status)) return false;
-      for (int rr = warp; rr < p.rows; rr += 4) {
+      for (int rr = warp; rr < p.rows && lane < kOG; rr += 4) {
         const int q = rr >> 5, i = rr & 31;
         float sum = 0.f;
 #pragma unroll
@@ -415,7 +431,7 @@ __device__ __forceinline__ bool epilogue(const Params &p, const Piece &pc, bool 
                     ? static_cast<T *>(p.o) + pc.b * p.o_sb + (pc.kvh * p.group + g2) * p.o_sh +
                           m2 * p.o_sm
                     : static_cast<T *>(p.part_o) + (static_cast<int64_t>(pc.slot) * p.rows + rr) * kD;
-        o2[32 * j + lane] = Elem<T>::from_f(sum);
+        o2[kOG * j + lane] = Elem<T>::from_f(sum);
       }
       if (!rs.sync(abort_flag, p.status)) return false;
     }
@@ -569,15 +585,22 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
         if (__any_sync(0xffffffffu, resc)) {
           tc_fence_after();
           const float a = resc ? alpha : 1.f;
+          constexpr int kOG = kD < 32 ? kD : 32;
 #pragma unroll 1
-          for (int j = 0; j < kD / 32; ++j) {
-            float v[32];
-            uint32_t u[32];
-            tmem_ld32(t_o + 32 * j, v);
+          for (int j = 0; j < kD / kOG; ++j) {
+            float v[kOG];
+            uint32_t u[kOG];
+            if constexpr (kOG == 32)
+              tmem_ld32(t_o + 32 * j, v);
+            else
+              tmem_ld16(t_o + kOG * j, v);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(v[i] * a);
-            tmem_st32(t_o + 32 * j, u);
+            for (int i = 0; i < kOG; ++i) u[i] = __float_as_uint(v[i] * a);
+            if constexpr (kOG == 32)
+              tmem_st32(t_o + 32 * j, u);
+            else
+              tmem_st16(t_o + kOG * j, u);
           }
         }
       }
@@ -594,11 +617,12 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
                                p.status, kDevTimeoutSoftmax)))
             break;
           const uint32_t tile = vbase + st * PL::kTileBytes;
-          const int units = (r1 - r0) * 8;
+          constexpr int kUnits = PL::kRowBytes / 16;  // 16-byte units per chunk row
+          const int units = (r1 - r0) * kUnits;
           for (int u = lane; u < units * PL::kChunks; u += 32) {
             const int ch = u / units, rem = u % units;
-            const uint32_t addr =
-                tile + ch * PL::kChunkBytes + (r0 + rem / 8) * 128 + (rem % 8) * 16;
+            const uint32_t addr = tile + ch * PL::kChunkBytes + (r0 + rem / kUnits) * PL::kRowBytes +
+                                  (rem % kUnits) * 16;
             asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u)
                          : "memory");
           }
@@ -751,8 +775,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane < nbox) {
 #pragma unroll
           for (int ch = 0; ch < PL::kChunks; ++ch)
-            tma_load_4d(kbase + st * PL::kTileBytes + ch * PL::kChunkBytes + lane * p.box_rows * 128,
-                        &k_map, kf, ch * 64, y, pc.kvh, page);
+            tma_load_4d(kbase + st * PL::kTileBytes + ch * PL::kChunkBytes +
+                            lane * p.box_rows * PL::kRowBytes,
+                        &k_map, kf, ch * PL::kChunkDims, y, pc.kvh, page);
         }
         ++gk;
         if (!(ok = warp_wait(smem_u32(&bars->v_empty[st]), ph, abort_flag, p.status,
@@ -764,8 +789,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane < nbox) {
 #pragma unroll
           for (int ch = 0; ch < PL::kChunks; ++ch)
-            tma_load_4d(vbase + st * PL::kTileBytes + ch * PL::kChunkBytes + lane * p.box_rows * 128,
-                        &v_map, vf, ch * 64, y, pc.kvh, page);
+            tma_load_4d(vbase + st * PL::kTileBytes + ch * PL::kChunkBytes +
+                            lane * p.box_rows * PL::kRowBytes,
+                        &v_map, vf, ch * PL::kChunkDims, y, pc.kvh, page);
         }
         ++gv;
       }
@@ -787,8 +813,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t kIdescQK = umma_idesc_f16(128, PL::kTile, fmt, 0);
     constexpr uint32_t kIdescPV = umma_idesc_f16(128, kD, fmt, 1);
     const uint32_t kbase = smem_u32(smem + PL::kOffK), vbase = smem_u32(smem + PL::kOffV);
-    const uint64_t k_desc = smem_desc_sw128(kbase, 16, 1024);
-    const uint64_t v_desc = smem_desc_sw128(vbase, PL::kChunkBytes, 1024);
+    const uint64_t k_desc = smem_desc_swz(kbase, 16, PL::kAtomBytes, PL::kSwizzle);
+    const uint64_t v_desc = smem_desc_swz(vbase, PL::kChunkBytes, PL::kAtomBytes, PL::kSwizzle);
     uint32_t g = 0, k = 0;
     bool ok = true;
     int pend = -1;             // tile whose PV is still to be issued
@@ -806,7 +832,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int kk = 0; kk < PL::kTile / 16; ++kk)
         umma_ts_warp(tmem + PL::kColO, tmem + PL::kColS + buf * PL::kTile + kk * 8,
-                     vd + static_cast<uint64_t>((kk * 16 * 128) >> 4), kIdescPV,
+                     vd + static_cast<uint64_t>((kk * 16 * PL::kRowBytes) >> 4), kIdescPV,
                      (first && kk == 0) ? 0u : 1u);
       tc_commit_warp(smem_u32(&bars->v_empty[st]));
       tc_commit_warp(smem_u32(&bars->pv_done));
@@ -834,7 +860,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int ch = 0; ch < PL::kChunks; ++ch)
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
+          for (int kk = 0; kk < PL::kChunkDims / 16; ++kk)
             umma_ts_warp(sd, qcol + ch * 32 + kk * 8,
                          kd + static_cast<uint64_t>((ch * PL::kChunkBytes + kk * 32) >> 4), kIdescQK,
                          (ch | kk) ? 1u : 0u);
@@ -895,34 +921,45 @@ cudaError_t launch_d(const CUtensorMap &km, const CUtensorMap &vm, const Params 
 
 }  // namespace gqa
 
-int gqa_max_balanced_batch() {
-  // the scan holds batch + 1 int64 in the K and V rings (same size for every
-  // head size)
-  static_assert(gqa::Plan<64>::kOffStage - gqa::Plan<64>::kOffK ==
-                        gqa::Plan<128>::kOffStage - gqa::Plan<128>::kOffK &&
-                    gqa::Plan<256>::kOffStage - gqa::Plan<256>::kOffK ==
-                        gqa::Plan<128>::kOffStage - gqa::Plan<128>::kOffK,
-                "ring sizes");
-  return (gqa::Plan<128>::kOffStage - gqa::Plan<128>::kOffK) / 8 - 1;
+namespace gqa {
+// f(Plan<d>) for the head sizes the kernel serves
+template <typename F>
+auto by_head(int d, F f) {
+  switch (d) {
+    case 16: return f(Plan<16>{});
+    case 32: return f(Plan<32>{});
+    case 64: return f(Plan<64>{});
+    case 256: return f(Plan<256>{});
+    default: return f(Plan<128>{});
+  }
+}
+}  // namespace gqa
+
+// Sequences the balanced schedule can scan at once for head size d: the scan
+// holds batch + 1 int64 in the (still empty) K and V rings.
+int gqa_max_balanced_batch(int d) {
+  return gqa::by_head(d, [](auto pl) {
+    using PL = decltype(pl);
+    return static_cast<int>((PL::kOffStage - PL::kOffK) / 8 - 1);
+  });
 }
 
 size_t gqa_smem_bytes(int d) {
-  return d == 64    ? gqa::Plan<64>::kSmemBytes
-         : d == 256 ? gqa::Plan<256>::kSmemBytes
-                    : gqa::Plan<128>::kSmemBytes;
+  return gqa::by_head(d, [](auto pl) { return static_cast<size_t>(decltype(pl)::kSmemBytes); });
 }
 
 int gqa_tile_tokens(int d) { return gqa::tile_tokens(d); }
 
-// The tensor-core kernel serves bf16 / f16 with d_qk == d_v in {64, 128,
-// 256}, at most 128 query rows per kv head, a positive scale, 16-byte aligned
-// rows and pages of at least 16 tokens that divide the tile (128 tokens; 64
-// for head size 256) or are a multiple of it.
+// The tensor-core kernel serves bf16 / f16 with d_qk == d_v in {16, 32, 64,
+// 128, 256}, at most 128 query rows per kv head, a positive scale, 16-byte
+// aligned rows and pages of at least 16 tokens that divide the tile (128
+// tokens; 64 for head size 256) or are a multiple of it.
 bool gqa_tc_eligible(const fa_decode_args *a) {
   auto al16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
   auto m8 = [](int64_t x) { return x % 8 == 0; };
   if (a->dtype != FA_DTYPE_BF16 && a->dtype != FA_DTYPE_F16) return false;
-  if (a->d_qk != a->d_v || (a->d_qk != 64 && a->d_qk != 128 && a->d_qk != 256)) return false;
+  const int d = a->d_qk;
+  if (a->d_qk != a->d_v || (d != 16 && d != 32 && d != 64 && d != 128 && d != 256)) return false;
   if (a->num_kv_heads <= 0 || a->num_q_heads % a->num_kv_heads) return false;
   const int64_t rows = static_cast<int64_t>(a->num_q_heads / a->num_kv_heads) * a->m_q;
   if (rows < 1 || rows > 128) return false;
@@ -988,6 +1025,12 @@ cudaError_t launch_gqa_tc(const CUtensorMap &km, const CUtensorMap &vm, const fa
   if (a->d_qk == 256)
     return f16 ? gqa::launch_d<__half, 256>(km, vm, p, grid, pdl, stream)
                : gqa::launch_d<__nv_bfloat16, 256>(km, vm, p, grid, pdl, stream);
+  if (a->d_qk == 32)
+    return f16 ? gqa::launch_d<__half, 32>(km, vm, p, grid, pdl, stream)
+               : gqa::launch_d<__nv_bfloat16, 32>(km, vm, p, grid, pdl, stream);
+  if (a->d_qk == 16)
+    return f16 ? gqa::launch_d<__half, 16>(km, vm, p, grid, pdl, stream)
+               : gqa::launch_d<__nv_bfloat16, 16>(km, vm, p, grid, pdl, stream);
   return f16 ? gqa::launch_d<__half, 128>(km, vm, p, grid, pdl, stream)
              : gqa::launch_d<__nv_bfloat16, 128>(km, vm, p, grid, pdl, stream);
 }

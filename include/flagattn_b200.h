@@ -106,7 +106,7 @@ int fa_split_kv_num_splits(int batch, int heads, int m, int n, int block_m,
  * Two kernels serve it:
  *  - the tensor-core kernel (tcgen05 + TMA), used whenever
  *    fa_decode_uses_tensor_cores() says so: bf16/f16, d_qk == d_v in
- *    {64, 128, 256}, at most 128 query rows per kv head (group * m_q),
+ *    {16, 32, 64, 128, 256}, at most 128 query rows per kv head (group * m_q),
  *    scale > 0, 16-byte aligned rows, and (paged) num_pages > 0 with a page
  *    size of at least 16 tokens that divides the tile (128 tokens, 64 for
  *    head size 256) or is a multiple of it.  num_splits == 0 selects its

@@ -4,8 +4,9 @@ The reference's paged test grid runs through the same kernel in
 test_gpu_generic.py; these cases pin what is specific to the tensor-core
 path: that it is the path taken, the balanced schedule of (sequence, kv head)
 entries bit-for-bit against its host specification, the copy layouts for
-1..128 query rows per kv head, head sizes 64, 128 and 256 (the last on
-64-token tiles), value rows past a sequence end holding NaN,
+1..128 query rows per kv head, head sizes 16, 32 (32- / 64-byte swizzled
+tiles), 64, 128 and 256 (64-token tiles), value rows past a sequence end
+holding NaN,
 explicit and automatic split counts, causal multi-token rows on contiguous
 caches, and a clean status word.
 """
@@ -75,7 +76,8 @@ def _args_for(q, k, lens, bt, out):
 @pytest.mark.parametrize("d, group, block, dtype, want", [
     (128, 8, 16, torch.float16, 1), (64, 1, 256, torch.bfloat16, 1), (128, 128, 128,
                                                                        torch.float16, 1),
-    (32, 8, 16, torch.float16, 0), (128, 8, 16, torch.float32, 0), (128, 8, 48, torch.float16, 0),
+    (32, 8, 16, torch.float16, 1), (16, 1, 128, torch.bfloat16, 1), (48, 8, 16, torch.float16, 0),
+    (128, 8, 16, torch.float32, 0), (128, 8, 48, torch.float16, 0),
     (128, 256, 16, torch.float16, 0), (256, 8, 16, torch.bfloat16, 1),
     (256, 4, 128, torch.float16, 1), (256, 8, 32, torch.float16, 1), (256, 8, 96, torch.float16, 0)])
 def test_tensor_core_path_selection(d, group, block, dtype, want):
@@ -86,7 +88,7 @@ def test_tensor_core_path_selection(d, group, block, dtype, want):
     assert _lib.lib().fa_decode_uses_tensor_cores(ctypes.byref(a)) == want
 
 
-@pytest.mark.parametrize("d", [64, 256])
+@pytest.mark.parametrize("d", [32, 64, 256])
 def test_balanced_schedule_bit_exact(d):
     """The merge records the kernel writes for every entry equal the host
     specification (oracle.gqa_schedule; 128-token blocks, 64 for head size
@@ -127,7 +129,7 @@ def test_balanced_schedule_bit_exact(d):
 
 @pytest.mark.parametrize("hq, group", [(64, 1), (64, 8), (16, 16), (64, 32), (64, 64), (96, 96),
                                        (128, 128)])
-@pytest.mark.parametrize("d", [64, 128, 256])
+@pytest.mark.parametrize("d", [16, 32, 64, 128, 256])
 def test_rows_per_kv_head(hq, group, d):
     """1..128 query rows per kv head: four, two or one copies of each row."""
     q, k, v, lens, bt, scale = _paged_inputs(5, hq, group, d, 16, 700, torch.bfloat16, group + d)
@@ -140,7 +142,7 @@ def test_rows_per_kv_head(hq, group, d):
 
 
 @pytest.mark.parametrize("d, block", [(128, 16), (128, 128), (128, 256), (256, 16),
-                                      (256, 128)])
+                                      (256, 128), (32, 16), (16, 128)])
 @pytest.mark.parametrize("num_splits", [0, 1, 3, 8])
 def test_nan_past_sequence_end_and_splits(d, block, num_splits):
     """Value / key slots past each sequence's end in its last page hold NaN;
@@ -184,7 +186,7 @@ def test_bench_shape_matches_oracle():
 
 @pytest.mark.parametrize("M", [1, 3, 4])
 @pytest.mark.parametrize("causal", [False, True])
-@pytest.mark.parametrize("D", [128, 256])
+@pytest.mark.parametrize("D", [16, 32, 128, 256])
 def test_contiguous_causal_rows(M, causal, D):
     """Contiguous caches (split-KV decoding) with several query tokens per
     sequence and bottom-right causal masking, GQA group 4."""
