@@ -29,8 +29,9 @@ cudaError_t launch_gqa_tc(const CUtensorMap &, const CUtensorMap &, const fa_dec
 cudaError_t launch_gqa_combine(const float *, const float *, const int4 *, int, int, int, int,
                                int, int, int, int, bool, void *, int, int64_t, int64_t, int64_t,
                                float *, cudaStream_t);
-int gqa_max_balanced_batch(int d);
-int gqa_tile_tokens(int d);
+int gqa_max_balanced_batch(const fa_decode_args *);
+int gqa_tile_tokens(const fa_decode_args *);
+int gqa_box_rows(const fa_decode_args *);
 cudaError_t launch_mla_sv(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                           const CUtensorMap &, const fa_mla_args *, int, cudaStream_t);
 }  // namespace fa
@@ -164,14 +165,14 @@ int encode_gather_map(CUtensorMap *map, const void *base, int dtype, uint64_t ro
   return FA_OK;
 }
 
-// K and V tensor maps of the grouped-query kernel: boxes of 64 dims x one
-// page (at most one tile: 128 rows, 64 for head size 256) over {d, page rows,
-// kv heads, pages}, or one tile of rows over {d, n, kv heads, batch} for
-// contiguous caches.
+// K and V tensor maps of the grouped-query kernel: boxes of up to 64 dims x
+// one page (at most one tile: 128 rows, 64 for head size 256, 64 of a
+// 192-token tile for smaller heads) over {d, page rows, kv heads, pages}, or
+// one tile of rows over {d, n, kv heads, batch} for contiguous caches.
 int encode_kv_maps(const fa_decode_args *a, CUtensorMap *km, CUtensorMap *vm) {
   const bool paged = a->block_table != nullptr;
-  const int tile = fa::gqa_tile_tokens(a->d_qk);
-  const uint32_t box_rows = static_cast<uint32_t>(paged && a->page_size < tile ? a->page_size : tile);
+  const uint32_t box_rows = static_cast<uint32_t>(
+      paged ? fa::gqa_box_rows(a) : fa::gqa_tile_tokens(a));
   const uint64_t rows = paged ? a->page_size : static_cast<uint64_t>(a->n_ctx > 0 ? a->n_ctx : 1);
   const uint64_t groups = paged ? a->num_pages : a->batch;
   int st = encode_map4(km, a->k, a->dtype, a->d_qk, rows, a->num_kv_heads, groups,
@@ -228,9 +229,9 @@ int validate_decode(const fa_decode_args *a, bool tc) {
                 a->num_splits);
   if (a->num_splits == 0 && !a->sched)
     return fail(FA_ERR_INVALID_ARGUMENT, "the balanced schedule needs the sched scratch");
-  if (a->num_splits == 0 && a->batch > fa::gqa_max_balanced_batch(a->d_qk))
+  if (a->num_splits == 0 && a->batch > fa::gqa_max_balanced_batch(a))
     return fail(FA_ERR_UNSUPPORTED, "balanced schedule: at most %d sequences per call",
-                fa::gqa_max_balanced_batch(a->d_qk));
+                fa::gqa_max_balanced_batch(a));
   if (a->num_splits != 1 && (!a->part_o || !a->part_lse || !aligned16(a->part_o)))
     return fail(FA_ERR_INVALID_ARGUMENT, "split decode needs 16-byte aligned f32 workspace");
   if (a->num_splits > 1 && a->partition_size <= 0)
@@ -452,9 +453,9 @@ int fa_decode_workspace_size(const fa_decode_args *a, size_t *part_o_bytes,
     int sms = 0;
     int st = current_sm_count(&sms);
     if (st != FA_OK) return st;
-    if (a->batch > fa::gqa_max_balanced_batch(a->d_qk))
+    if (a->batch > fa::gqa_max_balanced_batch(a))
       return fail(FA_ERR_UNSUPPORTED, "balanced schedule: at most %d sequences per call",
-                  fa::gqa_max_balanced_batch(a->d_qk));
+                  fa::gqa_max_balanced_batch(a));
     // two split slots per CTA (its first and its last piece); one int4 merge
     // record per entry
     slots = 2 * static_cast<size_t>(sms);

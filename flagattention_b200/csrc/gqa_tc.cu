@@ -46,13 +46,26 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;    // log2 units (factor 256)
 constexpr int kMaxStages = 12;
 
-// Tokens per tile (QK N, PV K): 128, or 64 for head size 256, where O (256
-// TMEM columns), two S / P buffers and one Q buffer fill the 512 columns.
-__host__ __device__ constexpr int tile_tokens(int d) { return d == 256 ? 64 : 128; }
+// Tokens per tile (QK N, PV K) for head size d and `rows` query rows per kv
+// head: 128; 64 for head size 256, where O (256 TMEM columns), two S / P
+// buffers and one Q buffer fill the 512 columns; 192 for head sizes up to 64
+// with at most 64 rows (two or four row copies), whose tiles carry few bytes
+// and are paced by per-tile latency (O, two 192-column S / P buffers and two
+// Q buffers still fit; with one copy a 192-column row would spill).
+__host__ __device__ constexpr int tile_tokens(int d, int rows) {
+  return d == 256 ? 64 : (d <= 64 && rows <= 64 ? 192 : 128);
+}
+// the tile of a kernel instance with kC copies of each row
+__host__ __device__ constexpr int tile_of(int d, int kC) { return tile_tokens(d, kC >= 2 ? 64 : 128); }
+// Rows of one TMA box: a whole page up to the tile (pages divide it), or 64
+// rows for 192-token tiles over pages of 64 tokens or more.
+__host__ __device__ constexpr int box_rows_for(int tile, int page) {
+  return tile == 192 ? (page < 64 ? page : 64) : (page < tile ? page : tile);
+}
 
-template <int kD>
+template <int kD, int kTileTokens>
 struct Plan {
-  static constexpr int kTile = tile_tokens(kD);
+  static constexpr int kTile = kTileTokens;
   // a chunk: up to 64 dims of every tile row, one swizzle row of kRowBytes
   // (128; 64 / 32 for head sizes 32 / 16, with the matching swizzle)
   static constexpr int kChunkDims = kD < 64 ? kD : 64;
@@ -62,7 +75,9 @@ struct Plan {
   static constexpr int kTileBytes = kChunks * kChunkBytes;       // 4 to 32 KB
   static constexpr uint32_t kSwizzle = smem_swizzle_code(kRowBytes);
   static constexpr uint32_t kAtomBytes = 8 * kRowBytes;          // 8-row swizzle atom
-  static constexpr int kStages = kD <= 32 ? 12 : (kD == 64 ? 6 : 3);  // per ring
+  // per ring: 3 for heads 128 / 256, else up to 12 stages of 96 KB in all
+  static constexpr int kStages =
+      kD >= 128 ? 3 : (98304 / kTileBytes < kMaxStages ? 98304 / kTileBytes : kMaxStages);
   static constexpr int kQBufs = kD == 256 ? 1 : 2;               // Q buffers in TMEM
   static constexpr int kOffK = 1024;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
@@ -119,7 +134,7 @@ struct Params {
   const int32_t *seq_lens;     // nullptr: every sequence has n_ctx tokens
   int32_t n_ctx;
   int32_t batch, hq, hkv, group, m_q, rows, causal;
-  int32_t tile_n;              // tokens per tile (tile_tokens(d)): the schedule's block
+  int32_t tile_n;              // tokens per tile (tile_tokens): the schedule's block
   float scale_log2;
   // num_splits == 0: the balanced schedule (Share); a split entry's pieces
   // go to slot parts + p (its first piece, in CTA p) and slots p (every
@@ -145,7 +160,7 @@ struct Piece {
   bool entry_first; // holds the entry's first block (or the entry is empty)
   int p_lo, p_hi;   // CTAs holding the entry's first / last block (balanced)
   __device__ __forceinline__ int tiles(int tile) const {
-    return tok_end > tok0 ? (tok_end - (tok0 & ~(tile - 1)) + tile - 1) / tile : 0;
+    return tok_end > tok0 ? (tok_end - (tok0 - tok0 % tile) + tile - 1) / tile : 0;
   }
 };
 
@@ -451,7 +466,7 @@ __device__ __forceinline__ bool epilogue(const Params &p, const Piece &pc, bool 
 template <typename T, int kD, int kC>
 __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *smem,
                                          uint32_t tmem, int warp, int lane) {
-  using PL = Plan<kD>;
+  using PL = Plan<kD, tile_of(kD, kC)>;
   constexpr int kCols = PL::kTile / kC;  // tile columns of one copy
   constexpr int kWords = kCols / 2;    // packed P words of one copy
   volatile int *abort_flag = &bars->abort_flag;
@@ -498,7 +513,7 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
     // m + len - m_q (bottom-right alignment, split_kv.py:88-92)
     const int row_end = p.causal ? min(pc.tok_end, m_idx + pc.len - p.m_q + 1) : pc.tok_end;
     float m_use = -INFINITY, l = 0.f;
-    int n0 = pc.tok0 & ~(PL::kTile - 1);
+    int n0 = pc.tok0 - pc.tok0 % PL::kTile;
     for (int t = 0; t < n_tiles; ++t, ++g, n0 += PL::kTile) {
       const uint32_t buf = g & 1u;
       if (!(ok = warp_wait(smem_u32(&bars->s_full[buf]), (g >> 1) & 1u, abort_flag, p.status,
@@ -507,12 +522,11 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
       tc_fence_after();
       const uint32_t t_s = tmem + lane_off + PL::kColS + buf * PL::kTile;
       float s[kCols];
-      if constexpr (kCols == 16) {
-        tmem_ld16(t_s + copy * kCols, s);
-      } else {
 #pragma unroll
-        for (int j = 0; j < kCols / 32; ++j) tmem_ld32(t_s + copy * kCols + 32 * j, s + 32 * j);
-      }
+      for (int j = 0; j < kCols / 32; ++j) tmem_ld32(t_s + copy * kCols + 32 * j, s + 32 * j);
+      if constexpr (kCols % 32 == 16)
+        tmem_ld16(t_s + copy * kCols + kCols - 16,
+                  *reinterpret_cast<float(*)[16]>(s + kCols - 16));
       tmem_wait_ld();
       // rows past the group (zero Q, so S = 0) count as fully valid: their
       // P and O rows are never read
@@ -559,14 +573,11 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
       l += a0 + a1;
       // P over the S buffer: this copy's words, zeros over the other copies'
       auto st_words = [&](uint32_t addr, const uint32_t *src) {  // kWords words
-        if constexpr (kWords >= 32) {
+        constexpr int n32 = kWords / 32, rem = kWords % 32;
 #pragma unroll
-          for (int j = 0; j < kWords / 32; ++j) tmem_st32(addr + 32 * j, src + 32 * j);
-        } else if constexpr (kWords == 16) {
-          tmem_st16p(addr, src);
-        } else {
-          tmem_st8p(addr, src);
-        }
+        for (int j = 0; j < n32; ++j) tmem_st32(addr + 32 * j, src + 32 * j);
+        if constexpr (rem >= 16) tmem_st16p(addr + 32 * n32, src + 32 * n32);
+        if constexpr (rem % 16 == 8) tmem_st8p(addr + kWords - 8, src + kWords - 8);
       };
       st_words(t_s + copy * kWords, w);
       if constexpr (kC > 1) {
@@ -664,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gqa_decode_kernel(const __grid_constant__ CUtensorMap k_map,
                       const __grid_constant__ CUtensorMap v_map,
                       const __grid_constant__ Params p) {
-  using PL = Plan<kD>;
+  using PL = Plan<kD, tile_of(kD, kC)>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
@@ -739,7 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         p.merge[pc.e] = make_int4(pc.final_out ? -1 : sh->parts + pc.p_lo, pc.p_lo + 1,
                                   pc.p_hi - pc.p_lo, 0);
       const int n_tiles = pc.tiles(p.tile_n);
-      int n0 = pc.tok0 & ~(PL::kTile - 1);
+      int n0 = pc.tok0 - pc.tok0 % PL::kTile;
       // box of lane j: tokens [n0 + j * box_rows, + box_rows); boxes that
       // miss the piece read an out-of-range page (zero fill, no traffic).
       // The page numbers of the next tile are read one tile ahead, so the
@@ -896,12 +907,12 @@ cudaError_t launch_t(const CUtensorMap &km, const CUtensorMap &vm, const Params 
                      bool pdl, cudaStream_t stream) {
   auto kern = gqa_decode_kernel<T, kD, kC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       Plan<kD>::kSmemBytes);
+                                       Plan<kD, tile_of(kD, kC)>::kSmemBytes);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = Plan<kD>::kSmemBytes;
+  cfg.dynamicSmemBytes = Plan<kD, tile_of(kD, kC)>::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -922,38 +933,45 @@ cudaError_t launch_d(const CUtensorMap &km, const CUtensorMap &vm, const Params 
 }  // namespace gqa
 
 namespace gqa {
-// f(Plan<d>) for the head sizes the kernel serves
-template <typename F>
-auto by_head(int d, F f) {
-  switch (d) {
-    case 16: return f(Plan<16>{});
-    case 32: return f(Plan<32>{});
-    case 64: return f(Plan<64>{});
-    case 256: return f(Plan<256>{});
-    default: return f(Plan<128>{});
-  }
+int rows_of(const fa_decode_args *a) {
+  return a->num_kv_heads > 0 ? (a->num_q_heads / a->num_kv_heads) * a->m_q : 0;
+}
+// Ring bytes of the instance the arguments select (the balanced schedule's
+// scan lives there before the first copy).
+template <int kD>
+int ring_bytes(int rows) {
+  return rows <= 64 ? Plan<kD, tile_tokens(kD, 64)>::kOffStage - Plan<kD, tile_tokens(kD, 64)>::kOffK
+                    : Plan<kD, tile_tokens(kD, 128)>::kOffStage -
+                          Plan<kD, tile_tokens(kD, 128)>::kOffK;
 }
 }  // namespace gqa
 
-// Sequences the balanced schedule can scan at once for head size d: the scan
-// holds batch + 1 int64 in the (still empty) K and V rings.
-int gqa_max_balanced_batch(int d) {
-  return gqa::by_head(d, [](auto pl) {
-    using PL = decltype(pl);
-    return static_cast<int>((PL::kOffStage - PL::kOffK) / 8 - 1);
-  });
+// Sequences the balanced schedule can scan at once: batch + 1 int64 in the
+// (still empty) K and V rings.
+int gqa_max_balanced_batch(const fa_decode_args *a) {
+  const int rows = gqa::rows_of(a);
+  int bytes;
+  switch (a->d_qk) {
+    case 16: bytes = gqa::ring_bytes<16>(rows); break;
+    case 32: bytes = gqa::ring_bytes<32>(rows); break;
+    case 64: bytes = gqa::ring_bytes<64>(rows); break;
+    case 256: bytes = gqa::ring_bytes<256>(rows); break;
+    default: bytes = gqa::ring_bytes<128>(rows); break;
+  }
+  return bytes / 8 - 1;
 }
 
-size_t gqa_smem_bytes(int d) {
-  return gqa::by_head(d, [](auto pl) { return static_cast<size_t>(decltype(pl)::kSmemBytes); });
+int gqa_tile_tokens(const fa_decode_args *a) {
+  return gqa::tile_tokens(a->d_qk, gqa::rows_of(a));
 }
-
-int gqa_tile_tokens(int d) { return gqa::tile_tokens(d); }
+int gqa_box_rows(const fa_decode_args *a) {
+  return gqa::box_rows_for(gqa_tile_tokens(a), a->page_size);
+}
 
 // The tensor-core kernel serves bf16 / f16 with d_qk == d_v in {16, 32, 64,
 // 128, 256}, at most 128 query rows per kv head, a positive scale, 16-byte
-// aligned rows and pages of at least 16 tokens that divide the tile (128
-// tokens; 64 for head size 256) or are a multiple of it.
+// aligned rows and pages of at least 16 tokens that divide the TMA box
+// (box_rows_for, which must divide the tile) or are a multiple of it.
 bool gqa_tc_eligible(const fa_decode_args *a) {
   auto al16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
   auto m8 = [](int64_t x) { return x % 8 == 0; };
@@ -971,8 +989,9 @@ bool gqa_tc_eligible(const fa_decode_args *a) {
   if (a->block_table) {
     const int ps = a->page_size;
     if (ps < 16 || ps % 16) return false;
-    const int tile = gqa::tile_tokens(a->d_qk);
-    if (ps <= tile ? (tile % ps) : (ps % tile)) return false;
+    // boxes tile the tile; pages divide the box or are multiples of it
+    const int box = gqa_box_rows(a);
+    if (gqa_tile_tokens(a) % box || (ps <= box ? (box % ps) : (ps % box))) return false;
     if (a->num_pages <= 0) return false;
   }
   return true;
@@ -994,8 +1013,8 @@ cudaError_t launch_gqa_tc(const CUtensorMap &km, const CUtensorMap &vm, const fa
   p.bt_stride = a->bt_stride;
   p.page_size = a->page_size;
   p.num_pages = a->num_pages;
-  p.tile_n = gqa::tile_tokens(a->d_qk);
-  p.box_rows = a->block_table && a->page_size < p.tile_n ? a->page_size : p.tile_n;
+  p.tile_n = gqa_tile_tokens(a);
+  p.box_rows = a->block_table ? gqa_box_rows(a) : p.tile_n;
   p.seq_lens = a->seq_lens;
   p.n_ctx = a->n_ctx;
   p.batch = a->batch;

@@ -91,8 +91,8 @@ def test_tensor_core_path_selection(d, group, block, dtype, want):
 @pytest.mark.parametrize("d", [32, 64, 256])
 def test_balanced_schedule_bit_exact(d):
     """The merge records the kernel writes for every entry equal the host
-    specification (oracle.gqa_schedule; 128-token blocks, 64 for head size
-    256), and the outputs match the oracle."""
+    specification (oracle.gqa_schedule with the kernel's tile as the block),
+    and the outputs match the oracle."""
     rs = np.random.RandomState(7 + d)
     lib = _lib.lib()
     sms = torch.cuda.get_device_properties(0).multi_processor_count
@@ -121,7 +121,10 @@ def test_balanced_schedule_bit_exact(d):
         assert st == 0
         torch.cuda.synchronize()
         got = ws[po.value + pl.value:].view(torch.int32).view(-1, 4)[:, :3].cpu().numpy()
-        _, merge = oracle.gqa_schedule(lens, hkv, sms, block_n=64 if d == 256 else 128)
+        # tile tokens: 64 for head 256, 192 for heads up to 64 with at most
+        # 64 query rows per kv head, else 128
+        block_n = 64 if d == 256 else (192 if d <= 64 else 128)
+        _, merge = oracle.gqa_schedule(lens, hkv, sms, block_n=block_n)
         assert np.array_equal(got, np.asarray(merge, np.int32)), trial
         ref = _oracle(q, k, v, bt, lens_t, scale).to(torch.float16).float()
         assert torch.allclose(out.float().cpu(), ref, atol=2e-3, rtol=1e-5), trial
