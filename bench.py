@@ -389,8 +389,8 @@ def run_long_context(args, world, rank, dev, flush):
     rows and merges them.  The same step with one NCCL all-gather of
     packed partials (decode + combine, all-gather, merge) is timed beside it.
     At N = 1 the step is the plain decode (+ combine) to bf16.  Every phase is
-    timed with CUDA events on the launching stream; the figures are the max
-    over ranks."""
+    timed with CUDA events on the launching stream; every figure (each phase,
+    and the whole step of a rank) is the max over ranks."""
     import torch
     import torch.distributed as dist
 
@@ -431,8 +431,14 @@ def run_long_context(args, world, rank, dev, flush):
         if world > 1:
             dist.barrier()
         assert fat.read_status(dev) == 0, "device wait timeout in the timed region (long context)"
+        # per phase, and the whole step (first to last event) of this rank;
+        # each the max over ranks.  The step's max is not the sum of the
+        # phases' maxima: a rank whose decode ends early waits longer in the
+        # exchange for the others.
         t = torch.tensor([sum(e[k].elapsed_time(e[k + 1]) for e in evs) / steps
-                          for k in range(n_ev - 1)], dtype=torch.float64, device=dev)
+                          for k in range(n_ev - 1)] +
+                         [sum(e[0].elapsed_time(e[n_ev - 1]) for e in evs) / steps],
+                         dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.tolist()
@@ -452,8 +458,8 @@ def run_long_context(args, world, rank, dev, flush):
             call.run()
             ev[1].record(stream)
 
-        dec_ms, = timed(step, 2)
-        step_ms, xchg_ms = dec_ms, None
+        dec_ms, step_ms = timed(step, 2)
+        xchg_ms = None
         launches = 2
     else:
         # the product path: partials exchanged by peer stores (no collective)
@@ -467,8 +473,7 @@ def run_long_context(args, world, rank, dev, flush):
             peer.exchange()
             ev[2].record(stream)
 
-        dec_ms, xchg_ms = timed(step, 3)
-        step_ms = dec_ms + xchg_ms
+        dec_ms, xchg_ms, step_ms = timed(step, 3)
         launches = 2
         # for comparison: the same step with one NCCL all-gather of packed partials
         part = shard.PartialDecode(q, pool, bt, seq, D_QK ** -0.5)
@@ -484,8 +489,8 @@ def run_long_context(args, world, rank, dev, flush):
             shard.merge_partials(gathered, rows, D_V, torch.bfloat16)
             ev[3].record(stream)
 
-        n_dec, n_gather, n_merge = timed(step_nccl, 4)
-        extra = {"nccl_allgather_path": {"ms_per_step": n_dec + n_gather + n_merge,
+        n_dec, n_gather, n_merge, n_step = timed(step_nccl, 4)
+        extra = {"nccl_allgather_path": {"ms_per_step": n_step,
                                          "ms_decode_and_combine": n_dec,
                                          "us_allgather": n_gather * 1e3, "us_merge": n_merge * 1e3}}
         dist.barrier()

@@ -223,10 +223,14 @@ __global__ void __launch_bounds__(256, 2)
   const int tasks_x = (rows + rows_per_task<true>() - 1) / rows_per_task<true>();
   const int tasks = tasks_x * a.batch;
   unsigned long long done = 0;
-  for (int t = blockIdx.x; t < tasks; t += gridDim.x)
+  for (int t = blockIdx.x; t < tasks; t += gridDim.x) {
     done += push_rows<true>(a.part_o, a.part_lse, a.num_splits, a.out, a.o_sb, a.o_ss, a.o_sh,
                             a.lse_in, a.batch, a.s_q, a.h_q, a.d_v, peers, world, rank,
                             t % tasks_x, t / tasks_x, states);
+    // the folding warps have read every warp's state before the next task's
+    // states overwrite `states`
+    __syncthreads();
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     count_rows(peers, world, rank, done);
