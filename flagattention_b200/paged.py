@@ -10,11 +10,13 @@ Two paths, chosen by shape:
 * the MLA latent shape (one kv head, 576-dim keys, values = the first 512
   dims of the same cache rows, block size a multiple of 64, bf16/f16) runs on
   the tcgen05 tensor-core kernel with the balanced tile scheduler;
-* bf16/f16 with head size 64 or 128 and up to 128 query heads per kv head
-  runs the tcgen05 grouped-query kernel (``csrc/gqa_tc.cu``); with the
-  default ``num_splits=0`` the device scheduler balances the key blocks over
-  the SMs, an explicit ``num_splits`` keeps the reference's partitions;
-* every other shape (head sizes 16..512, f32) runs the CUDA-core kernel with
+* bf16/f16 with head size 16, 32, 64, 128 or 256, up to 128 query heads per
+  kv head and a block size that the kernel's TMA boxes tile runs the tcgen05
+  grouped-query kernel (``csrc/gqa_tc.cu``); with the default
+  ``num_splits=0`` the device scheduler balances the key blocks over the
+  SMs, an explicit ``num_splits`` keeps the reference's partitions;
+* every other shape (head size 512, f32, more heads per kv head) runs the
+  CUDA-core kernel with
   the reference's split rule (``paged.py:54-67``, bit-exact through
   ``fa_paged_num_splits``).
 """

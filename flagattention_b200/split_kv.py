@@ -4,8 +4,8 @@
 ``split_kv.py:279-344`` and ``flash_attention(..., return_log_normalizer=True)``
 the split branch of ``flash.py:72-171`` (forward only): q [B, H, M, D],
 k [B, Hk, N, D], v [B, Hk, N, Dv], bottom-right causal masking, grouped
-heads.  bf16/f16 with head size 64 or 128 (up to 128 query rows per kv
-head) runs the tcgen05 grouped-query kernel with the device scheduler's
+heads.  bf16/f16 with head size 16, 32, 64, 128 or 256 (up to 128 query
+rows per kv head) runs the tcgen05 grouped-query kernel with the device scheduler's
 balanced split; other shapes run the CUDA-core kernel with the reference
 heuristic (``num_splits_herustic``, ``split_kv.py:247-276``, bit-exact through
 ``fa_split_kv_num_splits``) and its split size ``cdiv(cdiv(N, 128), S) * 128``
