@@ -24,14 +24,15 @@ cudaError_t launch_mla_combine(const float *, const float *, const int32_t *, in
 cudaError_t launch_generic_decode(const fa_decode_args *, cudaStream_t);
 size_t generic_smem_bytes(int, int);
 bool gqa_tc_eligible(const fa_decode_args *);
-cudaError_t launch_gqa_tc(const CUtensorMap &, const CUtensorMap &, const fa_decode_args *,
+cudaError_t launch_gqa_tc(const CUtensorMap &, const CUtensorMap &, const fa_decode_args *, int,
                           int4 *, int, int, bool, cudaStream_t);
 cudaError_t launch_gqa_combine(const float *, const float *, const int4 *, int, int, int, int,
                                int, int, int, int, bool, void *, int, int64_t, int64_t, int64_t,
                                float *, cudaStream_t);
 int gqa_max_balanced_batch(const fa_decode_args *);
-int gqa_tile_tokens(const fa_decode_args *);
-int gqa_box_rows(const fa_decode_args *);
+int gqa_tile_tokens(const fa_decode_args *, int pair);
+int gqa_box_rows(const fa_decode_args *, int pair);
+bool gqa_pairs_heads(const fa_decode_args *);
 cudaError_t launch_mla_sv(const CUtensorMap &, const CUtensorMap &, const CUtensorMap &,
                           const CUtensorMap &, const fa_mla_args *, int, cudaStream_t);
 }  // namespace fa
@@ -169,30 +170,46 @@ int encode_gather_map(CUtensorMap *map, const void *base, int dtype, uint64_t ro
 // one page (at most one tile: 128 rows, 64 for head size 256, 64 of a
 // 192-token tile for smaller heads) over {d, page rows, kv heads, pages}, or
 // one tile of rows over {d, n, kv heads, batch} for contiguous caches.
-int encode_kv_maps(const fa_decode_args *a, CUtensorMap *km, CUtensorMap *vm) {
+// With `pair` (gqa_pairs_heads) a box spans two adjacent kv heads.  `a`
+// describes the real heads.
+int encode_kv_maps(const fa_decode_args *a, int pair, CUtensorMap *km, CUtensorMap *vm) {
   const bool paged = a->block_table != nullptr;
   const uint32_t box_rows = static_cast<uint32_t>(
-      paged ? fa::gqa_box_rows(a) : fa::gqa_tile_tokens(a));
+      paged ? fa::gqa_box_rows(a, pair) : fa::gqa_tile_tokens(a, pair));
+  const uint32_t box_heads = pair ? 2u : 1u;
   const uint64_t rows = paged ? a->page_size : static_cast<uint64_t>(a->n_ctx > 0 ? a->n_ctx : 1);
   const uint64_t groups = paged ? a->num_pages : a->batch;
   int st = encode_map4(km, a->k, a->dtype, a->d_qk, rows, a->num_kv_heads, groups,
-                       a->k_stride_tok, a->k_stride_head, a->k_stride_seq, box_rows);
+                       a->k_stride_tok, a->k_stride_head, a->k_stride_seq, box_rows, box_heads);
   if (st != FA_OK) return st;
   return encode_map4(vm, a->v, a->dtype, a->d_v, rows, a->num_kv_heads, groups, a->k_stride_tok,
-                     a->k_stride_head, a->k_stride_seq, box_rows);
+                     a->k_stride_head, a->k_stride_seq, box_rows, box_heads);
+}
+
+// The arguments as the tensor-core kernel sees them: with paired kv heads,
+// half the kv heads (and so twice the group), everything else unchanged.
+fa_decode_args kernel_view(const fa_decode_args *a, int pair) {
+  fa_decode_args v = *a;
+  if (pair) v.num_kv_heads /= 2;
+  return v;
 }
 
 // Tensor-core kernel for these arguments?  Shapes, types and alignment
 // (gqa_tc_eligible), a batch the maps can describe, and strides the TMA unit
 // accepts (the encoder is asked; it runs on the host only).
-bool tc_maps(const fa_decode_args *a, CUtensorMap *km, CUtensorMap *vm) {
+bool tc_maps(const fa_decode_args *a, CUtensorMap *km, CUtensorMap *vm, int *pair) {
+  *pair = 0;
   if (a->block_table == nullptr && a->seq_lens == nullptr && a->n_ctx < 1) return false;
   if (a->batch < 1 || !fa::gqa_tc_eligible(a)) return false;
-  return encode_kv_maps(a, km, vm) == FA_OK;
+  *pair = fa::gqa_pairs_heads(a) ? 1 : 0;
+  return encode_kv_maps(a, *pair, km, vm) == FA_OK;
 }
-bool decode_on_tensor_cores(const fa_decode_args *a) {
+bool decode_on_tensor_cores(const fa_decode_args *a, int *pair = nullptr) {
   CUtensorMap km, vm;
-  return tc_maps(a, &km, &vm);
+  int pr = 0;
+  const bool tc = tc_maps(a, &km, &vm, &pr);
+  if (pair) *pair = pr;
+  return tc;
 }
 
 int current_sm_count(int *sms) {
@@ -244,7 +261,7 @@ int validate_decode(const fa_decode_args *a, bool tc) {
 // The tensor-core path: K / V tensor maps, then (balanced schedule) the
 // scheduler kernel, the decode as its programmatic dependent and the merge
 // of split entries as the decode's.
-int run_decode_tc(const fa_decode_args *a, const CUtensorMap &km, const CUtensorMap &vm,
+int run_decode_tc(const fa_decode_args *a, const CUtensorMap &km, const CUtensorMap &vm, int pair,
                   cudaStream_t s) {
   int sms = 0;
   int st = current_sm_count(&sms);
@@ -257,7 +274,7 @@ int run_decode_tc(const fa_decode_args *a, const CUtensorMap &km, const CUtensor
     // every CTA cuts its share of the work out of the sequence lengths;
     // split entries leave merge records in the sched scratch
     int4 *merge = reinterpret_cast<int4 *>(a->sched);
-    e = fa::launch_gqa_tc(km, vm, a, merge, sms, sms, true, s);
+    e = fa::launch_gqa_tc(km, vm, a, pair, merge, sms, sms, true, s);
     if (e != cudaSuccess) return cuda_fail(e, "tensor-core decode launch");
     e = fa::launch_gqa_combine(a->part_o, a->part_lse, merge, 0, entries, qrows, a->m_q, group,
                                a->num_kv_heads, a->num_q_heads, a->d_v,
@@ -270,7 +287,7 @@ int run_decode_tc(const fa_decode_args *a, const CUtensorMap &km, const CUtensor
   const int64_t parts = static_cast<int64_t>(entries) * ns;
   if (parts > INT32_MAX) return fail(FA_ERR_UNSUPPORTED, "too many partitions");
   const int grid = static_cast<int>(parts < sms ? parts : sms);
-  e = fa::launch_gqa_tc(km, vm, a, nullptr, static_cast<int>(parts), grid, false, s);
+  e = fa::launch_gqa_tc(km, vm, a, pair, nullptr, static_cast<int>(parts), grid, false, s);
   if (e != cudaSuccess) return cuda_fail(e, "tensor-core decode launch");
   if (ns > 1) {
     e = fa::launch_gqa_combine(a->part_o, a->part_lse, nullptr, ns, entries, qrows, a->m_q, group,
@@ -286,12 +303,14 @@ int run_decode(const fa_decode_args *a, void *stream) {
   if (!a) return fail(FA_ERR_INVALID_ARGUMENT, "null args");
   // one eligibility test, one pair of tensor maps per call
   CUtensorMap km, vm;
-  const bool tc = tc_maps(a, &km, &vm);
-  int st = validate_decode(a, tc);
+  int pair = 0;
+  const bool tc = tc_maps(a, &km, &vm, &pair);
+  const fa_decode_args v = kernel_view(a, pair);  // the tensor-core kernel's view
+  int st = validate_decode(tc ? &v : a, tc);
   if (st != FA_OK) return st;
   if (a->batch == 0) return FA_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (tc) return run_decode_tc(a, km, vm, s);
+  if (tc) return run_decode_tc(&v, km, vm, pair, s);
   cudaError_t e = fa::launch_generic_decode(a, s);
   if (e != cudaSuccess) return cuda_fail(e, "generic decode launch");
   if (a->num_splits > 1) {
@@ -447,8 +466,12 @@ int fa_decode_workspace_size(const fa_decode_args *a, size_t *part_o_bytes,
       a->d_v <= 0 || a->num_splits < 0)
     return fail(FA_ERR_INVALID_ARGUMENT, "bad arguments");
   size_t slots = 0, sched = 0;
+  int pair = 0;
+  const bool tc = decode_on_tensor_cores(a, &pair);
+  const fa_decode_args v = kernel_view(a, pair);
+  if (tc) a = &v;  // sizes of the tensor-core kernel's view (paired kv heads)
   if (a->num_splits == 0) {
-    if (!decode_on_tensor_cores(a))
+    if (!tc)
       return fail(FA_ERR_INVALID_ARGUMENT, "num_splits 0 needs the tensor-core kernel");
     int sms = 0;
     int st = current_sm_count(&sms);

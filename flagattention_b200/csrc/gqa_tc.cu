@@ -135,6 +135,11 @@ struct Params {
   int32_t n_ctx;
   int32_t batch, hq, hkv, group, m_q, rows, causal;
   int32_t tile_n;              // tokens per tile (tile_tokens): the schedule's block
+  // pair != 0: an entry covers two adjacent kv heads (hkv and group above are
+  // the halved / doubled counts; pair_group is one head's group), each TMA
+  // box brings both heads' rows of a page, and a tile holds tile_n tokens of
+  // each head (tile columns [box][head][row])
+  int32_t pair, pair_group;
   float scale_log2;
   // num_splits == 0: the balanced schedule (Share); a split entry's pieces
   // go to slot parts + p (its first piece, in CTA p) and slots p (every
@@ -477,6 +482,8 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
   const bool live = r < p.rows;
   const int g_idx = live ? r / p.m_q : 0;
   const int m_idx = live ? r % p.m_q : 0;
+  const int hh_r = p.pair && live ? g_idx / p.pair_group : 0;  // head of the row within its pair
+  const int tt = p.tile_n;                                    // tokens per tile
   const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
   const uint32_t t_o = tmem + lane_off + PL::kColO;
   float *stage = reinterpret_cast<float *>(smem + PL::kOffStage);
@@ -513,8 +520,8 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
     // m + len - m_q (bottom-right alignment, split_kv.py:88-92)
     const int row_end = p.causal ? min(pc.tok_end, m_idx + pc.len - p.m_q + 1) : pc.tok_end;
     float m_use = -INFINITY, l = 0.f;
-    int n0 = pc.tok0 - pc.tok0 % PL::kTile;
-    for (int t = 0; t < n_tiles; ++t, ++g, n0 += PL::kTile) {
+    int n0 = pc.tok0 - pc.tok0 % tt;
+    for (int t = 0; t < n_tiles; ++t, ++g, n0 += tt) {
       const uint32_t buf = g & 1u;
       if (!(ok = warp_wait(smem_u32(&bars->s_full[buf]), (g >> 1) & 1u, abort_flag, p.status,
                            kDevTimeoutSoftmax)))
@@ -534,7 +541,28 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
       const int lo = live ? pc.tok0 - c0 : 0;
       const int hi = live ? row_end - c0 : kCols;
       float mx = -INFINITY;
-      if (__all_sync(0xffffffffu, lo <= 0 && hi >= kCols)) {
+      if (p.pair) {
+        // column cj: box cj >> (lgR + 1), head (cj >> lgR) & 1, token
+        // n0 + box * R + (cj & (R - 1))  (paired pages hold 16 or 32 tokens)
+        const int lgR = __ffs(p.box_rows) - 1;
+        if (__all_sync(0xffffffffu, !live || (n0 >= pc.tok0 && n0 + tt <= row_end))) {
+#pragma unroll
+          for (int j = 0; j < kCols; ++j) {
+            const int cj = copy * kCols + j;
+            s[j] = (!live || ((cj >> lgR) & 1) == hh_r) ? s[j] : -INFINITY;
+            mx = fmaxf(mx, s[j]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < kCols; ++j) {
+            const int cj = copy * kCols + j;
+            const int tok = n0 + ((cj >> (lgR + 1)) << lgR) + (cj & (p.box_rows - 1));
+            const bool ok_j = !live || (((cj >> lgR) & 1) == hh_r && tok >= pc.tok0 && tok < row_end);
+            s[j] = ok_j ? s[j] : -INFINITY;  // select: NaN-safe
+            mx = fmaxf(mx, s[j]);
+          }
+        }
+      } else if (__all_sync(0xffffffffu, lo <= 0 && hi >= kCols)) {
 #pragma unroll
         for (int j = 0; j < kCols; j += 2) mx = fmax3(mx, s[j], s[j + 1]);
       } else {
@@ -618,7 +646,7 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
       // Value rows past the sequence end inside the last loaded page may
       // hold any bits (even NaN); P is 0 there but 0 * NaN is not, so clear
       // them before the PV product.
-      if (warp == 0 && pc.len > n0 && pc.len < n0 + PL::kTile && pc.len <= pc.tok_end) {
+      if (warp == 0 && pc.len > n0 && pc.len < n0 + tt && pc.len <= pc.tok_end) {
         const int jb = (pc.len - 1 - n0) / p.box_rows;
         const int r0 = pc.len - n0, r1 = (jb + 1) * p.box_rows;
         const int btok = n0 + jb * p.box_rows;
@@ -630,9 +658,13 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
           const uint32_t tile = vbase + st * PL::kTileBytes;
           constexpr int kUnits = PL::kRowBytes / 16;  // 16-byte units per chunk row
           const int units = (r1 - r0) * kUnits;
-          for (int u = lane; u < units * PL::kChunks; u += 32) {
-            const int ch = u / units, rem = u % units;
-            const uint32_t addr = tile + ch * PL::kChunkBytes + (r0 + rem / kUnits) * PL::kRowBytes +
+          // paired heads: the box's rows are [head][row], cleared for both
+          const int row0 = p.pair ? 2 * jb * p.box_rows + (r0 - jb * p.box_rows) : r0;
+          for (int u = lane; u < units * PL::kChunks << p.pair; u += 32) {
+            const int hh = u / (units * PL::kChunks), uu = u % (units * PL::kChunks);
+            const int ch = uu / units, rem = uu % units;
+            const uint32_t addr = tile + ch * PL::kChunkBytes +
+                                  (row0 + hh * p.box_rows + rem / kUnits) * PL::kRowBytes +
                                   (rem % kUnits) * 16;
             asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u)
                          : "memory");
@@ -739,7 +771,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kProducerWarp) {
     // ------------------------------------------------------- TMA producer
     const uint32_t kbase = smem_u32(smem + PL::kOffK), vbase = smem_u32(smem + PL::kOffV);
-    const int nbox = PL::kTile / p.box_rows;
+    const int tt = p.tile_n;            // tokens per tile
+    const int nbox = tt / p.box_rows;
     uint32_t g = 0, gk = 0, gv = 0;  // tiles begun, K tiles issued, V tiles issued
     bool ok = true;
     const Share *sh = &bars->share;
@@ -750,7 +783,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         p.merge[pc.e] = make_int4(pc.final_out ? -1 : sh->parts + pc.p_lo, pc.p_lo + 1,
                                   pc.p_hi - pc.p_lo, 0);
       const int n_tiles = pc.tiles(p.tile_n);
-      int n0 = pc.tok0 - pc.tok0 % PL::kTile;
+      int n0 = pc.tok0 - pc.tok0 % tt;
       // box of lane j: tokens [n0 + j * box_rows, + box_rows); boxes that
       // miss the piece read an out-of-range page (zero fill, no traffic).
       // The page numbers of the next tile are read one tile ahead, so the
@@ -773,9 +806,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       int ny, npage;
       box_coord(n0, ny, npage);
-      for (int t = 0; t < n_tiles; ++t, ++g, n0 += PL::kTile) {
+      for (int t = 0; t < n_tiles; ++t, ++g, n0 += tt) {
         const int y = ny, page = npage;
-        if (t + 1 < n_tiles) box_coord(n0 + PL::kTile, ny, npage);
+        if (t + 1 < n_tiles) box_coord(n0 + tt, ny, npage);
         const uint32_t st = g % PL::kStages, ph = ((g / PL::kStages) & 1u) ^ 1u;
         if (!(ok = warp_wait(smem_u32(&bars->k_empty[st]), ph, abort_flag, p.status,
                              kDevTimeoutProducer)))
@@ -787,8 +820,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int ch = 0; ch < PL::kChunks; ++ch)
             tma_load_4d(kbase + st * PL::kTileBytes + ch * PL::kChunkBytes +
-                            lane * p.box_rows * PL::kRowBytes,
-                        &k_map, kf, ch * PL::kChunkDims, y, pc.kvh, page);
+                            lane * (p.box_rows << p.pair) * PL::kRowBytes,
+                        &k_map, kf, ch * PL::kChunkDims, y, pc.kvh << p.pair, page);
         }
         ++gk;
         if (!(ok = warp_wait(smem_u32(&bars->v_empty[st]), ph, abort_flag, p.status,
@@ -801,8 +834,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int ch = 0; ch < PL::kChunks; ++ch)
             tma_load_4d(vbase + st * PL::kTileBytes + ch * PL::kChunkBytes +
-                            lane * p.box_rows * PL::kRowBytes,
-                        &v_map, vf, ch * PL::kChunkDims, y, pc.kvh, page);
+                            lane * (p.box_rows << p.pair) * PL::kRowBytes,
+                        &v_map, vf, ch * PL::kChunkDims, y, pc.kvh << p.pair, page);
         }
         ++gv;
       }
@@ -961,11 +994,26 @@ int gqa_max_balanced_batch(const fa_decode_args *a) {
   return bytes / 8 - 1;
 }
 
-int gqa_tile_tokens(const fa_decode_args *a) {
-  return gqa::tile_tokens(a->d_qk, gqa::rows_of(a));
+// Two adjacent kv heads per entry?  For paged head-128 caches with pages of
+// 32 tokens or fewer, each TMA box (one page's rows of one 64-dim chunk)
+// holds only 2-4 KB and the TMA unit's box rate, not HBM, paces the decode;
+// a box over both heads' rows of a page halves the box count.  Needs an even
+// number of kv heads and at most 64 query rows per pair (two or more row
+// copies).  `a` describes the real heads.
+bool gqa_pairs_heads(const fa_decode_args *a) {
+  return a->block_table && a->d_qk == 128 && (a->page_size == 16 || a->page_size == 32) &&
+         a->num_kv_heads >= 2 &&
+         a->num_kv_heads % 2 == 0 && 2 * gqa::rows_of(a) <= 64;
 }
-int gqa_box_rows(const fa_decode_args *a) {
-  return gqa::box_rows_for(gqa_tile_tokens(a), a->page_size);
+
+// Tokens per tile and rows per TMA box for the arguments as the kernel sees
+// them (`pair`: kv heads already halved): a paired tile holds 64 tokens of
+// each of its two heads.
+int gqa_tile_tokens(const fa_decode_args *a, int pair) {
+  return pair ? 64 : gqa::tile_tokens(a->d_qk, gqa::rows_of(a));
+}
+int gqa_box_rows(const fa_decode_args *a, int pair) {
+  return gqa::box_rows_for(gqa_tile_tokens(a, pair), a->page_size);
 }
 
 // The tensor-core kernel serves bf16 / f16 with d_qk == d_v in {16, 32, 64,
@@ -990,20 +1038,20 @@ bool gqa_tc_eligible(const fa_decode_args *a) {
     const int ps = a->page_size;
     if (ps < 16 || ps % 16) return false;
     // boxes tile the tile; pages divide the box or are multiples of it
-    const int box = gqa_box_rows(a);
-    if (gqa_tile_tokens(a) % box || (ps <= box ? (box % ps) : (ps % box))) return false;
+    const int box = gqa_box_rows(a, 0);
+    if (gqa_tile_tokens(a, 0) % box || (ps <= box ? (box % ps) : (ps % box))) return false;
     if (a->num_pages <= 0) return false;
   }
   return true;
 }
 
-// Launch the decode for eligible arguments.  Balanced schedule
+// Launch the decode for eligible arguments, `a` as the kernel sees them
+// (with `pair`, half the kv heads: gqa_pairs_heads).  Balanced schedule
 // (a->num_splits == 0): one CTA per part (grid), merge records into `merge`
 // (int4 per entry); fixed partitions: num_parts = entries * num_splits.
-// Sequences the balanced schedule can scan at once (the scan lives in the
-// rings' shared memory).
 cudaError_t launch_gqa_tc(const CUtensorMap &km, const CUtensorMap &vm, const fa_decode_args *a,
-                          int4 *merge, int num_parts, int grid, bool pdl, cudaStream_t stream) {
+                          int pair, int4 *merge, int num_parts, int grid, bool pdl,
+                          cudaStream_t stream) {
   gqa::Params p;
   p.q = a->q;
   p.q_sb = a->q_stride_b;
@@ -1013,8 +1061,10 @@ cudaError_t launch_gqa_tc(const CUtensorMap &km, const CUtensorMap &vm, const fa
   p.bt_stride = a->bt_stride;
   p.page_size = a->page_size;
   p.num_pages = a->num_pages;
-  p.tile_n = gqa_tile_tokens(a);
-  p.box_rows = a->block_table ? gqa_box_rows(a) : p.tile_n;
+  p.tile_n = gqa_tile_tokens(a, pair);
+  p.box_rows = a->block_table ? gqa_box_rows(a, pair) : p.tile_n;
+  p.pair = pair;
+  p.pair_group = pair ? a->num_q_heads / a->num_kv_heads / 2 : 0;
   p.seq_lens = a->seq_lens;
   p.n_ctx = a->n_ctx;
   p.batch = a->batch;

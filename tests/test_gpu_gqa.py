@@ -88,7 +88,7 @@ def test_tensor_core_path_selection(d, group, block, dtype, want):
     assert _lib.lib().fa_decode_uses_tensor_cores(ctypes.byref(a)) == want
 
 
-@pytest.mark.parametrize("d", [32, 64, 256])
+@pytest.mark.parametrize("d", [32, 64, 128, 256])
 def test_balanced_schedule_bit_exact(d):
     """The merge records the kernel writes for every entry equal the host
     specification (oracle.gqa_schedule with the kernel's tile as the block),
@@ -109,10 +109,14 @@ def test_balanced_schedule_bit_exact(d):
         a = _args_for(q, k, lens_t, bt, out)
         a.v = v.data_ptr()
         a.num_splits = 0
+        # head 128 over 16-token pages with an even kv-head count: entries
+        # cover two kv heads (half the entries, 64 tokens of each per tile)
+        paired = d == 128 and hkv % 2 == 0
+        ents = hkv // 2 if paired else hkv
         po, pl, sc = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
         assert lib.fa_decode_workspace_size(ctypes.byref(a), ctypes.byref(po), ctypes.byref(pl),
                                             ctypes.byref(sc)) == 0
-        assert sc.value == B * hkv * 16
+        assert sc.value == B * ents * 16
         ws = torch.empty(po.value + pl.value + sc.value, dtype=torch.uint8, device="cuda")
         a.part_o, a.part_lse = ws.data_ptr(), ws.data_ptr() + po.value
         a.sched = ws.data_ptr() + po.value + pl.value
@@ -123,8 +127,8 @@ def test_balanced_schedule_bit_exact(d):
         got = ws[po.value + pl.value:].view(torch.int32).view(-1, 4)[:, :3].cpu().numpy()
         # tile tokens: 64 for head 256, 192 for heads up to 64 with at most
         # 64 query rows per kv head, else 128
-        block_n = 64 if d == 256 else (192 if d <= 64 else 128)
-        _, merge = oracle.gqa_schedule(lens, hkv, sms, block_n=block_n)
+        block_n = 64 if d == 256 or paired else (192 if d <= 64 else 128)
+        _, merge = oracle.gqa_schedule(lens, ents, sms, block_n=block_n)
         assert np.array_equal(got, np.asarray(merge, np.int32)), trial
         ref = _oracle(q, k, v, bt, lens_t, scale).to(torch.float16).float()
         assert torch.allclose(out.float().cpu(), ref, atol=2e-3, rtol=1e-5), trial
