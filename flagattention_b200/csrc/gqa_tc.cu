@@ -994,23 +994,25 @@ int gqa_max_balanced_batch(const fa_decode_args *a) {
   return bytes / 8 - 1;
 }
 
-// Two adjacent kv heads per entry?  For paged head-128 caches with pages of
-// 32 tokens or fewer, each TMA box (one page's rows of one 64-dim chunk)
-// holds only 2-4 KB and the TMA unit's box rate, not HBM, paces the decode;
-// a box over both heads' rows of a page halves the box count.  Needs an even
-// number of kv heads and at most 64 query rows per pair (two or more row
-// copies).  `a` describes the real heads.
+// Two adjacent kv heads per entry?  For paged head-128 / 256 caches with
+// pages of 32 tokens or fewer, each TMA box (one page's rows of one 64-dim
+// chunk) holds only 2-4 KB and the TMA unit's box rate, not HBM, paces the
+// decode; a box over both heads' rows of a page halves the box count.  The
+// tile keeps its rows (and so its bytes and MMA work): half of them per head.
+// Needs an even number of kv heads and at most 64 query rows per pair (two
+// or more row copies).  `a` describes the real heads.
 bool gqa_pairs_heads(const fa_decode_args *a) {
-  return a->block_table && a->d_qk == 128 && (a->page_size == 16 || a->page_size == 32) &&
+  return a->block_table && (a->d_qk == 128 || a->d_qk == 256) &&
+         (a->page_size == 16 || a->page_size == 32) &&
          a->num_kv_heads >= 2 &&
          a->num_kv_heads % 2 == 0 && 2 * gqa::rows_of(a) <= 64;
 }
 
 // Tokens per tile and rows per TMA box for the arguments as the kernel sees
-// them (`pair`: kv heads already halved): a paired tile holds 64 tokens of
-// each of its two heads.
+// them (`pair`: kv heads already halved): a paired tile holds half its rows'
+// worth of tokens of each of its two heads (64 at head 128, 32 at head 256).
 int gqa_tile_tokens(const fa_decode_args *a, int pair) {
-  return pair ? 64 : gqa::tile_tokens(a->d_qk, gqa::rows_of(a));
+  return pair ? gqa::tile_tokens(a->d_qk, 128) / 2 : gqa::tile_tokens(a->d_qk, gqa::rows_of(a));
 }
 int gqa_box_rows(const fa_decode_args *a, int pair) {
   return gqa::box_rows_for(gqa_tile_tokens(a, pair), a->page_size);

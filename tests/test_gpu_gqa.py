@@ -109,9 +109,10 @@ def test_balanced_schedule_bit_exact(d):
         a = _args_for(q, k, lens_t, bt, out)
         a.v = v.data_ptr()
         a.num_splits = 0
-        # head 128 over 16-token pages with an even kv-head count: entries
-        # cover two kv heads (half the entries, 64 tokens of each per tile)
-        paired = d == 128 and hkv % 2 == 0
+        # heads 128 / 256 over 16-token pages with an even kv-head count:
+        # entries cover two kv heads (half the entries; 64 / 32 tokens of each
+        # per tile)
+        paired = d in (128, 256) and hkv % 2 == 0
         ents = hkv // 2 if paired else hkv
         po, pl, sc = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
         assert lib.fa_decode_workspace_size(ctypes.byref(a), ctypes.byref(po), ctypes.byref(pl),
@@ -127,7 +128,8 @@ def test_balanced_schedule_bit_exact(d):
         got = ws[po.value + pl.value:].view(torch.int32).view(-1, 4)[:, :3].cpu().numpy()
         # tile tokens: 64 for head 256, 192 for heads up to 64 with at most
         # 64 query rows per kv head, else 128
-        block_n = 64 if d == 256 or paired else (192 if d <= 64 else 128)
+        block_n = ({128: 64, 256: 32}[d] if paired else
+                   64 if d == 256 else (192 if d <= 64 else 128))
         _, merge = oracle.gqa_schedule(lens, ents, sms, block_n=block_n)
         assert np.array_equal(got, np.asarray(merge, np.int32)), trial
         ref = _oracle(q, k, v, bt, lens_t, scale).to(torch.float16).float()
