@@ -150,8 +150,8 @@ def test_rows_per_kv_head(hq, group, d):
     assert read_status(q.device) == 0
 
 
-@pytest.mark.parametrize("d, block", [(128, 16), (128, 128), (128, 256), (256, 16),
-                                      (256, 128), (32, 16), (16, 128)])
+@pytest.mark.parametrize("d, block", [(128, 16), (128, 32), (128, 128), (128, 256), (256, 16),
+                                      (256, 32), (256, 128), (32, 16), (16, 128)])
 @pytest.mark.parametrize("num_splits", [0, 1, 3, 8])
 def test_nan_past_sequence_end_and_splits(d, block, num_splits):
     """Value / key slots past each sequence's end in its last page hold NaN;
