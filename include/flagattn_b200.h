@@ -112,7 +112,10 @@ int fa_split_kv_num_splits(int batch, int heads, int m, int n, int block_m,
  *    head size 256) or is a multiple of it.  num_splits == 0 selects its
  *    balanced schedule (pieces cut by the device scheduler so that every SM
  *    gets the same work; needs `sched`); num_splits >= 1 keeps the
- *    reference's fixed partitions of partition_size tokens.
+ *    reference's fixed partitions of partition_size tokens.  Paged head-128
+ *    / 256 caches with 16- or 32-token pages, an even kv-head count and at
+ *    most 32 query rows per kv head are served two adjacent kv heads per
+ *    work entry (one TMA box over both heads' rows of a page).
  *  - the CUDA-core kernel for every other shape (num_splits >= 1).
  * With splits, partials go to part_o / part_lse and are merged in place
  * (part_lse f32; part_o f32 for the CUDA-core kernel, rows in the input type
