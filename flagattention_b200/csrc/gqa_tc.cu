@@ -482,7 +482,22 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
   const bool live = r < p.rows;
   const int g_idx = live ? r / p.m_q : 0;
   const int m_idx = live ? r % p.m_q : 0;
-  const int hh_r = p.pair && live ? g_idx / p.pair_group : 0;  // head of the row within its pair
+  // paired kv heads reach only heads 128 / 256 with two or more copies
+  // (gqa_pairs_heads); other instances compile without that code
+  constexpr bool kPairable = kC >= 2 && (kD == 128 || kD == 256);
+  const int pair = kPairable ? p.pair : 0;
+  const int hh_r = pair && live ? g_idx / p.pair_group : 0;  // head of the row within its pair
+  // paired: bit j set where this copy's column j holds the row's own head
+  // (column cj: box cj >> (lgR + 1), head (cj >> lgR) & 1, paired pages
+  // hold 16 or 32 tokens); every bit for rows past the group
+  const int lgR = pair ? __ffs(p.box_rows) - 1 : 0;
+  uint64_t own = ~0ull;
+  if (pair && live) {
+    own = 0;
+#pragma unroll
+    for (int j = 0; j < (kCols < 64 ? kCols : 64); ++j)
+      own |= static_cast<uint64_t>((((copy * kCols + j) >> lgR) & 1) == hh_r) << j;
+  }
   const int tt = p.tile_n;                                    // tokens per tile
   const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
   const uint32_t t_o = tmem + lane_off + PL::kColO;
@@ -541,23 +556,21 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
       const int lo = live ? pc.tok0 - c0 : 0;
       const int hi = live ? row_end - c0 : kCols;
       float mx = -INFINITY;
-      if (p.pair) {
-        // column cj: box cj >> (lgR + 1), head (cj >> lgR) & 1, token
-        // n0 + box * R + (cj & (R - 1))  (paired pages hold 16 or 32 tokens)
-        const int lgR = __ffs(p.box_rows) - 1;
+      if (pair) {
         if (__all_sync(0xffffffffu, !live || (n0 >= pc.tok0 && n0 + tt <= row_end))) {
 #pragma unroll
           for (int j = 0; j < kCols; ++j) {
-            const int cj = copy * kCols + j;
-            s[j] = (!live || ((cj >> lgR) & 1) == hh_r) ? s[j] : -INFINITY;
+            s[j] = (j < 64 && ((own >> j) & 1)) ? s[j] : -INFINITY;  // select: NaN-safe
             mx = fmaxf(mx, s[j]);
           }
         } else {
+          // token of column cj: n0 + box * R + (cj & (R - 1))
 #pragma unroll
           for (int j = 0; j < kCols; ++j) {
             const int cj = copy * kCols + j;
             const int tok = n0 + ((cj >> (lgR + 1)) << lgR) + (cj & (p.box_rows - 1));
-            const bool ok_j = !live || (((cj >> lgR) & 1) == hh_r && tok >= pc.tok0 && tok < row_end);
+            const bool ok_j =
+                !live || (j < 64 && ((own >> j) & 1) && tok >= pc.tok0 && tok < row_end);
             s[j] = ok_j ? s[j] : -INFINITY;  // select: NaN-safe
             mx = fmaxf(mx, s[j]);
           }
@@ -659,8 +672,8 @@ __device__ __forceinline__ void row_role(const Params &p, Bars *bars, uint8_t *s
           constexpr int kUnits = PL::kRowBytes / 16;  // 16-byte units per chunk row
           const int units = (r1 - r0) * kUnits;
           // paired heads: the box's rows are [head][row], cleared for both
-          const int row0 = p.pair ? 2 * jb * p.box_rows + (r0 - jb * p.box_rows) : r0;
-          for (int u = lane; u < units * PL::kChunks << p.pair; u += 32) {
+          const int row0 = pair ? 2 * jb * p.box_rows + (r0 - jb * p.box_rows) : r0;
+          for (int u = lane; u < units * PL::kChunks << pair; u += 32) {
             const int hh = u / (units * PL::kChunks), uu = u % (units * PL::kChunks);
             const int ch = uu / units, rem = uu % units;
             const uint32_t addr = tile + ch * PL::kChunkBytes +
@@ -960,6 +973,7 @@ cudaError_t launch_d(const CUtensorMap &km, const CUtensorMap &vm, const Params 
                      bool pdl, cudaStream_t stream) {
   if (p.rows <= 32) return launch_t<T, kD, 4>(km, vm, p, grid, pdl, stream);
   if (p.rows <= 64) return launch_t<T, kD, 2>(km, vm, p, grid, pdl, stream);
+  if (p.pair) return cudaErrorInvalidValue;  // one-copy instances hold no paired code
   return launch_t<T, kD, 1>(km, vm, p, grid, pdl, stream);
 }
 
