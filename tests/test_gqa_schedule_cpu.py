@@ -37,7 +37,7 @@ def _check(lens, hkv, parts, block_n=128):
     return pieces
 
 
-@pytest.mark.parametrize("block_n", [128, 64, 192])  # head 256 / small-head tiles
+@pytest.mark.parametrize("block_n", [128, 64, 192, 32])  # head 256 / small-head / paired head-256 tiles
 def test_schedule_covers_every_block_once(block_n):
     rs = np.random.RandomState(3)
     for trial in range(60):
